@@ -1,0 +1,116 @@
+"""ctypes binding of the C ABI in ``include/beam_b200.h``.
+
+The library is built in-tree (``beam_engine_b200/lib/libbeam_b200.so``).  There
+is no fallback: if the library is missing every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libbeam_b200.so")
+_lib = None
+
+i32, i64, f32, f64 = C.c_int32, C.c_int64, C.c_float, C.c_double
+vp = C.c_void_p
+P32 = C.POINTER(C.c_int32)
+PP32 = C.POINTER(P32)
+
+BE_OK, BE_EINVAL, BE_ENOMEM, BE_ECUDA, BE_ENOT_ALLOCATED, BE_ECAPACITY, BE_EDEVICE_RANGE = range(7)
+BE_F32, BE_F16, BE_BF16 = 0, 1, 2
+
+
+class AttnPlanInfo(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in (
+        "n_work", "n_work_wide", "n_queries", "n_parts", "n_merge", "off_work", "off_qlist",
+        "off_kvlist", "off_merge_q", "off_merge_ptr", "off_merge_parts", "total_ints",
+        "page_size", "group_size")]
+
+
+_SIGS = {
+    "be_last_error": (C.c_char_p, []),
+    "be_version": (C.c_int, []),
+    "be_device_status": (C.c_int, [P32, vp]),
+    "be_device_status_clear": (C.c_int, [vp]),
+    "be_append_paged_kv": (C.c_int, [vp, vp, i64, i64, vp, vp, vp, vp, C.c_int, vp, i64, C.c_int,
+                                     C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp]),
+    "be_fork_tail_copy": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                    vp, vp, vp, C.c_int, vp]),
+    "be_cascade_plan": (C.c_int, [C.c_int, PP32, PP32, PP32, PP32, P32, C.c_int, C.c_int, C.c_int,
+                                  C.c_int, C.c_int, C.c_int, C.c_int, P32, i64,
+                                  C.POINTER(AttnPlanInfo)]),
+    "be_tree_plan": (C.c_int, [C.c_int, P32, C.c_int, P32, P32, P32, P32, P32, P32, P32, C.c_int,
+                               C.c_int, C.c_int, C.c_int, P32, i64, C.POINTER(AttnPlanInfo)]),
+    "be_attn_run": (C.c_int, [vp, C.POINTER(AttnPlanInfo), vp, i64, vp, C.c_int, C.c_int, C.c_int,
+                              C.c_int, C.c_int, f32, vp, i64, vp, vp, vp, vp, vp]),
+    # host page manager
+    "be_trie_create": (vp, [C.c_int, C.c_int]),
+    "be_trie_destroy": (None, [vp]),
+    "be_alloc_page": (C.c_int, [vp, P32]),
+    "be_free_page": (C.c_int, [vp, i32]),
+    "be_num_free_pages": (C.c_int, [vp]),
+    "be_is_allocated": (C.c_int, [vp, i32]),
+    "be_free_list": (C.c_int, [vp, P32, C.c_int]),
+    "be_trie_warnings": (i64, [vp]),
+    "be_trie_num_nodes": (C.c_int, [vp]),
+    "be_node_new": (C.c_int, [vp, i32, i32, P32, C.c_int, P32]),
+    "be_node_info": (C.c_int, [vp, i32, P32, P32, P32, P32]),
+    "be_node_tokens": (C.c_int, [vp, i32, P32, C.c_int]),
+    "be_node_children": (C.c_int, [vp, i32, P32, C.c_int]),
+    "be_node_append_token": (C.c_int, [vp, i32, i32]),
+    "be_node_sequence": (i64, [vp, i32, P32, i64]),
+    "be_beam_add_root": (C.c_int, [vp, P32, C.c_int, P32, P32]),
+    "be_beam_update": (C.c_int, [vp, C.c_int, P32, P32, P32, P32, P32, P32, P32, P32, P32, P32]),
+    "be_beam_step_inputs": (C.c_int, [vp, C.c_int, P32, P32, P32, P32, P32]),
+    "be_cascade_build": (C.c_int, [vp, C.c_int, P32, C.c_int, C.c_int, C.c_int, P32, P32, P32, P32,
+                                   P32, P32]),
+    "be_tree_build": (C.c_int, [vp, C.c_int, P32, C.c_int, C.c_int, C.c_int, P32, P32, P32, P32, P32, P32,
+                                i64, P32, P32, i64]),
+    "be_fasttree_prepare": (C.c_int, [C.c_int, P32, P32, P32, P32, P32, i64, C.c_int, C.c_int,
+                                      C.c_int, C.c_int, C.c_int, P32, P32, P32, P32, P32, P32, P32,
+                                      P32, P32]),
+    "be_vanilla_select": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_double), P32,
+                                    C.POINTER(C.c_double), C.c_int, P32, P32,
+                                    C.POINTER(C.c_double)]),
+}
+
+
+def exported_symbols():
+    return list(_SIGS)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            raise RuntimeError(
+                f"beam_engine_b200 native library not found at {_LIB_PATH}; build it with "
+                "`python -m beam_engine_b200.build_lib` (there is no CPU fallback)")
+        L = C.CDLL(_LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+class BeamEngineError(RuntimeError):
+    pass
+
+
+def check(rc, what=""):
+    if rc == BE_OK:
+        return
+    msg = lib().be_last_error().decode(errors="replace")
+    text = f"{what}: {msg}" if what else msg
+    if rc == BE_EINVAL:
+        raise ValueError(text)
+    if rc == BE_ENOMEM:
+        raise MemoryError(text)
+    raise BeamEngineError(f"[status {rc}] {text}")
+
+
+def ptr32(arr):
+    """ctypes int32* of a contiguous numpy int32 array."""
+    return arr.ctypes.data_as(P32)

@@ -1,0 +1,360 @@
+"""BeamState: the beam trie over KV pages, same interface as the reference's
+``src/beam_engine/beam_state.py`` (``TrieNode`` :12-30, dataclasses :33-60,
+``BeamState`` :62-682), backed by the native host page manager.
+
+The trie (nodes, tokens, children) and the FIFO page allocator live in C++
+(``be_trie``, shared with the :class:`PageTable`); a :class:`TrieNode` is a
+handle ``(trie, node id)``.  Fork/free (``add_filtered_results``), cascade
+levels (``get_cascade_input``) and FastTree inputs (``get_fasttree_input``)
+run natively with the reference's semantics, including its quirks (the
+query's own K/V is excluded from the cascade; shallow candidates repeat their
+deepest pages at later levels).  Copy-on-write tail copies are collected and
+issued as ONE batched kernel (all copies, all layers) per update.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+from .fasttree import KVTreeNode
+
+
+class TrieNode:
+    """Handle to a trie node.  ``TrieNode(tokens, page_id, parent)`` creates a node
+    like the reference's constructor (a root without ``trie=`` gets its own trie)."""
+
+    __slots__ = ("_t", "_id", "_owner")
+
+    def __init__(self, tokens: List[int] = None, page_id: int = -1,
+                 parent: Optional["TrieNode"] = None, *, trie=None, node_id: int = None,
+                 _owner=None):
+        if node_id is not None:
+            self._t, self._id, self._owner = trie, node_id, _owner
+            return
+        if parent is not None:
+            self._t, self._owner = parent._t, parent._owner
+        elif trie is not None:
+            self._t, self._owner = trie, _owner
+        else:
+            self._owner = _StandaloneTrie()
+            self._t = self._owner.ptr
+        toks = np.asarray(list(tokens or []), np.int32)
+        out = C.c_int32()
+        check(lib().be_node_new(self._t, parent._id if parent is not None else -1, int(page_id),
+                                _lib.ptr32(toks), len(toks), C.byref(out)), "TrieNode")
+        self._id = out.value
+
+    def _info(self):
+        par, page, nt, nc = C.c_int32(), C.c_int32(), C.c_int32(), C.c_int32()
+        check(lib().be_node_info(self._t, self._id, C.byref(par), C.byref(page), C.byref(nt),
+                                 C.byref(nc)), "node info")
+        return par.value, page.value, nt.value, nc.value
+
+    @property
+    def tokens(self) -> List[int]:
+        n = self._info()[2]
+        buf = np.zeros(max(n, 1), np.int32)
+        lib().be_node_tokens(self._t, self._id, _lib.ptr32(buf), n)
+        return buf[:n].tolist()
+
+    @property
+    def page_id(self) -> int:
+        return self._info()[1]
+
+    @property
+    def parent(self) -> Optional["TrieNode"]:
+        p = self._info()[0]
+        return None if p < 0 else TrieNode(trie=self._t, node_id=p, _owner=self._owner)
+
+    @property
+    def children(self) -> List["TrieNode"]:
+        n = self._info()[3]
+        buf = np.zeros(max(n, 1), np.int32)
+        lib().be_node_children(self._t, self._id, _lib.ptr32(buf), n)
+        return [TrieNode(trie=self._t, node_id=int(c), _owner=self._owner) for c in buf[:n]]
+
+    def append_token(self, token: int):
+        check(lib().be_node_append_token(self._t, self._id, int(token)), "append_token")
+
+    def __eq__(self, other):
+        return isinstance(other, TrieNode) and other._t == self._t and other._id == self._id
+
+    def __hash__(self):
+        return hash((self._t, self._id))
+
+    def __repr__(self):
+        par, page, nt, nc = self._info()
+        return f"TrieNode(tokens={self.tokens}, page_id={page}, children={nc})"
+
+
+class _StandaloneTrie:
+    """Trie for hand-built nodes that belong to no PageTable (as in test trees)."""
+
+    def __init__(self, page_size=1):
+        self.ptr = lib().be_trie_create(page_size, 0)
+
+    def __del__(self):
+        if getattr(self, "ptr", None):
+            lib().be_trie_destroy(self.ptr)
+            self.ptr = None
+
+
+@dataclass
+class BeamCandidate:
+    trie_node: TrieNode
+    score: float
+    finished: bool = False
+
+
+@dataclass
+class BeamTokenCandidate:
+    token_id: int
+    log_prob: float
+
+
+@dataclass
+class BeamToken:
+    token_id: int
+    accumulated_score: float
+
+
+@dataclass
+class BeamGenerateInput:
+    candidate: BeamCandidate
+    children: List[BeamTokenCandidate]
+
+
+@dataclass
+class BeamGenerateResult:
+    candidate: BeamCandidate
+    children: List[BeamToken]
+
+
+class BeamState:
+    """Current beam candidates over the page trie (beam_state.py:62-682)."""
+
+    def __init__(self, beam_size: int, page_table):
+        self.beam_size = beam_size
+        self.page_table = page_table
+        self._t = page_table._trie
+        self._owner = page_table
+        self.root = None
+        self._leaves = np.zeros(0, np.int32)
+        self._scores = np.zeros(0, np.float64)
+        self._cand_objs = None
+        self.finished_candidates: List[BeamCandidate] = []
+        self._cached_write_batch_indices = None
+        self._cached_write_kv_indptr = None
+        self.last_copies = (np.zeros(0, np.int32),) * 3
+        self.defer_copies = False   # engine mode: caller issues the batched copy itself
+
+    # -- candidates view ----------------------------------------------------
+    @property
+    def candidates(self) -> List[BeamCandidate]:
+        if self._cand_objs is None:
+            self._cand_objs = [BeamCandidate(TrieNode(trie=self._t, node_id=int(n), _owner=self._owner),
+                                             float(s)) for n, s in zip(self._leaves, self._scores)]
+        return self._cand_objs
+
+    @candidates.setter
+    def candidates(self, cands: List[BeamCandidate]):
+        if cands:
+            self._t = cands[0].trie_node._t
+            self._owner = cands[0].trie_node._owner
+        self._leaves = np.asarray([c.trie_node._id for c in cands], np.int32)
+        self._scores = np.asarray([c.score for c in cands], np.float64)
+        self._cand_objs = None
+
+    def set_state(self, leaves, scores):
+        self._leaves = np.ascontiguousarray(leaves, np.int32)
+        self._scores = np.ascontiguousarray(scores, np.float64)
+        self._cand_objs = None
+
+    @property
+    def leaves(self) -> np.ndarray:
+        return self._leaves
+
+    @property
+    def scores(self) -> np.ndarray:
+        return self._scores
+
+    # -- beam_state.py:76-98 ------------------------------------------------
+    def add_root_sequence(self, sequence: List[int]) -> List[TrieNode]:
+        toks = np.asarray(sequence, np.int32)
+        leaf = C.c_int32()
+        pages = np.zeros(max(1, -(-len(toks) // self.page_table.page_size)), np.int32)
+        check(lib().be_beam_add_root(self._t, _lib.ptr32(toks), len(toks), C.byref(leaf),
+                                     _lib.ptr32(pages)), "add_root_sequence")
+        chain = []
+        n = TrieNode(trie=self._t, node_id=leaf.value, _owner=self._owner)
+        while n is not None:
+            chain.append(n)
+            n = n.parent
+        chain.reverse()
+        if self.root is None and chain:
+            self.root = chain[0]
+        self._leaves = np.append(self._leaves, np.int32(leaf.value))
+        self._scores = np.append(self._scores, 0.0)
+        self._cand_objs = None
+        return chain
+
+    # -- beam_state.py:101-209 ----------------------------------------------
+    def add_filtered_results(self, results: List[BeamGenerateResult]):
+        if len(results) != len(self._leaves):
+            self.candidates = [r.candidate for r in results]
+        ptr = np.zeros(len(results) + 1, np.int32)
+        toks, scores = [], []
+        for i, r in enumerate(results):
+            ptr[i + 1] = ptr[i] + len(r.children)
+            toks.extend(c.token_id for c in r.children)
+            scores.extend(c.accumulated_score for c in r.children)
+        leaves = np.asarray([r.candidate.trie_node._id for r in results], np.int32)
+        self.update_native(leaves, ptr, np.asarray(toks, np.int32), np.asarray(scores, np.float64))
+
+    def update_native(self, leaves, child_ptr, child_tokens, child_scores):
+        """Array form of add_filtered_results: candidate i's children are
+        child_tokens[child_ptr[i]:child_ptr[i+1]] with their accumulated scores."""
+        nc = max(int(child_ptr[-1]), 1)
+        new_leaf = np.zeros(nc, np.int32)
+        new_child = np.zeros(nc, np.int32)
+        cs, cd, cl = (np.zeros(nc, np.int32) for _ in range(3))
+        n_new, n_cp = C.c_int32(), C.c_int32()
+        leaves = np.ascontiguousarray(leaves, np.int32)
+        child_ptr = np.ascontiguousarray(child_ptr, np.int32)
+        child_tokens = np.ascontiguousarray(child_tokens, np.int32)
+        rc = lib().be_beam_update(self._t, len(leaves), _lib.ptr32(leaves), _lib.ptr32(child_ptr),
+                                  _lib.ptr32(child_tokens), _lib.ptr32(new_leaf),
+                                  _lib.ptr32(new_child), C.byref(n_new), _lib.ptr32(cs),
+                                  _lib.ptr32(cd), _lib.ptr32(cl), C.byref(n_cp))
+        if rc == _lib.BE_ENOMEM:
+            raise MemoryError("No free pages available")
+        check(rc, "add_filtered_results")
+        k, c = n_new.value, n_cp.value
+        self._leaves = new_leaf[:k].copy()
+        self._scores = np.asarray(child_scores, np.float64)[new_child[:k]]
+        self._cand_objs = None
+        self.last_copies = (cs[:c].copy(), cd[:c].copy(), cl[:c].copy())
+        if c and not self.defer_copies and self.page_table.kv_cache.is_cuda:
+            self.page_table.copy_blocks(*self.last_copies)
+
+    # -- decode inputs -------------------------------------------------------
+    def step_inputs(self):
+        """(query tokens, write pages, write positions, RoPE positions), int32 arrays."""
+        n = len(self._leaves)
+        out = [np.zeros(max(n, 1), np.int32) for _ in range(4)]
+        check(lib().be_beam_step_inputs(self._t, n, _lib.ptr32(self._leaves),
+                                        *[_lib.ptr32(o) for o in out]), "step inputs")
+        return [o[:n] for o in out]
+
+    def cascade_levels(self):
+        """Native get_cascade_input: list of per-level dicts of int32 numpy arrays."""
+        n = len(self._leaves)
+        if n == 0:
+            return []
+        cap_l, cap_g, cap_p = 64, 64 * (n + 1), 4096
+        while True:
+            lg = np.zeros(cap_l + 1, np.int32)
+            lp = np.zeros(cap_l + 1, np.int32)
+            qo = np.zeros(cap_g + cap_l, np.int32)
+            kvp = np.zeros(cap_g + cap_l, np.int32)
+            kvi = np.zeros(cap_p, np.int32)
+            last = np.zeros(cap_g, np.int32)
+            r = lib().be_cascade_build(self._t, n, _lib.ptr32(self._leaves), cap_l, cap_g, cap_p,
+                                       _lib.ptr32(lg), _lib.ptr32(lp), _lib.ptr32(qo),
+                                       _lib.ptr32(kvp), _lib.ptr32(kvi), _lib.ptr32(last))
+            if r == -_lib.BE_ECAPACITY:
+                cap_l, cap_g, cap_p = cap_l * 2, cap_g * 2, cap_p * 4
+                continue
+            if r < 0:
+                check(-r, "get_cascade_input")
+            break
+        levels = []
+        for lv in range(r):
+            g0, g1 = lg[lv], lg[lv + 1]
+            p0, p1 = lp[lv], lp[lv + 1]
+            levels.append(dict(qo_indptr=qo[g0 + lv:g1 + lv + 1], kv_indptr=kvp[g0 + lv:g1 + lv + 1],
+                               kv_indices=kvi[p0:p1], kv_last_page_len=last[g0:g1]))
+        return levels
+
+    def get_cascade_input(self):
+        """beam_state.py:211-412 -- same 7-tuple as the reference."""
+        if len(self._leaves) == 0:
+            return ([], [], [], [], torch.empty(0, 0, 0))
+        levels = self.cascade_levels()
+        qtok = self.step_inputs()[0]
+        dev = self.page_table.device
+        n = len(self._leaves)
+        if (self._cached_write_batch_indices is None
+                or self._cached_write_batch_indices.shape[0] != n):
+            self._cached_write_batch_indices = torch.arange(n, dtype=torch.int32, device=dev)
+            self._cached_write_kv_indptr = torch.arange(n + 1, dtype=torch.int32, device=dev)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32))  # noqa: E731
+        return ([t(lv["qo_indptr"]) for lv in levels], [t(lv["kv_indptr"]) for lv in levels],
+                [t(lv["kv_indices"]) for lv in levels], [t(lv["kv_last_page_len"]) for lv in levels],
+                torch.tensor(qtok.astype(np.int64), device=dev), self._cached_write_batch_indices,
+                self._cached_write_kv_indptr)
+
+    # -- beam_state.py:414-633 ----------------------------------------------
+    def tree_arrays(self, per_node: bool = False):
+        n = len(self._leaves)
+        nn, ml = C.c_int32(), C.c_int32()
+        z = np.zeros(1, np.int32)
+        args = [self._t, n, _lib.ptr32(self._leaves), 1 if per_node else 0,
+                self.page_table.page_size]
+        check(lib().be_tree_build(*args, 0, C.byref(nn), *[_lib.ptr32(z)] * 5, 0, C.byref(ml),
+                                  None, 0), "tree build")
+        N, M = nn.value, ml.value
+        par, seql, kids = (np.zeros(max(N, 1), np.int32) for _ in range(3))
+        rptr = np.zeros(N + 1, np.int32)
+        cap_r = max(1, N * n)
+        rl = np.zeros(cap_r, np.int32)
+        r2t = np.zeros((max(n, 1), max(M, 1)), np.int32)
+        check(lib().be_tree_build(*args, N, C.byref(nn), _lib.ptr32(par), _lib.ptr32(seql),
+                                  _lib.ptr32(kids), _lib.ptr32(rptr), _lib.ptr32(rl), cap_r,
+                                  C.byref(ml), _lib.ptr32(r2t), r2t.size), "tree build")
+        return par[:N], seql[:N], kids[:N], rptr, rl[:rptr[-1]], r2t[:n, :M]
+
+    def get_fasttree_input(self, per_node: bool = True):
+        """beam_state.py:566-633.  ``seqlen`` is per node by default -- the length
+        the FastTree planner assumes; ``per_node=False`` gives the reference's
+        cumulative value (which makes the reference's tree path attend the wrong
+        tokens)."""
+        par, seql, kids, rptr, rl, r2t = self.tree_arrays(per_node)
+        nodes = []
+        for i in range(len(par)):
+            k = KVTreeNode()
+            k.id, k.parent, k.seqlen, k.num_children = i, int(par[i]), int(seql[i]), int(kids[i])
+            k.requests = rl[rptr[i]:rptr[i + 1]].tolist()
+            nodes.append(k)
+        q, wp, wpos, _ = self.step_inputs()
+        dev = self.page_table.device
+        return (nodes, torch.from_numpy(r2t.copy()).to(dev), torch.tensor(q.astype(np.int64), device=dev),
+                torch.tensor(wp, device=dev), torch.tensor(wpos, device=dev))
+
+    # -- beam_state.py:646-682 ----------------------------------------------
+    def sequence(self, leaf: int) -> List[int]:
+        n = lib().be_node_sequence(self._t, int(leaf), None, 0)
+        buf = np.zeros(max(n, 1), np.int32)
+        lib().be_node_sequence(self._t, int(leaf), _lib.ptr32(buf), n)
+        return buf[:n].tolist()
+
+    def get_final_sequences(self, num_return: int, length_penalty: float = 1.0
+                            ) -> List[Tuple[List[int], float]]:
+        res = []
+        for c in self.finished_candidates:
+            res.append((self.sequence(c.trie_node._id), c.score))
+        for leaf, sc in zip(self._leaves, self._scores):
+            res.append((self.sequence(int(leaf)), float(sc)))
+        out = []
+        for seq, sc in res:
+            if length_penalty != 0 and len(seq) > 1:
+                sc = sc / (len(seq) ** length_penalty)
+            out.append((seq, sc))
+        out.sort(key=lambda x: x[1], reverse=True)
+        return out[:num_return]

@@ -1,0 +1,325 @@
+// Host-side attention planners: cascade levels / FastTree vnodes -> work items.
+//
+// The planner turns the reference's per-level cascade indices (or FastTree's
+// vnode metadata) into one flat int32 buffer that a single kernel launch
+// consumes: work items ordered heaviest-first (wide tiles, then narrow), the
+// query list, the KV list and the per-query merge lists.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <numeric>
+#include <vector>
+
+#include "beam_b200.h"
+
+namespace be {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+namespace {
+
+struct W {
+  be_attn_work w;
+  int64_t cost;
+  bool wide;
+};
+
+// Wide tiles hold up to 64 rows, narrow tiles 16 (rows = queries x group size).
+inline int tile_queries(int qlen, int g) {
+  if (qlen * g <= 16) return qlen;
+  return std::max(1, 64 / g);
+}
+
+int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
+              const std::vector<int32_t>& kvlist, int num_queries, bool allow_direct,
+              int page_size, int g, int32_t* plan, int64_t cap, be_attn_plan_info* info) {
+  // Which queries are covered exactly once (direct write) and which need merging.
+  std::vector<int> cover(num_queries, 0);
+  for (auto& it : items)
+    for (int i = 0; i < it.w.q_len; ++i) cover[qlist[it.w.q_off + i]]++;
+  int n_parts = 0;
+  for (auto& it : items) {
+    bool direct = allow_direct;
+    for (int i = 0; i < it.w.q_len && direct; ++i) direct = cover[qlist[it.w.q_off + i]] == 1;
+    if (direct) {
+      it.w.part_base = -1;
+    } else {
+      it.w.part_base = n_parts;
+      n_parts += it.w.q_len;
+    }
+  }
+  std::vector<std::vector<int32_t>> parts(num_queries);
+  std::vector<char> direct_q(num_queries, 0);
+  for (auto& it : items)
+    for (int i = 0; i < it.w.q_len; ++i) {
+      const int q = qlist[it.w.q_off + i];
+      if (it.w.part_base < 0) direct_q[q] = 1;
+      else parts[q].push_back(it.w.part_base + i);
+    }
+  std::stable_sort(items.begin(), items.end(), [](const W& a, const W& b) {
+    if (a.wide != b.wide) return a.wide;
+    return a.cost > b.cost;
+  });
+  std::vector<int32_t> mq, mptr{0}, mparts;
+  for (int q = 0; q < num_queries; ++q) {
+    if (direct_q[q]) continue;
+    mq.push_back(q);
+    mparts.insert(mparts.end(), parts[q].begin(), parts[q].end());
+    mptr.push_back((int32_t)mparts.size());
+  }
+  be_attn_plan_info in{};
+  in.n_work = (int32_t)items.size();
+  in.n_work_wide = (int32_t)std::count_if(items.begin(), items.end(), [](const W& x) { return x.wide; });
+  in.n_queries = num_queries;
+  in.n_parts = n_parts;
+  in.n_merge = (int32_t)mq.size();
+  int64_t off = 0;
+  in.off_work = 0;
+  off += (int64_t)items.size() * 8;
+  in.off_qlist = (int32_t)off;
+  off += qlist.size();
+  in.off_kvlist = (int32_t)off;
+  off += kvlist.size();
+  in.off_merge_q = (int32_t)off;
+  off += mq.size();
+  in.off_merge_ptr = (int32_t)off;
+  off += mptr.size();
+  in.off_merge_parts = (int32_t)off;
+  off += mparts.size();
+  if (off > INT32_MAX) {
+    set_error("plan too large (%lld ints)", (long long)off);
+    return BE_EINVAL;
+  }
+  in.total_ints = (int32_t)off;
+  in.page_size = page_size;
+  in.group_size = g;
+  *info = in;
+  if (off > cap || !plan) {
+    set_error("plan buffer too small: need %lld ints, have %lld", (long long)off, (long long)cap);
+    return BE_ECAPACITY;
+  }
+  int32_t* p = plan;
+  for (auto& it : items) {
+    std::memcpy(p, &it.w, sizeof(be_attn_work));
+    p += 8;
+  }
+  auto put = [&](const std::vector<int32_t>& v) {
+    if (!v.empty()) std::memcpy(p, v.data(), v.size() * sizeof(int32_t));
+    p += v.size();
+  };
+  put(qlist);
+  put(kvlist);
+  put(mq);
+  put(mptr);
+  put(mparts);
+  return BE_OK;
+}
+
+}  // namespace
+}  // namespace be
+
+using namespace be;
+
+extern "C" const char* be_last_error(void) { return g_err; }
+extern "C" int be_version(void) { return 1; }
+
+extern "C" int be_cascade_plan(int num_levels, const int32_t* const* qo_indptr,
+                               const int32_t* const* kv_indptr, const int32_t* const* kv_indices,
+                               const int32_t* const* last_page_len, const int32_t* num_groups,
+                               int num_queries, int page_size, int num_qo_heads, int num_kv_heads,
+                               int causal_last, int split_tokens, int num_sms, int32_t* plan,
+                               int64_t plan_capacity, be_attn_plan_info* info) {
+  if (num_levels < 0 || num_queries < 0 || page_size < 1 || num_kv_heads < 1 ||
+      num_qo_heads % num_kv_heads || !info) {
+    set_error("be_cascade_plan: invalid arguments");
+    return BE_EINVAL;
+  }
+  const int g = num_qo_heads / num_kv_heads;
+  if (g > 64) {
+    set_error("be_cascade_plan: group size %d > 64 unsupported", g);
+    return BE_EINVAL;
+  }
+  struct Grp {
+    int level, q0, qlen, kv_off, kv_len;
+  };
+  std::vector<Grp> groups;
+  std::vector<int32_t> kvlist;
+  int64_t total_cost = 0;
+  for (int l = 0; l < num_levels; ++l) {
+    const int G = num_groups[l];
+    const int base = (int)kvlist.size();
+    const int npages_total = G > 0 ? kv_indptr[l][G] : 0;
+    if (G > 0 && (qo_indptr[l][0] != 0 || kv_indptr[l][0] != 0 || qo_indptr[l][G] > num_queries)) {
+      set_error("be_cascade_plan: level %d indptr does not start at 0 or exceeds %d queries", l,
+                num_queries);
+      return BE_EINVAL;
+    }
+    kvlist.insert(kvlist.end(), kv_indices[l], kv_indices[l] + npages_total);
+    for (int gi = 0; gi < G; ++gi) {
+      const int qlen = qo_indptr[l][gi + 1] - qo_indptr[l][gi];
+      const int np = kv_indptr[l][gi + 1] - kv_indptr[l][gi];
+      if (qlen < 0 || np < 0) {
+        set_error("be_cascade_plan: level %d group %d has negative extent", l, gi);
+        return BE_EINVAL;
+      }
+      const int last = last_page_len[l][gi];
+      if (np > 0 && (last < 0 || last > page_size)) {
+        set_error("be_cascade_plan: level %d group %d last_page_len %d outside [0, %d]", l, gi, last,
+                  page_size);
+        return BE_EINVAL;
+      }
+      const int kv_len = np > 0 ? (np - 1) * page_size + last : 0;
+      groups.push_back({l, qo_indptr[l][gi], qlen, base + kv_indptr[l][gi], kv_len});
+      total_cost += (int64_t)kv_len * ((qlen + tile_queries(qlen, g) - 1) / std::max(1, tile_queries(qlen, g)));
+    }
+  }
+  // KV split: aim for ~4 CTAs per SM in total (CTAs = items x kv heads), but keep
+  // chunks long enough that the fp32 partial rows stay small next to the KV bytes
+  // they summarise (>= 8 tokens per row of the tile).
+  const int sms = num_sms > 0 ? num_sms : 148;
+  const int64_t target_items = std::max<int64_t>(1, (int64_t)sms * 4 / num_kv_heads);
+  auto round_pages = [&](int64_t t) {
+    return (int)std::max<int64_t>(page_size, (t + page_size - 1) / page_size * page_size);
+  };
+  const int balanced = round_pages((total_cost + target_items - 1) / target_items);
+  std::vector<W> items;
+  std::vector<int32_t> qlist;
+  for (const auto& gr : groups) {
+    if (gr.kv_len <= 0 || gr.qlen <= 0) continue;  // empty KV: lse = -inf, contributes nothing
+    const bool causal = causal_last && gr.level == num_levels - 1;
+    const int tq = tile_queries(gr.qlen, g);
+    const bool wide = tq * g > 16;
+    int chunk;
+    if (split_tokens > 0) {
+      chunk = round_pages(split_tokens);
+    } else {
+      const int min_chunk = round_pages((int64_t)std::min(gr.qlen, tq) * g * 8);
+      chunk = std::max(min_chunk, balanced);
+      const int nsplit = (gr.kv_len + chunk - 1) / chunk;
+      chunk = round_pages((gr.kv_len + nsplit - 1) / nsplit);
+    }
+    for (int qs = 0; qs < gr.qlen; qs += tq) {
+      const int ql = std::min(tq, gr.qlen - qs);
+      const int q_off = (int)qlist.size();
+      for (int i = 0; i < ql; ++i) qlist.push_back(gr.q0 + qs + i);
+      // causal limit of query i of this tile: kv_len - qlen + (qs + i) + 1
+      const int kv_total_eff = gr.kv_len - gr.qlen + qs + ql;
+      for (int t = 0; t < gr.kv_len; t += chunk) {
+        const int t1 = std::min(gr.kv_len, t + chunk);
+        if (causal && t >= kv_total_eff) break;  // no query of the tile sees this chunk
+        W it;
+        it.w.q_off = q_off;
+        it.w.q_len = ql;
+        it.w.kv_off = gr.kv_off;
+        it.w.kv_begin = t;
+        it.w.kv_end = t1;
+        it.w.kv_total = kv_total_eff;
+        it.w.part_base = 0;
+        it.w.flags = causal ? BE_WORK_CAUSAL : 0;
+        it.cost = (int64_t)(t1 - t);
+        it.wide = wide;
+        items.push_back(it);
+      }
+    }
+  }
+  return emit_plan(items, qlist, kvlist, num_queries, true, page_size, g, plan, plan_capacity, info);
+}
+
+extern "C" int be_tree_plan(int num_vnodes, const int32_t* q_entries, int num_q_entries,
+                            const int32_t* q_offs, const int32_t* q_lens, const int32_t* kv_offs,
+                            const int32_t* kv_lens, const int32_t* r2v_entries,
+                            const int32_t* r2v_offs, const int32_t* r2v_lens, int batch_size,
+                            int page_size, int num_qo_heads, int num_kv_heads, int32_t* plan,
+                            int64_t plan_capacity, be_attn_plan_info* info) {
+  if (num_vnodes < 0 || batch_size < 0 || page_size < 1 || num_kv_heads < 1 ||
+      num_qo_heads % num_kv_heads || !info) {
+    set_error("be_tree_plan: invalid arguments");
+    return BE_EINVAL;
+  }
+  const int g = num_qo_heads / num_kv_heads;
+  std::vector<W> items;
+  for (int v = 0; v < num_vnodes; ++v) {
+    if (q_lens[v] <= 0) continue;
+    if (q_lens[v] * g > 64) {
+      set_error("be_tree_plan: vnode %d has %d queries x group %d > 64 rows", v, q_lens[v], g);
+      return BE_EINVAL;
+    }
+    if (q_offs[v] < 0 || q_offs[v] + q_lens[v] > num_q_entries) {
+      set_error("be_tree_plan: vnode %d query range outside the entry list", v);
+      return BE_EINVAL;
+    }
+    W it;
+    it.w.q_off = q_offs[v];
+    it.w.q_len = q_lens[v];
+    it.w.kv_off = kv_offs[v];
+    it.w.kv_begin = 0;
+    it.w.kv_end = kv_lens[v];
+    it.w.kv_total = kv_lens[v];
+    it.w.part_base = 0;
+    it.w.flags = BE_WORK_SLOTS;
+    it.cost = kv_lens[v];
+    it.wide = q_lens[v] * g > 16;
+    items.push_back(it);
+  }
+  std::vector<int32_t> qlist(q_entries, q_entries + num_q_entries);
+  // Partial rows follow FastTree's layout: entry e of the query list owns row e.
+  std::stable_sort(items.begin(), items.end(), [](const W& a, const W& b) {
+    if (a.wide != b.wide) return a.wide;
+    return a.cost > b.cost;
+  });
+  std::vector<int32_t> mq, mptr{0}, mparts;
+  for (int b = 0; b < batch_size; ++b) {
+    mq.push_back(b);
+    for (int k = 0; k < r2v_lens[b]; ++k) mparts.push_back(r2v_entries[r2v_offs[b] + k]);
+    mptr.push_back((int32_t)mparts.size());
+  }
+  be_attn_plan_info in{};
+  in.n_work = (int32_t)items.size();
+  in.n_work_wide = (int32_t)std::count_if(items.begin(), items.end(), [](const W& x) { return x.wide; });
+  in.n_queries = batch_size;
+  in.n_parts = num_q_entries;
+  in.n_merge = batch_size;
+  int64_t off = (int64_t)items.size() * 8;
+  in.off_work = 0;
+  in.off_qlist = (int32_t)off;
+  off += qlist.size();
+  in.off_kvlist = (int32_t)off;
+  in.off_merge_q = (int32_t)off;
+  off += mq.size();
+  in.off_merge_ptr = (int32_t)off;
+  off += mptr.size();
+  in.off_merge_parts = (int32_t)off;
+  off += mparts.size();
+  in.total_ints = (int32_t)off;
+  in.page_size = page_size;
+  in.group_size = g;
+  *info = in;
+  if (off > plan_capacity || !plan) {
+    set_error("plan buffer too small: need %lld ints, have %lld", (long long)off,
+              (long long)plan_capacity);
+    return BE_ECAPACITY;
+  }
+  int32_t* p = plan;
+  for (auto& it : items) {
+    it.w.part_base = it.w.q_off;
+    std::memcpy(p, &it.w, sizeof(be_attn_work));
+    p += 8;
+  }
+  auto put = [&](const std::vector<int32_t>& v) {
+    if (!v.empty()) std::memcpy(p, v.data(), v.size() * sizeof(int32_t));
+    p += v.size();
+  };
+  put(qlist);
+  put(mq);
+  put(mptr);
+  put(mparts);
+  return BE_OK;
+}

@@ -1,0 +1,680 @@
+// Host page manager: FIFO page allocator + beam trie with copy-on-write forks,
+// cascade / FastTree metadata builders and the vanilla beam selection.
+//
+// Semantics follow the reference (brian030128/beam_engine):
+//   allocator            src/beam_engine/page_table.py:59-60, 77-124
+//   trie + fork/free      src/beam_engine/beam_state.py:12-30, 76-209
+//   cascade levels        src/beam_engine/beam_state.py:211-412
+//   FastTree inputs       src/beam_engine/beam_state.py:414-633
+//   FastTree planner      src/beam_engine/attention/fasttree/preparation.py:11-225
+//   vanilla selection     src/beam_engine/beam_strategy.py:433-488
+//   final ranking         src/beam_engine/beam_state.py:646-682
+// Node ids are stable handles; pages are plain ints shared with the device pools.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <deque>
+#include <numeric>
+#include <unordered_map>
+#include <vector>
+
+#include "beam_b200.h"
+
+namespace be {
+void set_error(const char* fmt, ...);
+}
+using be::set_error;
+
+struct be_trie {
+  struct Node {
+    int32_t parent = -1;
+    int32_t page = -1;
+    std::vector<int32_t> tokens;
+    std::vector<int32_t> children;
+  };
+  int page_size = 0;
+  int max_pages = 0;
+  std::deque<int32_t> free_pages;
+  std::vector<char> allocated;
+  std::vector<Node> nodes;
+  std::vector<int32_t> level_memo;  // per call scratch
+  std::vector<int32_t> memo_gen;
+  int32_t gen = 0;
+  int64_t warnings = 0;
+
+  int alloc(int32_t* out) {
+    if (free_pages.empty()) {
+      set_error("No free pages available");
+      return BE_ENOMEM;
+    }
+    *out = free_pages.front();
+    free_pages.pop_front();
+    allocated[*out] = 1;
+    return BE_OK;
+  }
+  int release(int32_t p) {
+    if (p < 0 || p >= max_pages || !allocated[p]) {
+      ++warnings;
+      set_error("Page %d is not allocated", p);
+      return BE_ENOT_ALLOCATED;
+    }
+    allocated[p] = 0;
+    free_pages.push_back(p);
+    return BE_OK;
+  }
+  int32_t add_node(int32_t parent, int32_t page, const int32_t* tok, int n) {
+    Node nd;
+    nd.parent = parent;
+    nd.page = page;
+    nd.tokens.assign(tok, tok + n);
+    nodes.push_back(std::move(nd));
+    const int32_t id = (int32_t)nodes.size() - 1;
+    if (parent >= 0) nodes[parent].children.push_back(id);
+    return id;
+  }
+  bool valid(int32_t n) const { return n >= 0 && n < (int32_t)nodes.size(); }
+  void path(int32_t leaf, std::vector<int32_t>& out) const {
+    out.clear();
+    for (int32_t n = leaf; n >= 0; n = nodes[n].parent) out.push_back(n);
+    std::reverse(out.begin(), out.end());
+  }
+  int64_t seq_len(int32_t leaf) const {
+    int64_t s = 0;
+    for (int32_t n = leaf; n >= 0; n = nodes[n].parent) s += nodes[n].tokens.size();
+    return s;
+  }
+  int32_t level(int32_t n) {
+    // level(root) = 0; level(n) = level(parent) + (parent has > 1 children)
+    std::vector<int32_t> stack;
+    int32_t cur = n;
+    while (cur >= 0 && memo_gen[cur] != gen) {
+      stack.push_back(cur);
+      cur = nodes[cur].parent;
+    }
+    int32_t lv = cur >= 0 ? level_memo[cur] : 0;
+    for (auto it = stack.rbegin(); it != stack.rend(); ++it) {
+      const int32_t p = nodes[*it].parent;
+      lv = p < 0 ? 0 : lv + (nodes[p].children.size() > 1 ? 1 : 0);
+      level_memo[*it] = lv;
+      memo_gen[*it] = gen;
+    }
+    return level_memo[n];
+  }
+  void new_generation() {
+    ++gen;
+    if (level_memo.size() < nodes.size()) {
+      level_memo.resize(nodes.size(), 0);
+      memo_gen.resize(nodes.size(), 0);
+    }
+  }
+};
+
+extern "C" {
+
+be_trie* be_trie_create(int page_size, int max_num_pages) {
+  if (page_size < 1 || max_num_pages < 0) {
+    set_error("be_trie_create: invalid page_size/max_num_pages");
+    return nullptr;
+  }
+  auto* t = new be_trie();
+  t->page_size = page_size;
+  t->max_pages = max_num_pages;
+  for (int i = 0; i < max_num_pages; ++i) t->free_pages.push_back(i);
+  t->allocated.assign(max_num_pages, 0);
+  return t;
+}
+
+void be_trie_destroy(be_trie* t) { delete t; }
+
+int be_alloc_page(be_trie* t, int32_t* page) { return t->alloc(page); }
+int be_free_page(be_trie* t, int32_t page) { return t->release(page); }
+int be_num_free_pages(be_trie* t) { return (int)t->free_pages.size(); }
+int be_is_allocated(be_trie* t, int32_t page) {
+  return page >= 0 && page < t->max_pages && t->allocated[page];
+}
+int be_free_list(be_trie* t, int32_t* out, int cap) {
+  const int n = (int)t->free_pages.size();
+  for (int i = 0; i < n && i < cap; ++i) out[i] = t->free_pages[i];
+  return n;
+}
+int64_t be_trie_warnings(be_trie* t) { return t->warnings; }
+int be_trie_num_nodes(be_trie* t) { return (int)t->nodes.size(); }
+
+int be_node_new(be_trie* t, int32_t parent, int32_t page, const int32_t* tokens, int n,
+                int32_t* node_out) {
+  if (parent >= 0 && !t->valid(parent)) {
+    set_error("be_node_new: bad parent %d", parent);
+    return BE_EINVAL;
+  }
+  *node_out = t->add_node(parent, page, tokens, n);
+  return BE_OK;
+}
+
+int be_node_info(be_trie* t, int32_t node, int32_t* parent, int32_t* page, int32_t* ntokens,
+                 int32_t* nchildren) {
+  if (!t->valid(node)) {
+    set_error("be_node_info: bad node %d", node);
+    return BE_EINVAL;
+  }
+  const auto& nd = t->nodes[node];
+  if (parent) *parent = nd.parent;
+  if (page) *page = nd.page;
+  if (ntokens) *ntokens = (int32_t)nd.tokens.size();
+  if (nchildren) *nchildren = (int32_t)nd.children.size();
+  return BE_OK;
+}
+
+int be_node_tokens(be_trie* t, int32_t node, int32_t* out, int cap) {
+  if (!t->valid(node)) return -1;
+  const auto& v = t->nodes[node].tokens;
+  for (int i = 0; i < (int)v.size() && i < cap; ++i) out[i] = v[i];
+  return (int)v.size();
+}
+
+int be_node_children(be_trie* t, int32_t node, int32_t* out, int cap) {
+  if (!t->valid(node)) return -1;
+  const auto& v = t->nodes[node].children;
+  for (int i = 0; i < (int)v.size() && i < cap; ++i) out[i] = v[i];
+  return (int)v.size();
+}
+
+int be_node_append_token(be_trie* t, int32_t node, int32_t token) {
+  if (!t->valid(node)) {
+    set_error("be_node_append_token: bad node %d", node);
+    return BE_EINVAL;
+  }
+  t->nodes[node].tokens.push_back(token);
+  return BE_OK;
+}
+
+// Token sequence root -> leaf; returns its length (writes up to cap tokens).
+int64_t be_node_sequence(be_trie* t, int32_t leaf, int32_t* out, int64_t cap) {
+  if (!t->valid(leaf)) return -1;
+  std::vector<int32_t> p;
+  t->path(leaf, p);
+  int64_t k = 0;
+  for (int32_t n : p)
+    for (int32_t tok : t->nodes[n].tokens) {
+      if (k < cap) out[k] = tok;
+      ++k;
+    }
+  return k;
+}
+
+// BeamState.add_root_sequence (beam_state.py:76-98).
+int be_beam_add_root(be_trie* t, const int32_t* tokens, int n, int32_t* leaf_out,
+                     int32_t* pages_out) {
+  int32_t cur = -1;
+  int k = 0;
+  for (int s = 0; s < n; s += t->page_size) {
+    int32_t page;
+    int rc = t->alloc(&page);
+    if (rc) return rc;
+    const int e = std::min(n, s + t->page_size);
+    cur = t->add_node(cur, page, tokens + s, e - s);
+    if (pages_out) pages_out[k] = page;
+    ++k;
+  }
+  *leaf_out = cur;
+  return BE_OK;
+}
+
+// BeamState.add_filtered_results (beam_state.py:101-209).
+// Candidate i's children are child_tokens[child_ptr[i] .. child_ptr[i+1]).
+// Outputs, in the reference's new-candidate order: new_leaf[k] and new_child[k]
+// (index into child_tokens, to carry the score), count in *n_new; the
+// copy-on-write copies (src page, dst page, tokens) in issue order, count in
+// *n_copies.  Output arrays need room for child_ptr[ncand] entries.
+int be_beam_update(be_trie* t, int ncand, const int32_t* cand_leaf, const int32_t* child_ptr,
+                   const int32_t* child_tokens, int32_t* new_leaf, int32_t* new_child,
+                   int32_t* n_new, int32_t* copy_src, int32_t* copy_dst, int32_t* copy_len,
+                   int32_t* n_copies) {
+  for (int i = 0; i < ncand; ++i)
+    if (!t->valid(cand_leaf[i])) {
+      set_error("be_beam_update: bad leaf %d", cand_leaf[i]);
+      return BE_EINVAL;
+    }
+  // 1. free dead branches upward
+  for (int i = 0; i < ncand; ++i) {
+    if (child_ptr[i + 1] > child_ptr[i]) continue;
+    int32_t n = cand_leaf[i];
+    while (n >= 0 && t->nodes[n].children.empty()) {
+      t->release(t->nodes[n].page);
+      const int32_t par = t->nodes[n].parent;
+      if (par >= 0) {
+        auto& ch = t->nodes[par].children;
+        auto it = std::find(ch.begin(), ch.end(), n);
+        if (it != ch.end()) ch.erase(it);
+      }
+      n = par;
+    }
+  }
+  // 2. expand survivors
+  int k = 0, c = 0;
+  const int ps = t->page_size;
+  for (int i = 0; i < ncand; ++i) {
+    const int c0 = child_ptr[i], c1 = child_ptr[i + 1];
+    if (c1 <= c0) continue;
+    const int32_t nid = cand_leaf[i];
+    if (c1 - c0 == 1) {
+      if ((int)t->nodes[nid].tokens.size() < ps) {
+        t->nodes[nid].tokens.push_back(child_tokens[c0]);
+        new_leaf[k] = nid;
+      } else {
+        int32_t page;
+        int rc = t->alloc(&page);
+        if (rc) return rc;
+        new_leaf[k] = t->add_node(nid, page, &child_tokens[c0], 1);
+      }
+      new_child[k++] = c0;
+      continue;
+    }
+    if ((int)t->nodes[nid].tokens.size() == ps) {
+      for (int j = c0; j < c1; ++j) {
+        int32_t page;
+        int rc = t->alloc(&page);
+        if (rc) return rc;
+        new_leaf[k] = t->add_node(nid, page, &child_tokens[j], 1);
+        new_child[k++] = j;
+      }
+    } else {
+      const std::vector<int32_t> base = t->nodes[nid].tokens;
+      const int32_t src_page = t->nodes[nid].page;
+      for (int j = c0 + 1; j < c1; ++j) {
+        int32_t page;
+        int rc = t->alloc(&page);
+        if (rc) return rc;
+        copy_src[c] = src_page;
+        copy_dst[c] = page;
+        copy_len[c] = (int32_t)base.size();
+        ++c;
+        std::vector<int32_t> tk = base;
+        tk.push_back(child_tokens[j]);
+        new_leaf[k] = t->add_node(t->nodes[nid].parent, page, tk.data(), (int)tk.size());
+        new_child[k++] = j;
+      }
+      t->nodes[nid].tokens.push_back(child_tokens[c0]);
+      new_leaf[k] = nid;
+      new_child[k++] = c0;
+    }
+  }
+  *n_new = k;
+  *n_copies = c;
+  return BE_OK;
+}
+
+// Per-candidate decode inputs (beam.py:168-221): query token (last token of the
+// leaf, 0 if empty), append target (leaf page, len(leaf tokens) - 1) and the
+// RoPE position (sequence length - 1).
+int be_beam_step_inputs(be_trie* t, int ncand, const int32_t* cand_leaf, int32_t* query_tok,
+                        int32_t* write_page, int32_t* write_pos, int32_t* position) {
+  for (int i = 0; i < ncand; ++i) {
+    const int32_t n = cand_leaf[i];
+    if (!t->valid(n)) {
+      set_error("be_beam_step_inputs: bad leaf %d", n);
+      return BE_EINVAL;
+    }
+    const auto& nd = t->nodes[n];
+    if (query_tok) query_tok[i] = nd.tokens.empty() ? 0 : nd.tokens.back();
+    if (write_page) write_page[i] = nd.page;
+    if (write_pos) write_pos[i] = (int32_t)nd.tokens.size() - 1;
+    if (position) position[i] = (int32_t)(t->seq_len(n) - 1);
+  }
+  return BE_OK;
+}
+
+// BeamState.get_cascade_input (beam_state.py:211-412).  Writes, per level l,
+// groups qo/kv indptr, page list and last-page lengths into flat arrays:
+// level l's groups are level_group_ptr[l]..[l+1] (qo_indptr/kv_indptr/last use
+// one entry per group plus a leading 0 per level for the indptrs), its pages
+// level_page_ptr[l]..[l+1].  Returns the number of levels (>= 0) or -status.
+// Capacities: levels <= cap_levels, groups <= cap_groups, pages <= cap_pages.
+int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_levels,
+                     int cap_groups, int cap_pages, int32_t* level_group_ptr,
+                     int32_t* level_page_ptr, int32_t* qo_indptr, int32_t* kv_indptr,
+                     int32_t* kv_indices, int32_t* last_page_len) {
+  t->new_generation();
+  struct Seg {
+    int32_t first, last;  // indices into the candidate's path
+  };
+  std::vector<std::vector<int32_t>> paths(ncand);
+  std::vector<std::vector<Seg>> segs(ncand);  // by level
+  int top = 0;
+  for (int c = 0; c < ncand; ++c) {
+    if (!t->valid(cand_leaf[c])) {
+      set_error("be_cascade_build: bad leaf %d", cand_leaf[c]);
+      return -BE_EINVAL;
+    }
+    t->path(cand_leaf[c], paths[c]);
+    auto& sg = segs[c];
+    for (int i = 0; i < (int)paths[c].size(); ++i) {
+      const int lv = t->level(paths[c][i]);
+      while ((int)sg.size() <= lv) sg.push_back({-1, -1});
+      if (sg[lv].first < 0) sg[lv].first = i;
+      sg[lv].last = i;
+      top = std::max(top, lv);
+    }
+  }
+  const int nlev = ncand > 0 ? top + 1 : 0;
+  if (nlev > cap_levels) {
+    set_error("be_cascade_build: %d levels exceed capacity %d", nlev, cap_levels);
+    return -BE_ECAPACITY;
+  }
+  int gbase = 0, pbase = 0;
+  std::unordered_map<int32_t, int> key_to_group;
+  std::vector<int32_t> seen;
+  for (int lv = 0; lv < nlev; ++lv) {
+    level_group_ptr[lv] = gbase;
+    level_page_ptr[lv] = pbase;
+    key_to_group.clear();
+    struct G {
+      int cand0, count;
+      Seg seg;
+    };
+    std::vector<G> groups;
+    for (int c = 0; c < ncand; ++c) {
+      const auto& sg = segs[c];
+      Seg s = (lv < (int)sg.size() && sg[lv].first >= 0) ? sg[lv] : sg.back();
+      if (s.first < 0) {  // deepest level always exists; keep the compiler honest
+        for (int k = (int)sg.size() - 1; k >= 0; --k)
+          if (sg[k].first >= 0) { s = sg[k]; break; }
+      }
+      const int32_t key = paths[c][s.last];
+      auto it = key_to_group.find(key);
+      if (it == key_to_group.end()) {
+        key_to_group[key] = (int)groups.size();
+        groups.push_back({c, 1, s});
+      } else {
+        groups[it->second].count++;
+      }
+    }
+    if (gbase + (int)groups.size() > cap_groups) {
+      set_error("be_cascade_build: group capacity %d exceeded", cap_groups);
+      return -BE_ECAPACITY;
+    }
+    // indptr arrays carry one leading zero per level: level lv occupies
+    // [gbase + lv, gbase + lv + ngroups]
+    int32_t* qo = qo_indptr + gbase + lv;
+    int32_t* kvp = kv_indptr + gbase + lv;
+    qo[0] = 0;
+    kvp[0] = 0;
+    int npages = 0;
+    for (size_t gi = 0; gi < groups.size(); ++gi) {
+      const auto& g = groups[gi];
+      const auto& p = paths[g.cand0];
+      seen.clear();
+      for (int i = g.seg.first; i <= g.seg.last; ++i) {
+        const int32_t pg = t->nodes[p[i]].page;
+        if (std::find(seen.begin(), seen.end(), pg) != seen.end()) continue;
+        seen.push_back(pg);
+        if (pbase + npages >= cap_pages) {
+          set_error("be_cascade_build: page capacity %d exceeded", cap_pages);
+          return -BE_ECAPACITY;
+        }
+        kv_indices[pbase + npages++] = pg;
+      }
+      const int32_t tail = p[g.seg.last];
+      const int ln = (int)t->nodes[tail].tokens.size();
+      last_page_len[gbase + gi] = (tail == cand_leaf[g.cand0]) ? std::max(0, ln - 1) : ln;
+      kvp[gi + 1] = npages;
+      qo[gi + 1] = qo[gi] + g.count;
+    }
+    gbase += (int)groups.size();
+    pbase += npages;
+  }
+  level_group_ptr[nlev] = gbase;
+  level_page_ptr[nlev] = pbase;
+  return nlev;
+}
+
+// BeamState._build_kv_tree_structure + _build_req_to_token (beam_state.py:414-564).
+// Nodes in BFS order from the roots: node_parent / node_seqlen / node_children
+// and their request lists (CSR req_ptr / req_list); per_node != 0 gives each
+// node's own token count as seqlen (the reference stores the cumulative length,
+// which its planner then misreads as a per-node length).  page_size > 0
+// overrides the trie's page size for the slot ids.  req_to_token is
+// [ncand][*max_len] slot ids (page * page_size + i), zero padded; pass
+// req_to_token = NULL to query *max_len and *num_nodes first.
+int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node, int page_size,
+                  int cap_nodes,
+                  int32_t* num_nodes, int32_t* node_parent, int32_t* node_seqlen,
+                  int32_t* node_children, int32_t* req_ptr, int32_t* req_list,
+                  int64_t cap_req_list, int32_t* max_len, int32_t* req_to_token,
+                  int64_t cap_req_to_token) {
+  std::vector<int32_t> roots;
+  std::vector<std::vector<int32_t>> paths(ncand);
+  int64_t ml = 0;
+  for (int c = 0; c < ncand; ++c) {
+    if (!t->valid(cand_leaf[c])) {
+      set_error("be_tree_build: bad leaf %d", cand_leaf[c]);
+      return BE_EINVAL;
+    }
+    t->path(cand_leaf[c], paths[c]);
+    if (std::find(roots.begin(), roots.end(), paths[c][0]) == roots.end())
+      roots.push_back(paths[c][0]);
+    ml = std::max(ml, t->seq_len(cand_leaf[c]));
+  }
+  std::unordered_map<int32_t, int32_t> tid;
+  std::vector<int32_t> order;
+  std::deque<int32_t> q(roots.begin(), roots.end());
+  while (!q.empty()) {
+    const int32_t n = q.front();
+    q.pop_front();
+    if (tid.count(n)) continue;
+    tid[n] = (int32_t)order.size();
+    order.push_back(n);
+    for (int32_t ch : t->nodes[n].children)
+      if (!tid.count(ch)) q.push_back(ch);
+  }
+  *num_nodes = (int32_t)order.size();
+  *max_len = (int32_t)ml;
+  if (!req_to_token) return BE_OK;
+  if ((int)order.size() > cap_nodes || (int64_t)ncand * ml > cap_req_to_token) {
+    set_error("be_tree_build: capacity exceeded");
+    return BE_ECAPACITY;
+  }
+  // requests per node (candidate order)
+  std::vector<std::vector<int32_t>> reqs(order.size());
+  for (int c = 0; c < ncand; ++c)
+    for (int32_t n : paths[c]) reqs[tid[n]].push_back(c);
+  int64_t rp = 0;
+  for (size_t i = 0; i < order.size(); ++i) {
+    const auto& nd = t->nodes[order[i]];
+    node_parent[i] = nd.parent < 0 ? -1 : (tid.count(nd.parent) ? tid[nd.parent] : -1);
+    node_seqlen[i] = per_node ? (int32_t)nd.tokens.size() : (int32_t)t->seq_len(order[i]);
+    node_children[i] = (int32_t)nd.children.size();
+    req_ptr[i] = (int32_t)rp;
+    for (int32_t r : reqs[i]) {
+      if (rp >= cap_req_list) {
+        set_error("be_tree_build: request list capacity exceeded");
+        return BE_ECAPACITY;
+      }
+      req_list[rp++] = r;
+    }
+  }
+  req_ptr[order.size()] = (int32_t)rp;
+  const int ps = page_size > 0 ? page_size : t->page_size;
+  for (int c = 0; c < ncand; ++c) {
+    int32_t* row = req_to_token + (int64_t)c * ml;
+    int64_t k = 0;
+    for (int32_t n : paths[c])
+      for (size_t i = 0; i < t->nodes[n].tokens.size(); ++i) row[k++] = t->nodes[n].page * ps + (int32_t)i;
+    for (; k < ml; ++k) row[k] = 0;
+  }
+  return BE_OK;
+}
+
+// prepare_fasttree_metadata_for_paged_cache (preparation.py:11-225, parameters
+// metadata.py:12-38): SplitK/SplitQ cost model per edge, merged request sets,
+// vnode emission with KV splits, req->vnode lists and the two-phase reorder.
+// Tree arrays as written by be_tree_build.  Output capacities: cap_vnodes for
+// the per-vnode arrays, cap_entries for q_entries / r2v_entries.  counts[0] =
+// vnodes, counts[1] = entries, counts[2..3] = phase node counts.
+int be_fasttree_prepare(int num_nodes, const int32_t* node_parent, const int32_t* node_seqlen,
+                        const int32_t* node_children, const int32_t* req_ptr,
+                        const int32_t* req_list, int64_t req_to_token_stride, int batch_size,
+                        int num_qo_heads, int num_kv_heads, int cap_vnodes, int cap_entries,
+                        int32_t* q_entries, int32_t* q_offs, int32_t* q_lens, int32_t* kv_offs,
+                        int32_t* kv_lens, int32_t* r2v_entries, int32_t* r2v_offs,
+                        int32_t* r2v_lens, int32_t* counts) {
+  if (num_kv_heads < 1 || num_qo_heads % num_kv_heads) {
+    set_error("be_fasttree_prepare: bad head counts");
+    return BE_EINVAL;
+  }
+  const int g = num_qo_heads / num_kv_heads;
+  const int tsq[2] = {std::max(1, 64 / g), std::max(1, 16 / g)};
+  const int tsk[2] = {32, 32};
+  const int split[2] = {1024, 1024};  // preparation.py:39 uses kv_split_sizes[0] for both phases
+  const double alpha = 0.6, beta = 0.3, gamma = 0.1;
+  // Python's floor modulo: ((n - 1) % ts) is ts - 1 for n = 0
+  auto padq = [](int ts, int n) { return ts - ((((n - 1) % ts) + ts) % ts + 1); };
+  auto padk = [](int ts, int n) { return std::max(0, ts - n); };
+  auto cmm = [&](int nq, int nk) {
+    const int ph = nq > tsq[1] ? 0 : 1;
+    return alpha * padq(tsq[ph], nq) * g * nk + beta * padk(tsk[ph], nk) * nq * g;
+  };
+  const int n = num_nodes;
+  auto nreq = [&](int i) { return req_ptr[i + 1] - req_ptr[i]; };
+  std::vector<std::vector<int>> kids(n);
+  for (int i = 0; i < n; ++i)
+    if (node_parent[i] != -1) kids[node_parent[i]].push_back(i);
+  std::vector<int64_t> L(node_seqlen, node_seqlen + n);
+  std::vector<int> merged(n, 0);
+  if (n > 0) {
+    std::deque<int> fifo{0};
+    while (!fifo.empty()) {
+      const int v = fifo.front();
+      fifo.pop_front();
+      int nq_cur = nreq(v);
+      const int64_t lenv = L[v];
+      for (int c : kids[v]) {
+        const int nql = nreq(c);
+        const int64_t lenl = L[c];
+        const double sk = cmm(nq_cur, (int)lenv) + cmm(nql, (int)lenl) + gamma * nql;
+        const double sq = cmm(nq_cur - nql, (int)lenv) + cmm(nql, (int)(lenl + lenv));
+        if (sk > sq) {
+          merged[c] = 1;
+          nq_cur -= nql;
+          L[c] = lenl + lenv;
+        }
+        fifo.push_back(c);
+      }
+    }
+  }
+  std::vector<std::vector<int32_t>> node_reqs(n);
+  std::deque<int> fifo;
+  for (int i = 0; i < n; ++i)
+    if (node_children[i] == 0) {
+      fifo.push_back(i);
+      node_reqs[i].assign(req_list + req_ptr[i], req_list + req_ptr[i + 1]);
+    }
+  std::vector<int> vkids(node_children, node_children + n);
+  while (!fifo.empty()) {
+    const int v = fifo.front();
+    fifo.pop_front();
+    const int par = node_parent[v];
+    if (merged[v] == 0 && v != 0)  // par == -1 would index the last entry, as in Python
+      node_reqs[par >= 0 ? par : n - 1].insert(node_reqs[par >= 0 ? par : n - 1].end(),
+                                                req_list + req_ptr[v], req_list + req_ptr[v + 1]);
+    vkids[par >= 0 ? par : n - 1] -= 1;
+    if (par >= 0 && vkids[par] == 0) fifo.push_back(par);
+  }
+  std::vector<int64_t> tok_off(n, 0);
+  for (int i = 1; i < n; ++i) tok_off[i] = tok_off[node_parent[i]] + node_seqlen[node_parent[i]];
+  std::vector<int32_t> qe, qo, ql, ko, kl;
+  for (int i = 0; i < n; ++i) {
+    const auto& reqs = node_reqs[i];
+    if (reqs.empty()) continue;
+    int64_t kv_len = node_seqlen[i];
+    int v = i;
+    while (merged[v] == 1) {
+      v = node_parent[v];
+      kv_len += node_seqlen[v];
+    }
+    const int nr = (int)reqs.size();
+    const int ph = nr > tsq[1] ? 0 : 1;
+    const int kvs = split[ph], qs = tsq[ph];
+    const int64_t kv_start = req_to_token_stride * reqs[0] + tok_off[v];
+    for (int64_t s = 0; s < (kv_len - 1) / kvs + 1; ++s) {
+      const int q0 = (int)qe.size();
+      qe.insert(qe.end(), reqs.begin(), reqs.end());
+      const int64_t koff = s * kvs;
+      const int64_t klen = std::min<int64_t>(koff + kvs, kv_len) - koff;
+      for (int j = 0; j < (nr - 1) / qs + 1; ++j) {
+        const int qoff = j * qs;
+        ko.push_back((int32_t)(kv_start + koff));
+        kl.push_back((int32_t)klen);
+        qo.push_back(q0 + qoff);
+        ql.push_back(std::min(qoff + qs, nr) - qoff);
+      }
+    }
+  }
+  const int nv = (int)ko.size(), ne = (int)qe.size();
+  if (nv > cap_vnodes || ne > cap_entries) {
+    set_error("be_fasttree_prepare: %d vnodes / %d entries exceed capacity", nv, ne);
+    counts[0] = nv;
+    counts[1] = ne;
+    return BE_ECAPACITY;
+  }
+  std::vector<std::vector<int32_t>> r2v(batch_size);
+  for (int e = 0; e < ne; ++e) r2v[qe[e]].push_back(e);
+  int off = 0, k = 0;
+  for (int b = 0; b < batch_size; ++b) {
+    r2v_offs[b] = off;
+    r2v_lens[b] = (int32_t)r2v[b].size();
+    off += (int)r2v[b].size();
+    for (int32_t e : r2v[b]) r2v_entries[k++] = e;
+  }
+  std::copy(qe.begin(), qe.end(), q_entries);
+  int w = 0, above = 0;
+  for (int pass = 0; pass < 2; ++pass)
+    for (int i = 0; i < nv; ++i) {
+      const bool is_above = ql[i] > tsq[1];
+      if ((pass == 0) != is_above) continue;
+      q_offs[w] = qo[i];
+      q_lens[w] = ql[i];
+      kv_offs[w] = ko[i];
+      kv_lens[w] = kl[i];
+      ++w;
+      if (pass == 0) ++above;
+    }
+  counts[0] = nv;
+  counts[1] = ne;
+  counts[2] = above;
+  counts[3] = nv - above;
+  return BE_OK;
+}
+
+// VanillaBeamSearchStrategy.select_candidates (beam_strategy.py:433-488).
+// Candidate i offers k children (tokens[i*k + j], logps[i*k + j], in top-k
+// order; the reference's log-probs are fp32 values held as Python floats); totals are parent_scores[i] + logp in double; a stable descending
+// sort keeps the first beam_size; results regroup per parent in sorted order.
+// Outputs: child_ptr [n+1], child_tokens / child_scores [beam_size].
+int be_vanilla_select(int n, int k, const double* parent_scores, const int32_t* tokens,
+                      const double* logps, int beam_size, int32_t* child_ptr,
+                      int32_t* child_tokens, double* child_scores) {
+  const int64_t total = (int64_t)n * k;
+  std::vector<int64_t> idx(total);
+  std::vector<double> sc(total);
+  for (int64_t e = 0; e < total; ++e) {
+    idx[e] = e;
+    sc[e] = parent_scores[e / k] + logps[e];
+  }
+  std::stable_sort(idx.begin(), idx.end(), [&](int64_t a, int64_t b) { return sc[a] > sc[b]; });
+  const int64_t keep = std::min<int64_t>(beam_size, total);
+  std::vector<std::vector<int64_t>> per(n);
+  for (int64_t r = 0; r < keep; ++r) per[idx[r] / k].push_back(idx[r]);
+  int o = 0;
+  child_ptr[0] = 0;
+  for (int i = 0; i < n; ++i) {
+    for (int64_t e : per[i]) {
+      child_tokens[o] = tokens[e];
+      child_scores[o] = sc[e];
+      ++o;
+    }
+    child_ptr[i + 1] = o;
+  }
+  return BE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,5 @@
+// Single translation unit for all device code of libbeam_b200.so: the
+// kernels share one device status word, so they are compiled together
+// instead of with relocatable device code.
+#include "page_ops.cu"
+#include "attention.cu"

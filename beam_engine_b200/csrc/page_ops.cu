@@ -1,0 +1,190 @@
+// Paged KV-cache data movement: decode append and copy-on-write tail forks.
+//
+// Both kernels are pure HBM streams: every thread moves one 16-byte vector,
+// consecutive threads touch consecutive 16-byte chunks of one head row (append)
+// or of one contiguous page prefix (fork), so each warp issues full 512-byte
+// coalesced transactions.  All layers go in one launch (the reference issues one
+// launch per layer and copy).
+#include "common.cuh"
+
+namespace be {
+
+// ---------------------------------------------------------------------------
+// Append (flashinfer.page.append_paged_kv_cache semantics, page_table.py:199-209)
+// ---------------------------------------------------------------------------
+template <int VEC_BYTES>
+__global__ void __launch_bounds__(256) append_kernel(
+    const char* __restrict__ k, const char* __restrict__ v, int64_t row_stride_b,
+    int64_t in_layer_stride_b, const int32_t* __restrict__ batch_indices,
+    const int32_t* __restrict__ positions, const int32_t* __restrict__ kv_indices,
+    const int32_t* __restrict__ kv_indptr, int nnz, char* __restrict__ pool,
+    int64_t pool_layer_stride_b, int num_layers, int num_pages, int page_size, int hkv,
+    int row_bytes /* head_dim * elt */, int64_t total_chunks) {
+  const int chunks_per_row = row_bytes / VEC_BYTES;          // per (token, head)
+  const int chunks_per_tok = chunks_per_row * hkv;            // per token, one plane
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < total_chunks;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = c;
+    const int cin = (int)(r % chunks_per_tok);
+    r /= chunks_per_tok;
+    const int plane = (int)(r % 2);
+    r /= 2;
+    const int i = (int)(r % nnz);
+    const int layer = (int)(r / nnz);
+    const int pos = positions[i];
+    const int b = batch_indices[i];
+    const int page = kv_indices[kv_indptr[b] + pos / page_size];
+    if (page < 0 || page >= num_pages || pos < 0) {
+      flag_range_error();
+      continue;
+    }
+    const int head = cin / chunks_per_row;
+    const int off = (cin % chunks_per_row) * VEC_BYTES;
+    const char* src = (plane ? v : k) + layer * in_layer_stride_b + i * row_stride_b +
+                      (int64_t)head * row_bytes + off;
+    char* dst = pool + layer * pool_layer_stride_b +
+                (((int64_t)page * 2 + plane) * page_size + pos % page_size) * hkv * row_bytes +
+                (int64_t)head * row_bytes + off;
+    if constexpr (VEC_BYTES == 16) {
+      *reinterpret_cast<int4*>(dst) = __ldg(reinterpret_cast<const int4*>(src));
+    } else if constexpr (VEC_BYTES == 4) {
+      *reinterpret_cast<int*>(dst) = __ldg(reinterpret_cast<const int*>(src));
+    } else {
+      *reinterpret_cast<short*>(dst) = *reinterpret_cast<const short*>(src);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fork: tokens [0, len) of K and V, page src -> page dst, every layer.
+// In one page plane the first `len` tokens are one contiguous run of
+// len * hkv * head_dim elements, so each (copy, layer, plane) is a memcpy.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) fork_kernel(
+    char* __restrict__ pool, int64_t pool_layer_stride_b, int num_layers, int num_pages,
+    int64_t plane_bytes, const int32_t* __restrict__ src_pages,
+    const int32_t* __restrict__ dst_pages, const int32_t* __restrict__ lens, int64_t tok_bytes) {
+  const int seg = blockIdx.y;                  // (copy, layer, plane)
+  const int plane = seg & 1;
+  const int layer = (seg >> 1) % num_layers;
+  const int j = (seg >> 1) / num_layers;
+  const int s = src_pages[j], d = dst_pages[j];
+  const int64_t n16 = (lens[j] * tok_bytes) >> 4;
+  if (s < 0 || s >= num_pages || d < 0 || d >= num_pages) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) flag_range_error();
+    return;
+  }
+  const char* src = pool + layer * pool_layer_stride_b + ((int64_t)s * 2 + plane) * plane_bytes;
+  char* dst = pool + layer * pool_layer_stride_b + ((int64_t)d * 2 + plane) * plane_bytes;
+  const int4* s4 = reinterpret_cast<const int4*>(src);
+  int4* d4 = reinterpret_cast<int4*>(dst);
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < n16;
+       c += (int64_t)gridDim.x * blockDim.x)
+    d4[c] = __ldg(s4 + c);
+}
+
+}  // namespace be
+
+using namespace be;
+
+extern "C" int be_append_paged_kv(const void* append_key, const void* append_value,
+                                  int64_t row_stride, int64_t input_layer_stride,
+                                  const int32_t* batch_indices, const int32_t* positions,
+                                  const int32_t* kv_indices, const int32_t* kv_indptr, int nnz,
+                                  void* paged_kv_cache, int64_t pool_layer_stride, int num_layers,
+                                  int num_pages, int page_size, int num_kv_heads, int head_dim,
+                                  int dtype, void* stream) {
+  if (nnz < 0 || num_layers < 1 || page_size < 1 || num_kv_heads < 1 || head_dim < 1 ||
+      dtype < BE_F32 || dtype > BE_BF16) {
+    set_error("be_append_paged_kv: invalid shape or dtype");
+    return BE_EINVAL;
+  }
+  if (nnz == 0) return BE_OK;
+  if (!append_key || !append_value || !batch_indices || !positions || !kv_indices || !kv_indptr ||
+      !paged_kv_cache) {
+    set_error("be_append_paged_kv: null pointer");
+    return BE_EINVAL;
+  }
+  const int elt = dtype_size(dtype);
+  const int row_bytes = head_dim * elt;
+  const int64_t rs = row_stride * elt, ls = input_layer_stride * elt, ps = pool_layer_stride * elt;
+  auto aligned = [](uintptr_t x, int a) { return (x % a) == 0; };
+  int vec = 2;
+  for (int a : {16, 4}) {
+    if (aligned((uintptr_t)append_key, a) && aligned((uintptr_t)append_value, a) &&
+        aligned((uintptr_t)paged_kv_cache, a) && rs % a == 0 && ls % a == 0 && ps % a == 0 &&
+        row_bytes % a == 0) {
+      vec = a;
+      break;
+    }
+  }
+  const int64_t chunks = (int64_t)num_layers * nnz * 2 * num_kv_heads * (row_bytes / vec);
+  const int threads = 256;
+  const int64_t want = (chunks + threads - 1) / threads;
+  const int blocks = (int)(want < 148 * 16 ? want : 148 * 16);
+  cudaStream_t st = (cudaStream_t)stream;
+  auto* k = (const char*)append_key;
+  auto* v = (const char*)append_value;
+  auto* pool = (char*)paged_kv_cache;
+  if (vec == 16)
+    append_kernel<16><<<blocks, threads, 0, st>>>(k, v, rs, ls, batch_indices, positions, kv_indices,
+                                                  kv_indptr, nnz, pool, ps, num_layers, num_pages,
+                                                  page_size, num_kv_heads, row_bytes, chunks);
+  else if (vec == 4)
+    append_kernel<4><<<blocks, threads, 0, st>>>(k, v, rs, ls, batch_indices, positions, kv_indices,
+                                                 kv_indptr, nnz, pool, ps, num_layers, num_pages,
+                                                 page_size, num_kv_heads, row_bytes, chunks);
+  else
+    append_kernel<2><<<blocks, threads, 0, st>>>(k, v, rs, ls, batch_indices, positions, kv_indices,
+                                                 kv_indptr, nnz, pool, ps, num_layers, num_pages,
+                                                 page_size, num_kv_heads, row_bytes, chunks);
+  BE_LAUNCH_CHECK();
+  return BE_OK;
+}
+
+extern "C" int be_fork_tail_copy(void* paged_kv_cache, int64_t pool_layer_stride, int num_layers,
+                                 int num_pages, int page_size, int num_kv_heads, int head_dim,
+                                 int dtype, const int32_t* src_pages, const int32_t* dst_pages,
+                                 const int32_t* lens, int num_copies, void* stream) {
+  if (num_copies < 0 || num_layers < 1 || page_size < 1 || num_kv_heads < 1 || head_dim < 1 ||
+      dtype < BE_F32 || dtype > BE_BF16) {
+    set_error("be_fork_tail_copy: invalid shape or dtype");
+    return BE_EINVAL;
+  }
+  if (num_copies == 0) return BE_OK;
+  const int elt = dtype_size(dtype);
+  const int64_t tok_bytes = (int64_t)num_kv_heads * head_dim * elt;
+  if (tok_bytes % 16 || ((uintptr_t)paged_kv_cache % 16) || (pool_layer_stride * elt) % 16) {
+    set_error("be_fork_tail_copy: pool rows must be 16-byte aligned (kv_heads*head_dim*elt %% 16)");
+    return BE_EINVAL;
+  }
+  const int64_t segs = (int64_t)num_copies * num_layers * 2;
+  if (segs > 65535) {
+    set_error("be_fork_tail_copy: too many copies x layers (%lld segments)", (long long)segs);
+    return BE_EINVAL;
+  }
+  const int64_t max16 = (page_size * tok_bytes) >> 4;
+  const int threads = 256;
+  int bx = (int)((max16 + threads * 2 - 1) / (threads * 2));
+  if (bx < 1) bx = 1;
+  dim3 grid(bx, (unsigned)segs);
+  fork_kernel<<<grid, threads, 0, (cudaStream_t)stream>>>(
+      (char*)paged_kv_cache, pool_layer_stride * elt, num_layers, num_pages, page_size * tok_bytes,
+      src_pages, dst_pages, lens, tok_bytes);
+  BE_LAUNCH_CHECK();
+  return BE_OK;
+}
+
+extern "C" int be_device_status(int* out, void* stream) {
+  BE_CUDA_CHECK(cudaMemcpyFromSymbolAsync(out, g_device_status, sizeof(int), 0,
+                                          cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  BE_CUDA_CHECK(cudaStreamSynchronize((cudaStream_t)stream));
+  return BE_OK;
+}
+
+extern "C" int be_device_status_clear(void* stream) {
+  static const int zero = 0;
+  BE_CUDA_CHECK(cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(int), 0,
+                                        cudaMemcpyHostToDevice, (cudaStream_t)stream));
+  return BE_OK;
+}

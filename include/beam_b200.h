@@ -1,0 +1,249 @@
+/* beam_b200.h -- C ABI of the B200 beam-decode path.
+ *
+ * Plain pointers and sizes only.  Device pointers are CUDA global-memory
+ * addresses on the current device; `stream` is a cudaStream_t passed as
+ * void* (NULL = legacy default stream).  Every call returns a be_status;
+ * be_last_error() gives the text of the last failure on the calling thread.
+ * Kernels never trap: an out-of-range page id or slot found on the device is
+ * skipped and recorded in a device status word (be_device_status()).
+ *
+ * Each entry point cites the reference interface it replaces
+ * (brian030128/beam_engine, paths relative to the project root).
+ */
+#ifndef BEAM_B200_H
+#define BEAM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  BE_OK = 0,
+  BE_EINVAL = 1,           /* bad argument (-> ValueError)                      */
+  BE_ENOMEM = 2,           /* page pool exhausted (-> MemoryError, page_table.py:87-88) */
+  BE_ECUDA = 3,            /* CUDA runtime error                               */
+  BE_ENOT_ALLOCATED = 4,   /* free of a page that is not allocated (a warning, page_table.py:117-119) */
+  BE_ECAPACITY = 5,        /* caller buffer too small; required size reported   */
+  BE_EDEVICE_RANGE = 6     /* device status: an index was out of range and skipped */
+} be_status;
+
+typedef enum { BE_F32 = 0, BE_F16 = 1, BE_BF16 = 2 } be_dtype;
+
+const char* be_last_error(void);
+int be_version(void);
+
+/* Device status word (per device).  be_device_status copies it to *out
+ * (synchronous on `stream`), be_device_status_clear resets it to 0.        */
+int be_device_status(int* out, void* stream);
+int be_device_status_clear(void* stream);
+
+/* ------------------------------------------------------------------------
+ * Paged KV pool layout: per layer [num_pages, 2, page_size, num_kv_heads,
+ * head_dim] (plane 0 = K, plane 1 = V), the reference's NHD pool
+ * (src/beam_engine/page_table.py:62-72).  Several layers may be addressed in
+ * one call through `pool_layer_stride` (elements between consecutive layers'
+ * pools; the reference keeps one tensor per layer).
+ * ---------------------------------------------------------------------- */
+
+/* Replaces flashinfer.page.append_paged_kv_cache as called by
+ * PageTable.write_blocks_vectorized (src/beam_engine/page_table.py:199-209).
+ * Entry i (0 <= i < nnz) writes key/value row i into page
+ * kv_indices[kv_indptr[batch_indices[i]] + positions[i] / page_size] at in-page
+ * slot positions[i] % page_size, for layers 0..num_layers-1.
+ * append_key/append_value: [num_layers][nnz][num_kv_heads][head_dim] with
+ * `row_stride` elements between rows i and i+1 (head/dim contiguous) and
+ * `input_layer_stride` elements between layers (so K/V can be read in place
+ * from a fused QKV projection output).                                        */
+int be_append_paged_kv(const void* append_key, const void* append_value, int64_t row_stride,
+                       int64_t input_layer_stride, const int32_t* batch_indices,
+                       const int32_t* positions, const int32_t* kv_indices, const int32_t* kv_indptr,
+                       int nnz, void* paged_kv_cache, int64_t pool_layer_stride, int num_layers,
+                       int num_pages, int page_size, int num_kv_heads, int head_dim, int dtype,
+                       void* stream);
+
+/* Copy-on-write fork of partially filled tail pages, all layers in one launch.
+ * Replaces the per-layer copy loop of PageTable.copy_block
+ * (src/beam_engine/page_table.py:96-106) issued by BeamState.add_filtered_results
+ * (src/beam_engine/beam_state.py:190-191).  Copy j moves tokens [0, lens[j]) of K
+ * and V from page src_pages[j] to page dst_pages[j] in every layer.  Copies must
+ * not read a page another copy of the same call writes (true for one fork step:
+ * sources are live leaves, destinations fresh pages).                         */
+int be_fork_tail_copy(void* paged_kv_cache, int64_t pool_layer_stride, int num_layers,
+                      int num_pages, int page_size, int num_kv_heads, int head_dim, int dtype,
+                      const int32_t* src_pages, const int32_t* dst_pages, const int32_t* lens,
+                      int num_copies, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Paged attention plans.  A plan is a flat int32 buffer built on the host by
+ * be_cascade_plan / be_tree_plan, copied to the device by the caller, and run
+ * by be_attn_run.  It lists work items, each "some queries of one group x a
+ * token range of that group's KV", plus the per-query list of partial states
+ * that be_attn_run merges by log-sum-exp.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t q_off;     /* first entry in the query list                          */
+  int32_t q_len;     /* number of queries (rows = q_len * group size)          */
+  int32_t kv_off;    /* first entry in the KV list (page ids or slot ids)      */
+  int32_t kv_begin;  /* token range [kv_begin, kv_end) of the group's sequence */
+  int32_t kv_end;
+  int32_t kv_total;  /* group's full KV length (causal alignment)              */
+  int32_t part_base; /* partial row of query 0 (>= 0) or -1: write output directly */
+  int32_t flags;     /* BE_WORK_CAUSAL | BE_WORK_SLOTS                         */
+} be_attn_work;
+
+#define BE_WORK_CAUSAL 1 /* query i sees tokens t < kv_total - q_len + i + 1 */
+#define BE_WORK_SLOTS 2  /* KV list holds slot ids (page*page_size+i), else page ids */
+
+typedef struct {
+  int32_t n_work;        /* work items                                         */
+  int32_t n_work_wide;   /* leading items whose rows exceed 16 (wide tiles)    */
+  int32_t n_queries;     /* rows of q / out                                    */
+  int32_t n_parts;       /* partial states (rows of mid_o / mid_lse)           */
+  int32_t n_merge;       /* queries with >= 1 partial (merged by be_attn_run)  */
+  int32_t off_work;      /* int32 offsets into the plan buffer                 */
+  int32_t off_qlist;
+  int32_t off_kvlist;
+  int32_t off_merge_q;   /* [n_merge] query ids                                */
+  int32_t off_merge_ptr; /* [n_merge + 1] CSR into merge_parts                 */
+  int32_t off_merge_parts;
+  int32_t total_ints;    /* ints to copy to the device                         */
+  int32_t page_size;
+  int32_t group_size;    /* num_qo_heads / num_kv_heads                        */
+} be_attn_plan_info;
+
+/* Plans MultiLevelCascadeAttentionWrapper.plan + .run
+ * (src/beam_engine/models/modeling_llama.py:733-755, :362; FlashInfer
+ * cascade semantics: level l group g owns queries qo_indptr[l][g]..[g+1] and
+ * pages kv_indices[l][kv_indptr[l][g]..[g+1]], kv_len =
+ * (npages-1)*page_size + last_page_len[l][g]; only the last level is causal
+ * when causal_last != 0; levels merged by LSE).  Arrays are host int32.
+ * split_tokens = 0 picks the KV split per group from num_sms; > 0 forces it
+ * (rounded to pages).  On BE_ECAPACITY info->total_ints holds the size needed. */
+int be_cascade_plan(int num_levels, const int32_t* const* qo_indptr,
+                    const int32_t* const* kv_indptr, const int32_t* const* kv_indices,
+                    const int32_t* const* last_page_len, const int32_t* num_groups,
+                    int num_queries, int page_size, int num_qo_heads, int num_kv_heads,
+                    int causal_last, int split_tokens, int num_sms, int32_t* plan,
+                    int64_t plan_capacity, be_attn_plan_info* info);
+
+/* Plans fasttree_decode (src/beam_engine/attention/fasttree/kernel.py:288-348)
+ * from the vnode metadata of prepare_fasttree_metadata_for_paged_cache
+ * (attention/fasttree/preparation.py:11-225): vnode v attends queries
+ * q_entries[q_offs[v] .. +q_lens[v]] to slots kv_entries[kv_offs[v] .. +kv_lens[v]];
+ * request b merges the partial rows req_to_vnode_entries[r2v_offs[b] .. +r2v_lens[b]].
+ * The KV entries themselves stay in the caller's device buffer (kv_entries_dev
+ * is passed to be_attn_run as kv_list_override).                              */
+int be_tree_plan(int num_vnodes, const int32_t* q_entries, int num_q_entries,
+                 const int32_t* q_offs, const int32_t* q_lens, const int32_t* kv_offs,
+                 const int32_t* kv_lens, const int32_t* r2v_entries, const int32_t* r2v_offs,
+                 const int32_t* r2v_lens, int batch_size, int page_size, int num_qo_heads,
+                 int num_kv_heads, int32_t* plan, int64_t plan_capacity, be_attn_plan_info* info);
+
+/* Runs a plan for one layer.  q: [n_queries][num_qo_heads][head_dim] with
+ * q_row_stride elements between queries; paged_kv_cache: one layer's pool;
+ * out: [n_queries][num_qo_heads][head_dim] (out_row_stride); lse (nullable):
+ * [n_queries][num_qo_heads] float32, natural log.  mid_o / mid_lse: float32
+ * scratch of n_parts*num_qo_heads*head_dim and n_parts*num_qo_heads floats.
+ * kv_list_override (nullable): device int32 KV list used instead of the plan's.
+ * Queries that appear in no work item get out = 0, lse = -inf.               */
+int be_attn_run(const int32_t* plan_dev, const be_attn_plan_info* info, const void* q,
+                int64_t q_row_stride, const void* paged_kv_cache, int num_pages,
+                int num_qo_heads, int num_kv_heads, int head_dim, int dtype, float sm_scale,
+                void* out, int64_t out_row_stride, float* lse, float* mid_o, float* mid_lse,
+                const int32_t* kv_list_override, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Host page manager (no CUDA): FIFO page allocator + beam trie.  One
+ * be_trie backs one PageTable and the BeamState objects over it.
+ * Single-threaded, like the reference.
+ * ---------------------------------------------------------------------- */
+typedef struct be_trie be_trie;
+
+/* PageTable.__init__ free list (src/beam_engine/page_table.py:59-60).       */
+be_trie* be_trie_create(int page_size, int max_num_pages);
+void be_trie_destroy(be_trie* t);
+/* PageTable.allocate_block (page_table.py:77-94): pops the FRONT of the free
+ * list; BE_ENOMEM when empty.                                               */
+int be_alloc_page(be_trie* t, int32_t* page);
+/* PageTable.free_block (page_table.py:110-124): appends to the BACK;
+ * BE_ENOT_ALLOCATED (a warning, no state change) for a page not allocated.  */
+int be_free_page(be_trie* t, int32_t page);
+int be_num_free_pages(be_trie* t);
+int be_is_allocated(be_trie* t, int32_t page);
+/* Free list in FIFO order (up to cap entries); returns its length.          */
+int be_free_list(be_trie* t, int32_t* out, int cap);
+int64_t be_trie_warnings(be_trie* t);
+int be_trie_num_nodes(be_trie* t);
+
+/* TrieNode(tokens, page_id, parent) (src/beam_engine/beam_state.py:20-27);
+ * parent = -1 for a root.  Node ids are stable handles.                      */
+int be_node_new(be_trie* t, int32_t parent, int32_t page, const int32_t* tokens, int n,
+                int32_t* node_out);
+int be_node_info(be_trie* t, int32_t node, int32_t* parent, int32_t* page, int32_t* ntokens,
+                 int32_t* nchildren);
+int be_node_tokens(be_trie* t, int32_t node, int32_t* out, int cap);
+int be_node_children(be_trie* t, int32_t node, int32_t* out, int cap);
+int be_node_append_token(be_trie* t, int32_t node, int32_t token);
+/* Root-to-leaf token sequence (beam_state.py:667-671); returns its length.  */
+int64_t be_node_sequence(be_trie* t, int32_t leaf, int32_t* out, int64_t cap);
+
+/* BeamState.add_root_sequence (beam_state.py:76-98).                        */
+int be_beam_add_root(be_trie* t, const int32_t* tokens, int n, int32_t* leaf_out,
+                     int32_t* pages_out);
+/* BeamState.add_filtered_results (beam_state.py:101-209): frees dead branches,
+ * appends / allocates / forks.  Candidate i's children: child_tokens[child_ptr[i]
+ * .. child_ptr[i+1]).  new_leaf/new_child (index of the child, to carry its
+ * score) in the reference's new-candidate order; copy_src/dst/len: the
+ * copy-on-write tail copies (PageTable.copy_block calls, :190-191) to run with
+ * be_fork_tail_copy.  Output arrays need child_ptr[ncand] entries.          */
+int be_beam_update(be_trie* t, int ncand, const int32_t* cand_leaf, const int32_t* child_ptr,
+                   const int32_t* child_tokens, int32_t* new_leaf, int32_t* new_child,
+                   int32_t* n_new, int32_t* copy_src, int32_t* copy_dst, int32_t* copy_len,
+                   int32_t* n_copies);
+/* Decode inputs per candidate (src/beam_engine/beam.py:168-221): query token,
+ * append page, append slot (len(leaf)-1), RoPE position (seq len - 1).      */
+int be_beam_step_inputs(be_trie* t, int ncand, const int32_t* cand_leaf, int32_t* query_tok,
+                        int32_t* write_page, int32_t* write_pos, int32_t* position);
+/* BeamState.get_cascade_input (beam_state.py:211-412).  Returns the level count
+ * or -status.  Level l: groups level_group_ptr[l]..[l+1]; its qo/kv indptr at
+ * [level_group_ptr[l] + l, level_group_ptr[l+1] + l] (one leading 0 per level);
+ * last_page_len at [level_group_ptr[l], level_group_ptr[l+1]); pages
+ * kv_indices[level_page_ptr[l] .. level_page_ptr[l+1]).                       */
+int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_levels,
+                     int cap_groups, int cap_pages, int32_t* level_group_ptr,
+                     int32_t* level_page_ptr, int32_t* qo_indptr, int32_t* kv_indptr,
+                     int32_t* kv_indices, int32_t* last_page_len);
+/* BeamState._build_kv_tree_structure + _build_req_to_token
+ * (beam_state.py:414-564): BFS nodes, request lists, req_to_token slot table
+ * [ncand][max_len].  per_node != 0 stores each node's own length as seqlen
+ * (the reference stores the cumulative length).  req_to_token == NULL: sizes only. */
+int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node, int page_size,
+                  int cap_nodes, int32_t* num_nodes, int32_t* node_parent, int32_t* node_seqlen,
+                  int32_t* node_children, int32_t* req_ptr, int32_t* req_list,
+                  int64_t cap_req_list, int32_t* max_len, int32_t* req_to_token,
+                  int64_t cap_req_to_token);
+/* prepare_fasttree_metadata_for_paged_cache
+ * (src/beam_engine/attention/fasttree/preparation.py:11-225): cost model,
+ * vnodes, req->vnode lists, two-phase order.  counts = {vnodes, entries,
+ * phase-0 vnodes, phase-1 vnodes}.                                           */
+int be_fasttree_prepare(int num_nodes, const int32_t* node_parent, const int32_t* node_seqlen,
+                        const int32_t* node_children, const int32_t* req_ptr,
+                        const int32_t* req_list, int64_t req_to_token_stride, int batch_size,
+                        int num_qo_heads, int num_kv_heads, int cap_vnodes, int cap_entries,
+                        int32_t* q_entries, int32_t* q_offs, int32_t* q_lens, int32_t* kv_offs,
+                        int32_t* kv_lens, int32_t* r2v_entries, int32_t* r2v_offs,
+                        int32_t* r2v_lens, int32_t* counts);
+/* VanillaBeamSearchStrategy.select_candidates (src/beam_engine/beam_strategy.py:433-488).
+ * tokens/logps: [n][k] children in top-k order.  Outputs child_ptr [n+1],
+ * child_tokens / child_scores [<= beam_size].                                */
+int be_vanilla_select(int n, int k, const double* parent_scores, const int32_t* tokens,
+                      const double* logps, int beam_size, int32_t* child_ptr,
+                      int32_t* child_tokens, double* child_scores);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BEAM_B200_H */

@@ -1,0 +1,141 @@
+"""Native host page manager (C++ via the C ABI) against the reference fixtures.
+CPU only: allocation, trie forks, cascade / FastTree metadata, selection."""
+import re
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT, load_json
+from beam_engine_b200 import _lib
+from beam_engine_b200.beam_state import BeamCandidate, BeamState, TrieNode
+from beam_engine_b200.beam_strategy import vanilla_select_arrays
+from beam_engine_b200.fasttree import plan_vnodes
+from beam_engine_b200.page_table import PageTable
+
+
+def header_functions():
+    names = set()
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", fn)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(be_\w+)\s*\(", src))
+    return names
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.lib()
+    names = header_functions()
+    assert len(names) > 20
+    for n in sorted(names):
+        assert hasattr(lib, n), n
+    assert set(_lib.exported_symbols()) <= names | set()
+    assert lib.be_version() >= 1
+
+
+def cpu_table(ps, pages, layers=1):
+    return PageTable(layer_num=layers, page_size=ps, max_num_pages=pages, head_num=1, head_dim=8,
+                     device="cpu", store_dtype=torch.float32)
+
+
+def state_from_spec(spec, ps):
+    nodes, cands = spec
+    made = []
+    for n in nodes:
+        par = made[n["parent"]] if n["parent"] >= 0 else None
+        made.append(TrieNode(tokens=n["tokens"], page_id=n["page"], parent=par))
+    bs = BeamState(len(cands), cpu_table(ps, 4))
+    bs.candidates = [BeamCandidate(trie_node=made[c], score=0.0) for c in cands]
+    return bs
+
+
+def levels_as_lists(levels):
+    return [{k: [int(x) for x in v] for k, v in lv.items()} for lv in levels]
+
+
+@pytest.mark.parametrize("name", ["example", "swapped", "uneven"])
+def test_cascade_known_answers_native(cascade_trees, name):
+    t = cascade_trees[name]
+    bs = state_from_spec((t["nodes"], t["candidates"]), t["page_size"])
+    out = bs.get_cascade_input()
+    qo, kvp, kvi, last, q = out[:5]
+    got = [dict(qo_indptr=a.tolist(), kv_indptr=b.tolist(), kv_indices=c.tolist(),
+                kv_last_page_len=d.tolist()) for a, b, c, d in zip(qo, kvp, kvi, last)]
+    assert got == t["expect"]["levels"]
+    assert q.tolist() == t["expect"]["query"]
+
+
+@pytest.mark.parametrize("case", ["ps4_w4", "ps16_w8", "ps8_w6_churn", "ps16_w16"])
+def test_trajectory_native(trajectories, case):
+    rec = trajectories[case]
+    cs = rec["case"]
+    pt = cpu_table(cs["ps"], cs["pages"])
+    bs = BeamState(cs["W"], pt)
+    bs.add_root_sequence(rec["prompt"])
+    toks, sc = rec["root_children"]
+    bs.update_native(bs.leaves, np.array([0, len(toks)]), np.array(toks), np.array(sc))
+    for step in rec["steps"]:
+        assert levels_as_lists(bs.cascade_levels()) == step["cascade"]["levels"]
+        q, wp, wpos, pos = bs.step_inputs()
+        assert q.tolist() == step["cascade"]["query"]
+        assert (wp.tolist(), wpos.tolist()) == (step["write_pages"], step["write_pos"])
+        par, seql, kids, rptr, rl, r2t = bs.tree_arrays(per_node=False)
+        tree = [dict(parent=int(par[i]), id=i, seqlen=int(seql[i]), num_children=int(kids[i]),
+                     requests=rl[rptr[i]:rptr[i + 1]].tolist()) for i in range(len(par))]
+        assert tree == step["tree"]
+        assert r2t.tolist() == step["req_to_token"]
+        B = len(bs.leaves)
+        for key, per_node in (("ft_cumulative", False), ("ft_per_node", True)):
+            p2, s2, k2, rp2, rl2, _ = bs.tree_arrays(per_node=per_node)
+            v = plan_vnodes(p2, s2, k2, rp2, np.ascontiguousarray(rl2) if len(rl2) else np.zeros(1, np.int32),
+                            r2t.shape[1], B, cs["hq"], cs["hkv"])
+            for k, exp in step[key].items():
+                assert [int(x) for x in v[k]] == exp, (key, k)
+        kid_t = np.array([c[0] for c in step["children"]], np.int32)
+        kid_l = np.array([c[1] for c in step["children"]], np.float64)
+        ptr, ct, csc = vanilla_select_arrays(bs.scores, kid_t, kid_l, cs["W"])
+        sel = [[[int(ct[j]), float(csc[j])] for j in range(ptr[i], ptr[i + 1])] for i in range(B)]
+        assert sel == step["selected"]
+        bs.update_native(bs.leaves, ptr, ct, csc)
+        copies = [list(map(int, c)) for c in zip(*bs.last_copies)]
+        assert copies == step["copies"]
+        assert pt.free_pages == step["free_after"]
+    final = bs.get_final_sequences(cs["W"], 1.0)
+    assert [[s, x] for s, x in final] == rec["final"]
+
+
+def test_allocator_errors_and_warnings():
+    pt = cpu_table(4, 3)
+    pages = [pt.allocate_block() for _ in range(3)]
+    assert pages == [0, 1, 2]
+    with pytest.raises(MemoryError):
+        pt.allocate_block()
+    pt.free_block(1)
+    pt.free_block(1)          # double free: warning, no change
+    assert pt.free_pages == [1]
+    assert _lib.lib().be_trie_warnings(pt._trie) == 1
+    pt.free_block(0)
+    assert pt.free_pages == [1, 0]
+    assert pt.allocate_block() == 1
+
+
+def test_object_api_select_and_update():
+    """The reference-style object API (BeamGenerateInput/Result) end to end."""
+    from beam_engine_b200.beam_state import BeamGenerateInput, BeamTokenCandidate
+    from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy
+    pt = cpu_table(4, 32)
+    bs = BeamState(2, pt)
+    bs.add_root_sequence([1, 2, 3, 4, 5, 6])
+    st = VanillaBeamSearchStrategy()
+    inputs = [BeamGenerateInput(bs.candidates[0], [BeamTokenCandidate(7, -0.1),
+                                                   BeamTokenCandidate(8, -0.2),
+                                                   BeamTokenCandidate(9, -0.3)])]
+    res = st.select_candidates(bs, inputs, 0)
+    assert [(c.token_id, c.accumulated_score) for c in res[0].children] == [(7, -0.1), (8, -0.2)]
+    bs.add_filtered_results(res)
+    # partial tail page [5, 6] forked: copy for child 2 first, child 1 appends in place
+    assert [c.trie_node.tokens for c in bs.candidates] == [[5, 6, 8], [5, 6, 7]]
+    assert [list(map(int, c)) for c in zip(*bs.last_copies)] == [[1, 2, 2]]
+    assert bs.candidates[0].trie_node.parent == bs.candidates[1].trie_node.parent
