@@ -43,6 +43,10 @@ _SIGS = {
                                C.c_int, C.c_int, C.c_int, P32, i64, C.POINTER(AttnPlanInfo)]),
     "be_attn_run": (C.c_int, [vp, C.POINTER(AttnPlanInfo), vp, i64, vp, C.c_int, C.c_int, C.c_int,
                               C.c_int, C.c_int, f32, vp, i64, vp, vp, vp, vp, vp]),
+    "be_add_rmsnorm": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, f32, C.c_int, vp]),
+    "be_rope_qkv_append": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp,
+                                     C.c_int, C.c_int, vp, vp, C.c_int, C.c_int, vp]),
+    "be_silu_mul": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
     # host page manager
     "be_trie_create": (vp, [C.c_int, C.c_int]),
     "be_trie_destroy": (None, [vp]),

@@ -1,0 +1,284 @@
+"""BeamSearchGenerator: the reference's engine loop (src/beam_engine/beam.py:17-352)
+on the B200 path.
+
+Same constructor and ``generate`` signature as the reference.  One decode step:
+  host (C++): cascade levels of the trie -> work-item plan; decode inputs
+  device: one forward over all beams (fused RoPE/append, paged attention,
+          cuBLAS GEMMs), log-softmax + top-2W per beam
+  host (C++): global top-W per prompt, trie update; device: ONE batched
+          copy-on-write kernel for every fork of the step (all layers).
+Per step there is one H2D copy of the step's metadata + plan and one D2H copy
+of the [beams, 2W] top-k (the reference makes W*2W ``.item()`` syncs).
+``generate_ids`` runs several prompts at once (each with its own W beams) in
+the same forward; the trie holds one root chain per prompt.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import logging
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+from .beam_state import BeamState
+from .cascade import _Plan
+from .page_table import PageTable, stream_ptr
+
+logger = logging.getLogger(__name__)
+
+
+def _i32(a):
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+class PlannedAttention:
+    """Paged attention for every layer of one forward, from one plan."""
+
+    def __init__(self, model, page_table, workspace):
+        self.m = model
+        self.pt = page_table
+        self.plan = _Plan(workspace)
+        self.scale = model.D ** -0.5
+        self.kv_list = None
+        self.timer = None          # optional (start_event, end_event) list collector
+
+    def plan_levels(self, levels, num_queries, causal=True, split_tokens=0):
+        L = len(levels)
+        arrs = [[_i32(lv[k]) for lv in levels] for k in
+                ("qo_indptr", "kv_indptr", "kv_indices", "kv_last_page_len")]
+        ng = _i32([len(a) - 1 for a in arrs[0]])
+        ptrs = [(_lib.P32 * max(L, 1))(*[_lib.ptr32(a) for a in grp]) for grp in arrs]
+        m, ps, p = self.m, self.pt.page_size, self.plan
+
+        def fn(buf, cap, info):
+            return lib().be_cascade_plan(L, *ptrs, _lib.ptr32(ng), num_queries, ps, m.Hq, m.Hkv,
+                                         1 if causal else 0, split_tokens, p.num_sms,
+                                         C.cast(buf, _lib.P32), cap, info)
+        p.build(fn)
+        p.place(m.Hq, m.D)
+        self.kv_list = None
+
+    def plan_tree(self, vnodes, batch_size, kv_entries_dev):
+        from .fasttree import build_tree_plan
+        info, buf = build_tree_plan(vnodes, batch_size, self.pt.page_size, self.m.Hq, self.m.Hkv)
+        p = self.plan
+        p.info = info
+        host = torch.from_numpy(buf)
+        if p.host.numel() < host.numel():
+            p.host = torch.empty(host.numel(), dtype=torch.int32).pin_memory()
+        if p.copied is not None:
+            p.copied.synchronize()
+        p.host[:host.numel()].copy_(host)
+        p.place(self.m.Hq, self.m.D)
+        self.kv_list = kv_entries_dev
+
+    def run(self, layer, qkv, out):
+        m = self.m
+        t = self.timer
+        if t is not None:
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+        rc = lib().be_attn_run(
+            C.c_void_p(self.plan.plan_dev), C.byref(self.plan.info), qkv.data_ptr(), qkv.stride(0),
+            self.pt.kv_cache[layer].data_ptr(), self.pt.max_num_pages, m.Hq, m.Hkv, m.D,
+            m.dt, self.scale, out.data_ptr(), out.stride(0), None,
+            C.c_void_p(self.plan.mid_o), C.c_void_p(self.plan.mid_lse),
+            self.kv_list.data_ptr() if self.kv_list is not None else None, stream_ptr(qkv.device))
+        check(rc, "be_attn_run")
+        if t is not None:
+            e.record()
+            t.append((s, e))
+
+
+class BeamSearchGenerator:
+    """beam.py:17-352.  ``model`` is a :class:`BeamLlama`."""
+
+    def __init__(self, model, tokenizer, strategy, page_size: int = 8, kernel_type: str = "cascade",
+                 max_num_pages: int = 1024, store_dtype: Optional[torch.dtype] = None,
+                 workspace_bytes: int = 128 << 20):
+        if kernel_type not in ("cascade", "fasttree"):
+            raise ValueError(f"Unknown kernel_type: {kernel_type}. Must be 'cascade' or 'fasttree'.")
+        self.model = model
+        self.tokenizer = tokenizer
+        self.strategy = strategy
+        self.device = model.device
+        self.page_size = page_size
+        self.kernel_type = kernel_type
+        c = model.config
+        self.page_table = PageTable(layer_num=c["num_hidden_layers"], page_size=page_size,
+                                    max_num_pages=max_num_pages, head_num=model.Hkv,
+                                    head_dim=model.D, device=self.device,
+                                    store_dtype=store_dtype or model.dtype)
+        self.workspace = torch.empty(workspace_bytes, dtype=torch.uint8, device=self.device)
+        self.attn = PlannedAttention(model, self.page_table, self.workspace)
+        self.meta_host = torch.empty(0, dtype=torch.int32).pin_memory()
+        self.topk_host = None
+        self.step_timer = None
+
+    # ------------------------------------------------------------------
+    def generate(self, input_text: str, beam_size: int = 4, max_length: int = 50,
+                 num_return_sequences: int = 1, temperature: float = 1.0,
+                 pad_token_id: Optional[int] = None, eos_token_id: Optional[int] = None) -> List[str]:
+        inputs = self.tokenizer(input_text, return_tensors="pt")
+        ids = inputs.input_ids[0].tolist()
+        final = self.generate_ids([ids], beam_size, max_length=max_length,
+                                  num_return_sequences=num_return_sequences,
+                                  temperature=temperature)[0]
+        return [self.tokenizer.decode(t, skip_special_tokens=True) for t, _ in final]
+
+    def _to_device(self, arrays: Sequence[np.ndarray]):
+        """One pinned staging buffer, one H2D copy -> list of int32 device views."""
+        n = sum(len(a) for a in arrays)
+        if self.meta_host.numel() < n:
+            self.meta_host = torch.empty(max(n, 1024) * 2, dtype=torch.int32).pin_memory()
+        if getattr(self, "_meta_ev", None) is not None:
+            self._meta_ev.synchronize()
+        hv = self.meta_host.numpy()
+        off = 0
+        for a in arrays:
+            hv[off:off + len(a)] = a
+            off += len(a)
+        dev = torch.empty(n, dtype=torch.int32, device=self.device)
+        dev.copy_(self.meta_host[:n], non_blocking=True)
+        self._meta_ev = torch.cuda.Event()
+        self._meta_ev.record()
+        out, off = [], 0
+        for a in arrays:
+            out.append(dev[off:off + len(a)])
+            off += len(a)
+        return out
+
+    def _topk(self, logits, k, temperature):
+        if temperature != 1.0:
+            logits = logits / temperature
+        lp = torch.log_softmax(logits, dim=-1)
+        vals, idx = torch.topk(lp, k, dim=-1)
+        n = vals.shape[0]
+        if self.topk_host is None or self.topk_host[0].shape[0] < n * k:
+            self.topk_host = (torch.empty(n * k * 2, dtype=torch.float32).pin_memory(),
+                              torch.empty(n * k * 2, dtype=torch.int64).pin_memory())
+        hv, hi = self.topk_host
+        hv[:n * k].copy_(vals.reshape(-1), non_blocking=True)
+        hi[:n * k].copy_(idx.reshape(-1), non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return (hv[:n * k].numpy().reshape(n, k).astype(np.float64),
+                hi[:n * k].numpy().reshape(n, k).astype(np.int32))
+
+    def prefill(self, state: BeamState, prompts: List[List[int]]):
+        """Allocate each prompt's pages, run the causal prompt forward, return the
+        last-position logits of each prompt [P, vocab]."""
+        ps = self.page_table.page_size
+        pages_all, qo, kvp, last = [], [0], [0], []
+        ids, pos, wpage, wpos = [], [], [], []
+        for pr in prompts:
+            chain = state.add_root_sequence(pr)
+            pages = [n.page_id for n in chain]
+            pages_all.extend(pages)
+            kvp.append(kvp[-1] + len(pages))
+            last.append(len(chain[-1].tokens))
+            qo.append(qo[-1] + len(pr))
+            ids.extend(pr)
+            pos.extend(range(len(pr)))
+            for i in range(len(pr)):
+                wpage.append(pages[i // ps])
+                wpos.append(i % ps)
+        rows = np.asarray(qo[1:], np.int32) - 1
+        d_ids, d_pos, d_wp, d_wpos, d_rows = self._to_device(
+            [_i32(ids), _i32(pos), _i32(wpage), _i32(wpos), rows])
+        self.attn.plan_levels([dict(qo_indptr=qo, kv_indptr=kvp, kv_indices=pages_all,
+                                    kv_last_page_len=last)], len(ids), causal=True)
+        logits = self.model.forward(d_ids.long(), d_pos, self.page_table, d_wp, d_wpos, self.attn,
+                                    logits_rows=d_rows.long())
+        return logits
+
+    def decode_step(self, state: BeamState):
+        """One beam step's forward: returns logits [beams, vocab]."""
+        q, wp, wpos, pos = state.step_inputs()
+        if self.kernel_type == "cascade":
+            levels = state.cascade_levels()
+            self.attn.plan_levels(levels, len(q), causal=True)
+        else:
+            from .fasttree import plan_vnodes
+            par, seql, kids, rptr, rl, r2t = state.tree_arrays(per_node=True)
+            v = plan_vnodes(par, seql, kids, rptr, np.ascontiguousarray(rl) if len(rl) else
+                            np.zeros(1, np.int32), r2t.shape[1], len(q), self.model.Hq_total,
+                            self.model.Hkv_total)
+            flat = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)])
+        arrays = [q, pos, wp, wpos]
+        if self.kernel_type != "cascade":
+            arrays.append(_i32(flat))
+        dev = self._to_device(arrays)
+        if self.kernel_type != "cascade":
+            self.attn.plan_tree(v, len(q), dev[4])
+        return self.model.forward(dev[0].long(), dev[1], self.page_table, dev[2], dev[3], self.attn)
+
+    def generate_ids(self, prompts: List[List[int]], beam_size: int = 4,
+                     max_length: Optional[int] = None, max_new_tokens: Optional[int] = None,
+                     num_return_sequences: int = 1, temperature: float = 1.0):
+        """Beam search over several prompts at once.  ``max_length`` is per-prompt
+        total length as in the reference (new tokens = max_length - len(prompt));
+        ``max_new_tokens`` sets the same for every prompt.  Returns, per prompt,
+        the ranked [(tokens, score)] list."""
+        if max_new_tokens is None:
+            if max_length is None:
+                raise ValueError("give max_length or max_new_tokens")
+            steps_left = [max_length - len(p) - 1 for p in prompts]
+            if len(set(steps_left)) != 1:
+                raise ValueError("prompts of different lengths need max_new_tokens")
+            n_steps = steps_left[0]
+        else:
+            n_steps = max_new_tokens - 1
+        W = beam_size
+        state = BeamState(W, self.page_table)
+        state.defer_copies = True
+        V = self.model.vocab
+        with torch.no_grad():
+            logits = self.prefill(state, prompts)
+            k0 = min(2 * W, V)
+            vals, idx = self._topk(logits, k0, temperature)
+            kw = min(W, k0)
+            ptr = np.arange(len(prompts) + 1, dtype=np.int32) * kw
+            self._apply(state, ptr, idx[:, :kw].reshape(-1), vals[:, :kw].reshape(-1))
+            seg = np.arange(len(prompts) + 1) * kw          # candidates per prompt
+            for step in range(n_steps):
+                if self.strategy.should_stop(state, 10 ** 9, step):
+                    break
+                logits = self.decode_step(state)
+                k = min(2 * W, V) if W != 1 else 1
+                vals, idx = self._topk(logits, k, temperature)
+                ptr_all, tok_all, sc_all = [0], [], []
+                new_seg = [0]
+                for p in range(len(prompts)):
+                    a, b = seg[p], seg[p + 1]
+                    cp, ct, cs = self.strategy.select_arrays(state.scores[a:b], idx[a:b], vals[a:b], W)
+                    ptr_all.extend((cp[1:] + len(tok_all)).tolist())
+                    tok_all.extend(ct.tolist())
+                    sc_all.extend(cs.tolist())
+                    new_seg.append(new_seg[-1] + int(cp[-1]))
+                self._apply(state, np.asarray(ptr_all, np.int32), np.asarray(tok_all, np.int32),
+                            np.asarray(sc_all, np.float64))
+                seg = np.asarray(new_seg)
+        out = []
+        for p in range(len(prompts)):
+            sub = BeamState(W, self.page_table)
+            sub.set_state(state.leaves[seg[p]:seg[p + 1]], state.scores[seg[p]:seg[p + 1]])
+            out.append(self.strategy.get_final_sequences(sub, num_return_sequences))
+        self.last_state = state
+        return out
+
+    def _apply(self, state, child_ptr, child_tokens, child_scores):
+        state.update_native(state.leaves, child_ptr, child_tokens, child_scores)
+        cs, cd, cl = state.last_copies
+        if len(cs):
+            d = self._to_device([cs, cd, cl])
+            pt = self.page_table
+            check(lib().be_fork_tail_copy(pt.kv_cache.data_ptr(), pt.kv_cache.stride(0),
+                                          pt.layer_num, pt.max_num_pages, pt.page_size,
+                                          pt.head_num, pt.head_dim,
+                                          _lib.BE_F32 if pt.store_dtype == torch.float32 else
+                                          (_lib.BE_BF16 if pt.store_dtype == torch.bfloat16 else _lib.BE_F16),
+                                          d[0].data_ptr(), d[1].data_ptr(), d[2].data_ptr(), len(cs),
+                                          stream_ptr(self.device)), "fork")

@@ -5,6 +5,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "beam_b200.h"
 
 namespace be {

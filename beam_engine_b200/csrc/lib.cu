@@ -3,3 +3,4 @@
 // instead of with relocatable device code.
 #include "page_ops.cu"
 #include "attention.cu"
+#include "model_ops.cu"

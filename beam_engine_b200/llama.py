@@ -1,0 +1,136 @@
+"""Llama decoder for beam decode on the paged KV cache (the reference's patched HF
+Llama, ``src/beam_engine/models/modeling_llama.py``), B200 layout.
+
+Per layer: fused residual-add + RMSNorm -> one QKV GEMM -> fused RoPE + K/V
+append into the pages -> paged attention (cascade / prefill / tree plan) ->
+O GEMM -> fused add + RMSNorm -> one gate|up GEMM -> SiLU*up -> down GEMM.
+GEMMs are cuBLAS (torch.mm on pre-fused weights); every other op is a kernel
+of ``libbeam_b200.so``.  Tensor parallelism (``tp``) shards q/k/v heads, the
+O-projection rows, gate/up columns and down rows, with one all-reduce after
+the O and down projections.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import torch
+
+from ._lib import check, lib
+from .page_table import dtype_code, stream_ptr
+from .weights import random_llama_weights
+
+
+def inv_freq_table(head_dim, theta, device):
+    """HF default RoPE inverse frequencies (float32), modeling_llama.py:89-110."""
+    return (1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+            ).to(device)
+
+
+class BeamLlama:
+    def __init__(self, cfg: dict, weights: Optional[dict] = None, dtype=torch.bfloat16,
+                 device="cuda", seed=0, tp=None):
+        self.config = dict(cfg)
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.tp = tp
+        ts, tr = (tp.size, tp.rank) if tp is not None else (1, 0)
+        c = self.config
+        self.L = c["num_hidden_layers"]
+        self.D = c["head_dim"]
+        self.Hq_total, self.Hkv_total = c["num_attention_heads"], c["num_key_value_heads"]
+        if self.Hq_total % ts or self.Hkv_total % ts or c["intermediate_size"] % ts:
+            raise ValueError(f"heads / ffn not divisible by tensor-parallel size {ts}")
+        self.Hq, self.Hkv = self.Hq_total // ts, self.Hkv_total // ts
+        self.F = c["intermediate_size"] // ts
+        self.H = c["hidden_size"]
+        self.eps = float(c["rms_norm_eps"])
+        self.vocab = c["vocab_size"]
+        if weights is None:
+            weights = random_llama_weights(c, seed=seed, dtype=dtype, device=self.device)
+        D, Hq, Hkv, F = self.D, self.Hq, self.Hkv, self.F
+
+        def shard_rows(w, n_per, idx):   # output-feature shard
+            return w[idx * n_per:(idx + 1) * n_per]
+
+        def prep(t):
+            return t.to(device=self.device, dtype=dtype).contiguous()
+
+        self.w_qkv, self.w_o, self.w_gu, self.w_down, self.n_in, self.n_post = [], [], [], [], [], []
+        for i in range(self.L):
+            p = f"layers.{i}."
+            q = shard_rows(weights[p + "q"], Hq * D, tr)
+            k = shard_rows(weights[p + "k"], Hkv * D, tr)
+            v = shard_rows(weights[p + "v"], Hkv * D, tr)
+            self.w_qkv.append(prep(torch.cat([q, k, v], 0)))
+            self.w_o.append(prep(weights[p + "o"][:, tr * Hq * D:(tr + 1) * Hq * D]))
+            g = shard_rows(weights[p + "gate"], F, tr)
+            u = shard_rows(weights[p + "up"], F, tr)
+            self.w_gu.append(prep(torch.cat([g, u], 0)))
+            self.w_down.append(prep(weights[p + "down"][:, tr * F:(tr + 1) * F]))
+            self.n_in.append(prep(weights[p + "input_norm"]))
+            self.n_post.append(prep(weights[p + "post_norm"]))
+        self.embed = prep(weights["embed"])
+        self.norm = prep(weights["norm"])
+        # vocab-parallel lm_head under TP (each rank scores its vocabulary slice)
+        V = self.vocab
+        self.v0, self.v1 = (tr * V) // ts, ((tr + 1) * V) // ts
+        self.lm_head = prep(weights["lm_head"][self.v0:self.v1])
+        self.inv_freq = inv_freq_table(D, float(c["rope_theta"]), self.device)
+        self.dt = dtype_code(dtype)
+        self.qkv_width = (Hq + 2 * Hkv) * D
+        del weights
+
+    def parameters(self):
+        yield self.embed
+
+    # ------------------------------------------------------------------
+    def forward(self, ids: torch.Tensor, positions: torch.Tensor, page_table, write_pages,
+                write_pos, attention, logits_rows: Optional[torch.Tensor] = None,
+                layer_hook=None) -> torch.Tensor:
+        """ids [n] (device), positions/write_pages/write_pos [n] int32 (device).
+        attention.run(layer, qkv, out) computes paged attention for one layer.
+        Returns logits [len(logits_rows) or n, vocab slice] in float32."""
+        n = ids.shape[0]
+        dev, dt = self.device, self.dtype
+        st = stream_ptr(dev)
+        L = lib()
+        x = self.embed.index_select(0, ids)                     # residual stream [n, H]
+        h = torch.empty_like(x)
+        qkv = torch.empty((n, self.qkv_width), dtype=dt, device=dev)
+        att = torch.empty((n, self.Hq * self.D), dtype=dt, device=dev)
+        gu = torch.empty((n, 2 * self.F), dtype=dt, device=dev)
+        act = torch.empty((n, self.F), dtype=dt, device=dev)
+        delta = torch.empty_like(x)
+        pool = page_table.kv_cache
+        P, ps = page_table.max_num_pages, page_table.page_size
+        have_delta = False
+        for i in range(self.L):
+            check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr() if have_delta else None,
+                                   self.n_in[i].data_ptr(), h.data_ptr(), n, self.H, self.eps,
+                                   self.dt, st), "add_rmsnorm")
+            torch.mm(h, self.w_qkv[i].t(), out=qkv)
+            check(L.be_rope_qkv_append(qkv.data_ptr(), self.qkv_width, n, self.Hq, self.Hkv, self.D,
+                                       positions.data_ptr(), self.inv_freq.data_ptr(),
+                                       pool[i].data_ptr(), P, ps, write_pages.data_ptr(),
+                                       write_pos.data_ptr(), 0, self.dt, st), "rope_append")
+            attention.run(i, qkv, att)
+            if layer_hook is not None:
+                layer_hook(i)
+            torch.mm(att, self.w_o[i].t(), out=delta)
+            self._all_reduce(delta)
+            check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.n_post[i].data_ptr(),
+                                   h.data_ptr(), n, self.H, self.eps, self.dt, st), "add_rmsnorm")
+            torch.mm(h, self.w_gu[i].t(), out=gu)
+            check(L.be_silu_mul(gu.data_ptr(), act.data_ptr(), n, self.F, self.dt, st), "silu_mul")
+            torch.mm(act, self.w_down[i].t(), out=delta)
+            self._all_reduce(delta)
+            have_delta = True
+        check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.norm.data_ptr(), h.data_ptr(),
+                               n, self.H, self.eps, self.dt, st), "final norm")
+        hs = h if logits_rows is None else h.index_select(0, logits_rows)
+        return torch.mm(hs, self.lm_head.t()).float()
+
+    def _all_reduce(self, t):
+        if self.tp is not None and self.tp.size > 1:
+            self.tp.all_reduce(t)

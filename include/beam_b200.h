@@ -156,6 +156,34 @@ int be_attn_run(const int32_t* plan_dev, const be_attn_plan_info* info, const vo
                 const int32_t* kv_list_override, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Decoder-layer kernels of the model runner (the reference runs these as
+ * separate PyTorch ops inside src/beam_engine/models/modeling_llama.py).
+ * ---------------------------------------------------------------------- */
+
+/* LlamaDecoderLayer residual add + LlamaRMSNorm (modeling_llama.py:68-86,
+ * 577-621) in one pass: residual += delta (delta may be NULL), then
+ * out = weight * cast(residual * rsqrt(mean(residual^2) + eps)).            */
+int be_add_rmsnorm(void* residual, const void* delta, const void* weight, void* out, int rows,
+                   int hidden, float eps, int dtype, void* stream);
+
+/* RoPE (HF rotate_half, modeling_llama.py:113-157) on the q and k heads of a
+ * fused QKV projection row [q heads | k heads | v heads] (row_stride elements
+ * apart), q rotated in place, rotated k and v appended into page
+ * write_page[i] slot write_pos[i] -- apply_rotary_pos_emb followed by
+ * PageTable.write_blocks_vectorized (modeling_llama.py:464-514) in one launch.
+ * inv_freq: [head_dim/2] float32 device array.  rope_k_in_place != 0 also
+ * leaves the rotated k in the QKV row.                                       */
+int be_rope_qkv_append(void* qkv, int64_t row_stride, int n, int num_qo_heads, int num_kv_heads,
+                       int head_dim, const int32_t* positions, const float* inv_freq,
+                       void* paged_kv_cache, int num_pages, int page_size,
+                       const int32_t* write_page, const int32_t* write_pos, int rope_k_in_place,
+                       int dtype, void* stream);
+
+/* LlamaMLP activation (modeling_llama.py:160-173): out = silu(gate) * up on a
+ * fused [n][2*ffn] gate|up projection.                                       */
+int be_silu_mul(const void* gate_up, void* out, int n, int ffn, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * Host page manager (no CUDA): FIFO page allocator + beam trie.  One
  * be_trie backs one PageTable and the BeamState objects over it.
  * Single-threaded, like the reference.
