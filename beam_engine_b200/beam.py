@@ -217,11 +217,12 @@ class BeamSearchGenerator:
 
     def generate_ids(self, prompts: List[List[int]], beam_size: int = 4,
                      max_length: Optional[int] = None, max_new_tokens: Optional[int] = None,
-                     num_return_sequences: int = 1, temperature: float = 1.0):
+                     num_return_sequences: int = 1, temperature: float = 1.0, on_step=None):
         """Beam search over several prompts at once.  ``max_length`` is per-prompt
         total length as in the reference (new tokens = max_length - len(prompt));
         ``max_new_tokens`` sets the same for every prompt.  Returns, per prompt,
-        the ranked [(tokens, score)] list."""
+        the ranked [(tokens, score)] list.  ``on_step(i)`` (optional) is called
+        before decode step i and once more with the step count after the last."""
         if max_new_tokens is None:
             if max_length is None:
                 raise ValueError("give max_length or max_new_tokens")
@@ -246,6 +247,8 @@ class BeamSearchGenerator:
             for step in range(n_steps):
                 if self.strategy.should_stop(state, 10 ** 9, step):
                     break
+                if on_step is not None:
+                    on_step(step)
                 logits = self.decode_step(state)
                 k = min(2 * W, V) if W != 1 else 1
                 vals, idx = self._topk(logits, k, temperature)
@@ -261,6 +264,8 @@ class BeamSearchGenerator:
                 self._apply(state, np.asarray(ptr_all, np.int32), np.asarray(tok_all, np.int32),
                             np.asarray(sc_all, np.float64))
                 seg = np.asarray(new_seg)
+            if on_step is not None:
+                on_step(n_steps)
         out = []
         for p in range(len(prompts)):
             sub = BeamState(W, self.page_table)

@@ -1,0 +1,402 @@
+"""Benchmark: beam decode tokens/s on the Llama-3-8B shape (W=16), with the
+paged-attention kernel's HBM roofline.
+
+Workload: random-init Llama-3-8B-shaped model in bf16,
+8 prompts x 1024 uniform-random token ids, beam width 16, 128 new tokens,
+page size 16.  A "step" is one beam decode step over all 8 x 16 beams
+(forward over 32 layers with cascade attention, log-softmax + top-2W,
+global top-W per prompt, trie update, copy-on-write forks).  ``--warmup W``
+decode steps run untimed after the prefill, then ``--steps K`` are timed with
+CUDA events (barrier + synchronize on both sides); W + K <= 127 (the 128th
+token comes from the prefill).  Every step streams the 15 GB of weights, far
+more than L2, so no flush is needed between steps.
+
+Multi-GPU (torchrun, one process per GPU): every rank decodes its own 8
+prompts (independent replicas, weak scaling, no collective on the data path);
+value = all ranks' beam tokens / max-over-ranks time.
+
+``--impl reference`` times the CPU restatement of the reference engine (the
+oracle; the reference's own GPU path needs FlashInfer 0.2.8, and its Python
+tree cannot travel to the GPU box) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "beam decode tokens/s, Llama-3-8B-shape W=16; paged attn HBM GB/s vs peak"
+PROMPTS, PROMPT_LEN, BEAM, NEW_TOKENS, PAGE = 8, 1024, 16, 128, 16
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except Exception:
+            self.p.kill()
+            out = ""
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def attn_plan_bytes(levels, hkv, d, hq, elt=2):
+    """Algorithmic bytes of one cascade attention launch: every group's K and V
+    read once (2 * kv_len * Hkv * D * elt) plus q in and o out."""
+    kv = 0
+    nq = 0
+    for lv in levels:
+        kvp, last, ps = lv["kv_indptr"], lv["kv_last_page_len"], PAGE
+        for g in range(len(kvp) - 1):
+            npg = int(kvp[g + 1] - kvp[g])
+            if npg:
+                kv += (npg - 1) * ps + int(last[g])
+        nq = int(lv["qo_indptr"][-1])
+    return kv * 2 * hkv * d * elt + 2 * nq * hq * d * elt
+
+
+def run_b200(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from beam_engine_b200.beam import BeamSearchGenerator
+    from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy
+    from beam_engine_b200.configs import LLAMA3_8B, param_count
+    from beam_engine_b200.llama import BeamLlama
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = dict(LLAMA3_8B)
+    model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=dev, seed=1234 + rank)
+    gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=PAGE,
+                              max_num_pages=args.pages)
+    g = torch.Generator().manual_seed(rank)
+    prompts = [torch.randint(0, cfg["vocab_size"], (PROMPT_LEN,), generator=g).tolist()
+               for _ in range(PROMPTS)]
+    W, K = args.warmup, args.steps
+    total_steps = NEW_TOKENS - 1
+    if W + K > total_steps:
+        raise SystemExit(f"warmup + steps must be <= {total_steps}")
+    ev = {}
+    clocks = Clocks(local_rank)
+    attn_events = []
+    launches = {"n": 0}
+    plan_bytes = []
+    plan_stats = []
+    orig_plan = gen.attn.plan_levels
+
+    def plan_hook(levels, nq, causal=True, split_tokens=0):
+        orig_plan(levels, nq, causal, split_tokens)
+        if gen.attn.timer is not None:
+            plan_bytes.append(attn_plan_bytes(levels, model.Hkv, model.D, model.Hq))
+            inf = gen.attn.plan.info
+            plan_stats.append((len(levels), inf.n_work, inf.n_work_wide, inf.n_parts, inf.n_merge))
+            n_merge = gen.attn.plan.info.n_merge
+            launches["n"] += cfg["num_hidden_layers"] * (4 + 1 + (1 if n_merge else 0)) + 1
+
+    gen.attn.plan_levels = plan_hook
+    orig_apply = gen._apply
+
+    def apply_hook(state, *a):
+        orig_apply(state, *a)
+        if gen.attn.timer is not None and len(state.last_copies[0]):
+            launches["n"] += 1
+
+    gen._apply = apply_hook
+
+    def on_step(i):
+        if i == W:
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            clocks.start()
+            ev["start"] = torch.cuda.Event(enable_timing=True)
+            ev["start"].record()
+            gen.attn.timer = attn_events
+        if i == W + K:
+            ev["end"] = torch.cuda.Event(enable_timing=True)
+            ev["end"].record()
+            torch.cuda.synchronize()
+            gen.attn.timer = None
+            if world > 1:
+                dist.barrier()
+            ev["clocks"] = clocks.stop()
+
+    # -- timed decode run (inputs resident: model, pages) ------------------
+    gen.generate_ids(prompts, BEAM, max_new_tokens=W + K + 1, on_step=on_step)
+    ms = ev["start"].elapsed_time(ev["end"])
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    tokens = PROMPTS * BEAM * K * world
+    value = tokens / (ms_max / 1e3)
+    # attention roofline: algorithmic bytes / launch duration, live events
+    attn_ms = [s.elapsed_time(e) for s, e in attn_events]
+    L = cfg["num_hidden_layers"]
+    bytes_total = sum(b * L for b in plan_bytes)
+    attn_total_ms = sum(attn_ms)
+    hbm, tflops, src = peaks()
+    achieved = bytes_total / (attn_total_ms / 1e3) / 1e9 if attn_total_ms else 0.0
+    step_bytes = (param_count(cfg) - cfg["vocab_size"] * cfg["hidden_size"]) * 2
+    if args.no_e2e:
+        return dict(value=value, ms_per_step=ms_max / K, attn_us=attn_total_ms / max(len(attn_ms), 1) * 1e3,
+                    achieved=achieved, plan_avg=[float(np.mean([p[i] for p in plan_stats])) for i in range(5)])
+    # -- end-to-end: the public API call from host token ids to host beams ----
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    gen2_t0 = torch.cuda.Event(enable_timing=True)
+    gen2_t1 = torch.cuda.Event(enable_timing=True)
+    h2d = {"b": 0}
+    orig_to_dev = gen._to_device
+
+    def count_h2d(arrays):
+        h2d["b"] += sum(len(a) for a in arrays) * 4
+        return orig_to_dev(arrays)
+
+    gen._to_device = count_h2d
+    gen2_t0.record()
+    t0 = time.perf_counter()
+    out = gen.generate_ids(prompts, BEAM, max_new_tokens=NEW_TOKENS)
+    gen2_t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = gen2_t0.elapsed_time(gen2_t1)
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    t = torch.tensor([e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    e2e_tokens = PROMPTS * BEAM * NEW_TOKENS * world
+    steps_e2e = NEW_TOKENS
+    d2h = PROMPTS * BEAM * 2 * BEAM * (4 + 8)   # top-2W values (f32) + ids (i64) per beam
+    assert len(out) == PROMPTS and all(len(o) == 1 for o in out)
+    res = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "beam tokens/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(ms_max / K, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded uniform token ids, random-init N(0,0.02) weights)",
+        "config": {"workload": "cfg3: Llama-3-8B shape, 8 prompts x 1024 tokens, beam width 16, "
+                               "128 new tokens, page size 16, cascade attention",
+                   "model": "Llama-3-8B-shape (random init)", "global_batch": PROMPTS * BEAM * world,
+                   "seq_len": PROMPT_LEN, "parallelism": f"replicas x{world}",
+                   "l2": "no flush needed: each step reads 15 GB of weights (> 126 MB L2)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "kernel": "be_attn_run (paged cascade attention + LSE merge), per layer",
+                     "peak_source": src,
+                     "avg_launch_us": round(attn_total_ms / max(len(attn_ms), 1) * 1e3, 2),
+                     "bytes_per_launch": round(bytes_total / max(len(attn_ms), 1)),
+                     "plan_avg": dict(zip(("levels", "work_items", "wide_items", "partial_rows",
+                                           "merged_queries"),
+                                          [round(float(np.mean([p[i] for p in plan_stats])), 1)
+                                           for i in range(5)])) if plan_stats else None},
+        "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs":
+                          round(step_bytes / (ms_max / K / 1e3) / 1e9, 1),
+                          "frac": round(step_bytes / (ms_max / K / 1e3) / 1e9 / hbm, 4)},
+        "e2e": {"value": round(e2e_tokens / (e2e_ms / 1e3), 2), "unit": "beam tokens/s",
+                "h2d_bytes_per_step": int(h2d["b"] / steps_e2e),
+                "d2h_bytes_per_step": d2h,
+                "includes": "prefill of 8 x 1024 prompt tokens + 127 decode steps, host ids in, "
+                            "host beams out", "wall_ms": round(wall_ms, 1)},
+        "gpu_launches": launches["n"],
+        "clocks": ev.get("clocks"),
+    }
+    return res
+
+
+def cpu_baseline_sample(threads=None, layers_timed=2):
+    """The oracle (CPU restatement of the reference engine) on a bounded sample
+    of one cfg3 decode step: `layers_timed` decoder layers over all 128 beams
+    (cascade attention over 8 x 1024-token prefixes + suffixes), the lm_head and
+    top-k / selection once; scaled to 32 layers."""
+    import numpy as np
+    import torch
+    from beam_engine_b200.configs import LLAMA3_8B
+    from oracle.attention import cascade_attention
+    from oracle.llama import rmsnorm, silu
+    n_threads = threads or os.cpu_count()
+    torch.set_num_threads(n_threads)
+    cfg = LLAMA3_8B
+    rng = np.random.default_rng(0)
+    H, F, D, Hq, Hkv, V = (cfg["hidden_size"], cfg["intermediate_size"], cfg["head_dim"],
+                           cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["vocab_size"])
+    N = PROMPTS * BEAM
+    # synthetic decode state: per prompt 64 prefix pages, per beam 1-4 suffix pages
+    P = PROMPTS * 64 + N * 4 + 8
+    pool = rng.standard_normal((P, 2, PAGE, Hkv, D), dtype=np.float32)
+    lv0 = dict(qo_indptr=[i * BEAM for i in range(PROMPTS + 1)],
+               kv_indptr=[i * 64 for i in range(PROMPTS + 1)],
+               kv_indices=list(range(PROMPTS * 64)), kv_last_page_len=[PAGE] * PROMPTS)
+    kvp, kvi, last, nxt = [0], [], [], PROMPTS * 64
+    for b in range(N):
+        n = 1 + b % 4
+        kvi += list(range(nxt, nxt + n))
+        nxt += n
+        kvp.append(len(kvi))
+        last.append(1 + b % PAGE)
+    lv1 = dict(qo_indptr=list(range(N + 1)), kv_indptr=kvp, kv_indices=kvi, kv_last_page_len=last)
+
+    def w(*s):
+        return (rng.standard_normal(s, dtype=np.float32) * 0.02)
+    wq, wk, wv, wo = w(Hq * D, H), w(Hkv * D, H), w(Hkv * D, H), w(H, Hq * D)
+    wg, wu, wd = w(F, H), w(F, H), w(H, F)
+    x = rng.standard_normal((N, H), dtype=np.float32)
+    ones = np.ones(H, np.float32)
+    t_layers = []
+    for _ in range(layers_timed):
+        t0 = time.perf_counter()
+        h = rmsnorm(x, ones, 1e-5)
+        q = (h @ wq.T).reshape(N, Hq, D)
+        _k = h @ wk.T
+        _v = h @ wv.T
+        a = cascade_attention(q, pool, [lv0, lv1], PAGE, D ** -0.5).astype(np.float32)
+        x2 = x + a.reshape(N, -1) @ wo.T
+        h = rmsnorm(x2, ones, 1e-5)
+        m = silu(h @ wg.T) * (h @ wu.T)
+        _ = x2 + m.astype(np.float32) @ wd.T
+        t_layers.append(time.perf_counter() - t0)
+    del wq, wk, wv, wo, wg, wu, wd
+    lm = w(V, H)
+    t0 = time.perf_counter()
+    logits = h @ lm.T
+    lp = logits - logits.max(-1, keepdims=True)
+    lp = lp - np.log(np.exp(lp).sum(-1, keepdims=True))
+    np.argpartition(-lp, 2 * BEAM, axis=-1)[:, :2 * BEAM]
+    t_head = time.perf_counter() - t0
+    step_s = statistics.mean(t_layers) * cfg["num_hidden_layers"] + t_head
+    return {"value": round(N / step_s, 3), "unit": "beam tokens/s", "cores": n_threads,
+            "kind": "port",
+            "sample": f"{layers_timed} of 32 decoder layers of one cfg3 decode step (128 beams, "
+                      "cascade over 8 x 1024 prefixes + 1-4 page suffixes) + lm_head/top-k once, "
+                      "numpy oracle fp32, scaled to 32 layers",
+            "step_s": round(step_s, 3)}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    import numpy as np
+    warm = cpu_baseline_sample(layers_timed=1)
+    vals = []
+    for _ in range(max(1, min(args.steps, 3))):
+        vals.append(cpu_baseline_sample(layers_timed=1)["step_s"])
+    step_s = statistics.mean(vals)
+    value = PROMPTS * BEAM / step_s
+    base = dict(warm)
+    base["value"] = round(value, 3)
+    base["sample"] += f"; {len(vals)} timed samples after 1 warm-up"
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": "beam tokens/s", "n_gpus": world,
+        "steps": len(vals), "warmup": 1, "ms_per_step": round(step_s * 1e3, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": "cfg3: Llama-3-8B shape, 8 prompts x 1024 tokens, beam width 16, "
+                               "128 new tokens, page size 16, cascade attention",
+                   "model": "Llama-3-8B-shape (random init)", "global_batch": PROMPTS * BEAM,
+                   "seq_len": PROMPT_LEN, "parallelism": "cpu"},
+        "cpu_baseline": base,
+        "e2e": {"value": round(value, 3), "unit": "beam tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--pages", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the end-to-end pass and print a short line (for profiling)")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    res = run_b200(args, rank, world, local_rank)
+    if rank == 0:
+        if not args.no_cpu_baseline and not args.no_e2e:
+            res["cpu_baseline"] = cpu_baseline_sample()
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
