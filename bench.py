@@ -363,6 +363,131 @@ def run_reference(args, rank, world):
     }
 
 
+def run_op_bench(args):
+    """cfg2: op-level cascade attention, append and fork
+    microbench, bf16, Hq 32 / Hkv 8 / D 128 / page 16; shared prefix 2048
+    tokens, W = 16 suffixes of U[1, 256] tokens, page ids a seeded permutation
+    of the pool.  Each timed iteration is preceded by a 256 MB L2 flush;
+    durations are CUDA events on the launching stream (median of --iters)."""
+    import numpy as np
+    import torch
+    from beam_engine_b200 import _lib
+    from beam_engine_b200.cascade import MultiLevelCascadeAttentionWrapper
+    from beam_engine_b200.page_table import PageTable
+    dev = torch.device("cuda", 0)
+    Hq, Hkv, D, ps, W, prefix = 32, 8, 128, 16, 16, 2048
+    P = args.pool_pages
+    g = torch.Generator().manual_seed(0)
+    perm = torch.randperm(P, generator=g)
+    suf = torch.randint(1, 257, (W,), generator=g).tolist()
+    npre = prefix // ps
+    off = npre
+    kvp, kvi, last = [0], [], []
+    for L in suf:
+        n = -(-L // ps)
+        kvi += perm[off:off + n].tolist()
+        off += n
+        kvp.append(len(kvi))
+        last.append(L - (n - 1) * ps)
+    levels = [dict(qo_indptr=[0, W], kv_indptr=[0, npre], kv_indices=perm[:npre].tolist(),
+                   kv_last_page_len=[ps]),
+              dict(qo_indptr=list(range(W + 1)), kv_indptr=kvp, kv_indices=kvi, kv_last_page_len=last)]
+    layers = args.op_layers
+    pt = PageTable(1, ps, P, Hkv, D, device=dev, store_dtype=torch.bfloat16)
+    pt.kv_cache.normal_(generator=torch.Generator(device=dev).manual_seed(1))
+    P2 = min(P, 4096)        # all-layer pool for the fused append / fork launches
+    ptL = PageTable(layers, ps, P2, Hkv, D, device=dev, store_dtype=torch.bfloat16)
+    q = torch.randn((W, Hq, D), device=dev).to(torch.bfloat16)
+    ws = torch.empty(128 << 20, dtype=torch.uint8, device=dev)
+    w = MultiLevelCascadeAttentionWrapper(2, ws)
+    t = lambda a: torch.tensor(np.asarray(a, np.int32))  # noqa: E731
+    w.plan([t(x["qo_indptr"]) for x in levels], [t(x["kv_indptr"]) for x in levels],
+           [t(x["kv_indices"]) for x in levels], [t(x["kv_last_page_len"]) for x in levels],
+           Hq, Hkv, D, ps, causal=True, sm_scale=D ** -0.5, split_tokens=args.split)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    hbm, _, src = peaks()
+
+    def timeit(fn, iters):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            ts.append(s.elapsed_time(e))
+        return statistics.median(ts) * 1e3
+    out = torch.empty_like(q)
+    attn_us = timeit(lambda: w.run(q, pt.kv_cache_at_layer[0], out=out), args.iters)
+    kv_tokens = prefix + sum(suf)
+    attn_bytes = kv_tokens * 2 * Hkv * D * 2 + 2 * W * Hq * D * 2
+    pre_bytes = prefix * 2 * Hkv * D * 2
+    # append: one token per beam at (tail page, L % 16), one layer and all layers
+    pages = torch.tensor([kvi[kvp[b + 1] - 1] for b in range(W)], dtype=torch.int32, device=dev)
+    pos = torch.tensor([L % ps for L in suf], dtype=torch.int32, device=dev)
+    kk = torch.randn((layers, W, Hkv, D), device=dev).to(torch.bfloat16)
+    vv = torch.randn((layers, W, Hkv, D), device=dev).to(torch.bfloat16)
+    ar = torch.arange(W + 1, dtype=torch.int32, device=dev)
+    L = _lib.lib()
+    pagesL = pages % P2
+
+    def app(nl):
+        tab, pg, npg = (pt, pages, P) if nl == 1 else (ptL, pagesL, P2)
+        _lib.check(L.be_append_paged_kv(kk.data_ptr(), vv.data_ptr(), Hkv * D, W * Hkv * D,
+                                        ar.data_ptr(), pos.data_ptr(), pg.data_ptr(),
+                                        ar.data_ptr(), W, tab.kv_cache.data_ptr(),
+                                        tab.kv_cache.stride(0), nl, npg, ps, Hkv, D, _lib.BE_BF16,
+                                        None))
+    app1_us = timeit(lambda: app(1), args.iters)
+    appL_us = timeit(lambda: app(layers), args.iters)
+    app_bytes = W * 2 * Hkv * D * 2 * 2          # read + write, K and V
+    # fork: beams remapped by a random parent vector; a parent with c children
+    # copies its partial tail page c - 1 times
+    parent = torch.randint(0, W, (W,), generator=g).tolist()
+    src_p, dst_p, lens = [], [], []
+    fresh = iter(perm[off:].tolist())
+    for p_ in sorted(set(parent)):
+        c = parent.count(p_)
+        tail = suf[p_] - (-(-suf[p_] // ps) - 1) * ps
+        if tail < ps:
+            for _ in range(c - 1):
+                src_p.append(kvi[kvp[p_ + 1] - 1])
+                dst_p.append(next(fresh))
+                lens.append(tail)
+    sd = torch.tensor(src_p or [0], dtype=torch.int32, device=dev)
+    dd = torch.tensor(dst_p or [0], dtype=torch.int32, device=dev)
+    ld = torch.tensor(lens or [0], dtype=torch.int32, device=dev)
+    sdL, ddL = sd % P2, (dd % P2 + P2 // 2) % P2
+
+    def fork(nl):
+        tab, a, b, npg = (pt, sd, dd, P) if nl == 1 else (ptL, sdL, ddL, P2)
+        _lib.check(L.be_fork_tail_copy(tab.kv_cache.data_ptr(), tab.kv_cache.stride(0), nl, npg, ps,
+                                       Hkv, D, _lib.BE_BF16, a.data_ptr(), b.data_ptr(),
+                                       ld.data_ptr(), len(src_p), None))
+    fork1_us = timeit(lambda: fork(1), args.iters) if src_p else 0.0
+    forkL_us = timeit(lambda: fork(layers), args.iters) if src_p else 0.0
+    fork_bytes = sum(lens) * Hkv * D * 2 * 2 * 2   # K+V, read + write
+    inf = w._plan.info
+
+    def rl(b, us):
+        a = b / (us / 1e6) / 1e9 if us else 0.0
+        return {"us": round(us, 2), "bytes": b, "gbs": round(a, 1), "frac": round(a / hbm, 4)}
+    return {
+        "config": {"workload": "cfg2 op microbench", "pool_pages": P, "layers_for_multi": layers,
+                   "prefix": prefix, "beams": W, "suffix_tokens": suf, "l2": "256 MB flush per iter"},
+        "peak_gbs": hbm, "peak_source": src,
+        "cascade_attention": dict(rl(attn_bytes, attn_us), prefix_bytes=pre_bytes,
+                                  plan=dict(work=inf.n_work, wide=inf.n_work_wide, parts=inf.n_parts)),
+        "append_1layer": rl(app_bytes, app1_us),
+        f"append_{layers}layers_1launch": rl(app_bytes * layers, appL_us),
+        "fork_1layer": dict(rl(fork_bytes, fork1_us), copies=len(src_p)),
+        f"fork_{layers}layers_1launch": rl(fork_bytes * layers, forkL_us),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -371,12 +496,21 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--pages", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", default=None, choices=["cfg2"],
+                    help="op-level microbench instead of the decode benchmark")
+    ap.add_argument("--pool-pages", type=int, default=65536)
+    ap.add_argument("--op-layers", type=int, default=32)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end pass and print a short line (for profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.op:
+        print(json.dumps(run_op_bench(args)), flush=True)
+        return
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if rank == 0:
