@@ -16,7 +16,8 @@ vp = C.c_void_p
 P32 = C.POINTER(C.c_int32)
 PP32 = C.POINTER(P32)
 
-BE_OK, BE_EINVAL, BE_ENOMEM, BE_ECUDA, BE_ENOT_ALLOCATED, BE_ECAPACITY, BE_EDEVICE_RANGE = range(7)
+(BE_OK, BE_EINVAL, BE_ENOMEM, BE_ECUDA, BE_ENOT_ALLOCATED, BE_ECAPACITY, BE_EDEVICE_RANGE,
+ BE_EDEVICE_TIMEOUT) = range(8)
 BE_F32, BE_F16, BE_BF16 = 0, 1, 2
 
 
@@ -24,7 +25,7 @@ class AttnPlanInfo(C.Structure):
     _fields_ = [(n, C.c_int32) for n in (
         "n_work", "n_work_wide", "n_queries", "n_parts", "n_merge", "off_work", "off_qlist",
         "off_kvlist", "off_merge_q", "off_merge_ptr", "off_merge_parts", "total_ints",
-        "page_size", "group_size")]
+        "page_size", "group_size", "any_slots", "max_item_tokens", "total_tokens")]
 
 
 _SIGS = {

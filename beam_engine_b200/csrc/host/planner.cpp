@@ -101,6 +101,12 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
   in.total_ints = (int32_t)off;
   in.page_size = page_size;
   in.group_size = g;
+  for (auto& it : items) {
+    const int len = it.w.kv_end - it.w.kv_begin;
+    in.max_item_tokens = std::max(in.max_item_tokens, len);
+    in.total_tokens += len;
+    if (it.w.flags & BE_WORK_SLOTS) in.any_slots = 1;
+  }
   *info = in;
   if (off > cap || !plan) {
     set_error("plan buffer too small: need %lld ints, have %lld", (long long)off, (long long)cap);
@@ -301,6 +307,12 @@ extern "C" int be_tree_plan(int num_vnodes, const int32_t* q_entries, int num_q_
   in.total_ints = (int32_t)off;
   in.page_size = page_size;
   in.group_size = g;
+  in.any_slots = 1;
+  for (auto& it : items) {
+    const int len = it.w.kv_end - it.w.kv_begin;
+    in.max_item_tokens = std::max(in.max_item_tokens, len);
+    in.total_tokens += len;
+  }
   *info = in;
   if (off > plan_capacity || !plan) {
     set_error("plan buffer too small: need %lld ints, have %lld", (long long)off,

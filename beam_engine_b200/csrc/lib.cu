@@ -3,4 +3,6 @@
 // instead of with relocatable device code.
 #include "page_ops.cu"
 #include "attention.cu"
+#include "attention_tma.cu"
+#include "attn_api.cu"
 #include "model_ops.cu"

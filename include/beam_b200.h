@@ -27,7 +27,8 @@ typedef enum {
   BE_ECUDA = 3,            /* CUDA runtime error                               */
   BE_ENOT_ALLOCATED = 4,   /* free of a page that is not allocated (a warning, page_table.py:117-119) */
   BE_ECAPACITY = 5,        /* caller buffer too small; required size reported   */
-  BE_EDEVICE_RANGE = 6     /* device status: an index was out of range and skipped */
+  BE_EDEVICE_RANGE = 6,    /* device status: an index was out of range and skipped */
+  BE_EDEVICE_TIMEOUT = 7   /* device status: a bounded pipeline wait expired; output invalid */
 } be_status;
 
 typedef enum { BE_F32 = 0, BE_F16 = 1, BE_BF16 = 2 } be_dtype;
@@ -112,6 +113,9 @@ typedef struct {
   int32_t total_ints;    /* ints to copy to the device                         */
   int32_t page_size;
   int32_t group_size;    /* num_qo_heads / num_kv_heads                        */
+  int32_t any_slots;     /* some item lists slot ids (BE_WORK_SLOTS)           */
+  int32_t max_item_tokens; /* longest work item (tokens)                      */
+  int32_t total_tokens;  /* sum of work-item token ranges                      */
 } be_attn_plan_info;
 
 /* Plans MultiLevelCascadeAttentionWrapper.plan + .run
