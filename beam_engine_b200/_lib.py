@@ -25,7 +25,7 @@ class AttnPlanInfo(C.Structure):
     _fields_ = [(n, C.c_int32) for n in (
         "n_work", "n_work_wide", "n_queries", "n_parts", "n_merge", "off_work", "off_qlist",
         "off_kvlist", "off_merge_q", "off_merge_ptr", "off_merge_parts", "total_ints",
-        "page_size", "group_size", "any_slots", "max_item_tokens", "total_tokens")]
+        "page_size", "group_size", "any_slots", "max_item_tokens", "total_tokens", "max_wide_tokens")]
 
 
 _SIGS = {

@@ -41,6 +41,7 @@ struct AttnParams {
   float* mid_o;
   float* mid_lse;
   int n_work, n_wide;
+  int debug;             // profiling switches (BE_ATTN_DEBUG), 0 in normal runs
 };
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -456,7 +457,9 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p, int D) {
   }
 }
 
-// LSE merge: one warp per (query, head).
+// LSE merge: one warp per (query, head).  Lanes hold head_dim in float4
+// chunks; partial rows are read four at a time with independent loads, and
+// the log-sum-exp weights come from a lane-parallel pass over the lse values.
 template <typename T>
 __global__ void __launch_bounds__(128) merge_kernel(const int32_t* __restrict__ mq,
                                                     const int32_t* __restrict__ mptr,
@@ -471,7 +474,9 @@ __global__ void __launch_bounds__(128) merge_kernel(const int32_t* __restrict__ 
   const int qi = mq[b];
   const int p0 = mptr[b], p1 = mptr[b + 1];
   float mx = -INFINITY;
-  for (int k = p0; k < p1; ++k) mx = fmaxf(mx, mid_lse[(int64_t)mparts[k] * hq + head]);
+  for (int k = p0 + lane; k < p1; k += 32) mx = fmaxf(mx, mid_lse[(int64_t)mparts[k] * hq + head]);
+#pragma unroll
+  for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
   T* dst = reinterpret_cast<T*>(out) + qi * out_row_stride + (int64_t)head * D;
   if (mx == -INFINITY) {
     for (int d = lane; d < D; d += 32) dst[d] = from_f<T>(0.f);
@@ -479,20 +484,53 @@ __global__ void __launch_bounds__(128) merge_kernel(const int32_t* __restrict__ 
     return;
   }
   float den = 0.f;
-  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int k = p0; k < p1; ++k) {
-    const int64_t pr = (int64_t)mparts[k] * hq + head;
-    const float wgt = expf(mid_lse[pr] - mx);
-    den += wgt;
-    const float* src = mid_o + pr * D;
+  for (int k = p0 + lane; k < p1; k += 32) den += expf(mid_lse[(int64_t)mparts[k] * hq + head] - mx);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (lane + 32 * j < D) acc[j] += wgt * src[lane + 32 * j];
+  for (int off = 16; off; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+  const int nv = D / 4;                 // float4 chunks per row (<= 64)
+  float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  for (int k0 = p0; k0 < p1; k0 += 4) {
+    float wgt[4];
+    const float* src[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + u;
+      if (k < p1) {
+        const int64_t pr = (int64_t)mparts[k] * hq + head;
+        wgt[u] = expf(mid_lse[pr] - mx);
+        src[u] = mid_o + pr * D;
+      } else {
+        wgt[u] = 0.f;
+        src[u] = nullptr;
+      }
+    }
+    float4 v[4][2];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = lane + 32 * h;
+        v[u][h] = (src[u] && c < nv) ? __ldg(reinterpret_cast<const float4*>(src[u]) + c)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        acc[h].x += wgt[u] * v[u][h].x; acc[h].y += wgt[u] * v[u][h].y;
+        acc[h].z += wgt[u] * v[u][h].z; acc[h].w += wgt[u] * v[u][h].w;
+      }
   }
   const float inv = 1.f / den;
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
-    if (lane + 32 * j < D) dst[lane + 32 * j] = from_f<T>(acc[j] * inv);
+  for (int h = 0; h < 2; ++h) {
+    const int c = lane + 32 * h;
+    if (c < nv) {
+      T* o4 = dst + c * 4;
+      o4[0] = from_f<T>(acc[h].x * inv); o4[1] = from_f<T>(acc[h].y * inv);
+      o4[2] = from_f<T>(acc[h].z * inv); o4[3] = from_f<T>(acc[h].w * inv);
+    }
+  }
   if (lse && lane == 0) lse[(int64_t)qi * hq + head] = mx + logf(den);
 }
 

@@ -7,9 +7,10 @@
 //     map over the pool [pages][2][page_size][kv_heads][dims] into an 8-stage
 //     ring, each stage signalled by an mbarrier with complete_tx;
 //   * consumers: S = Q K^T and O += P V on the tensor cores (mma.sync
-//     m16n8k16, fp32 accumulate), online softmax in registers; wide tiles
-//     (<= 64 rows) give each warp 16 rows and every page, narrow tiles
-//     (<= 16 rows) give each warp every 4th page;
+//     m16n8k16, fp32 accumulate), online softmax in registers, several pages
+//     per step for instruction-level parallelism; wide tiles (<= 64 rows)
+//     give each warp 16 rows and every 4-page step, narrow tiles (<= 16 rows)
+//     give each warp every 4th 2-page step;
 //   * end: the CTA folds its warps' (m, l, O) in shared memory, then rank 0 of
 //     the cluster folds the peers' states over distributed shared memory (no
 //     HBM traffic for the split); the result goes to the output or to a
@@ -110,15 +111,26 @@ constexpr size_t tma_smem_bytes() {
 }
 // fold buffers (4 slots x 16 rows or 1 slot x 64 rows, m/l, per-rank weights)
 // reuse the stage ring
-static_assert(64 * 128 * 4 + 2 * 64 * 4 + 64 * 8 * 4 <= TMA_NS * 2 * 2 * TMA_BOX_BYTES,
+static_assert(64 * 132 * 4 + 2 * 64 * 4 + 64 * 8 * 4 <= TMA_NS * 2 * 2 * TMA_BOX_BYTES,
               "fold buffers must fit in the stage ring (D = 128)");
-static_assert(64 * 64 * 4 + 2 * 64 * 4 + 64 * 8 * 4 <= TMA_NS * 2 * 1 * TMA_BOX_BYTES,
+static_assert(64 * 68 * 4 + 2 * 64 * 4 + 64 * 8 * 4 <= TMA_NS * 2 * 1 * TMA_BOX_BYTES,
               "fold buffers must fit in the stage ring (D = 64)");
+
+// Profiling stamps (BE_ATTN_DEBUG & 4): globaltimer per phase into p.lse.
+__device__ __forceinline__ void stamp(const AttnParams& p, int phase) {
+  if ((p.debug & 4) && p.lse && threadIdx.x == 0)
+    reinterpret_cast<unsigned long long*>(p.lse)[((int64_t)blockIdx.x * gridDim.y + blockIdx.y) * 8 +
+                                                 phase] = gtimer();
+}
 
 template <typename T, int D, int MT>
 __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Work& w, int kvh,
                          int cs, int rank, char* smem) {
   constexpr int NWM = MT / 16, NWK = 4 / NWM, KSTEPS = D / 16;
+  // pages per consumer step: wide tiles take 4 (all warps share each step),
+  // narrow tiles 2 (each warp owns every 4th step, 4 steps fill the ring)
+  constexpr int PG = MT == 64 ? 4 : 2;
+  static_assert(TMA_NS % (PG * NWK) == 0 || NWK == 1, "ring must hold one step per warp");
   constexpr int STAGE = tma_stage_bytes<D>();
   char* sStage = smem;                                   // TMA_NS * STAGE, 1024-aligned
   char* sQ = smem + TMA_NS * STAGE;                      // [64][D] T
@@ -134,6 +146,7 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
   const int pb = (int)((int64_t)n_pages * (rank + 1) / cs);
   const int npg = pb - pa;
   const int first_page = w.kv_begin / ps + pa;
+  stamp(p, 0);
   if (tid == 0) {
     for (int s = 0; s < TMA_NS; ++s) {
       mbar_init(&full[s], 1);
@@ -143,20 +156,31 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
     *issued_ptr = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp < 4) {  // Q tile, zero rows past q_len * g
+  __syncthreads();   // barriers ready: the producer starts streaming now
+  if (warp < 4) {    // Q tile (overlaps the first TMA loads), zero rows past q_len * g
     constexpr int CPR = D / 8;
-    for (int idx = tid; idx < MT * CPR; idx += 128) {
+    constexpr int PER = MT * CPR / 128;
+    int4 val[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int idx = tid + k * 128;
       const int r = idx / CPR, c = idx % CPR;
-      int4 val = make_int4(0, 0, 0, 0);
+      val[k] = make_int4(0, 0, 0, 0);
       if (r < rows) {
         const int qi = p.qlist[w.q_off + r / g];
-        val = *reinterpret_cast<const int4*>(reinterpret_cast<const T*>(p.q) + qi * p.q_row_stride +
-                                             (int64_t)(kvh * g + r % g) * D + c * 8);
+        val[k] = *reinterpret_cast<const int4*>(reinterpret_cast<const T*>(p.q) +
+                                                qi * p.q_row_stride + (int64_t)(kvh * g + r % g) * D +
+                                                c * 8);
       }
-      *reinterpret_cast<int4*>(sQ + swz<D>(r, c)) = val;
     }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int idx = tid + k * 128;
+      *reinterpret_cast<int4*>(sQ + swz<D>(idx / CPR, idx % CPR)) = val[k];
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // consumer warps only
   }
-  __syncthreads();
+  stamp(p, 1);
 
   float o[D / 8][4];
 #pragma unroll
@@ -167,33 +191,50 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
 
   if (warp == 4) {
     // ---------------- producer ----------------
-    if (lane == 0) {
-      const uint32_t tx = STAGE;
-      int j = 0;
-      for (; j < npg; ++j) {
-        const int s = j % TMA_NS;
-        if (j >= TMA_NS && !mbar_wait(&empty[s], ((j / TMA_NS) - 1) & 1)) {
-          *abort_flag = 1;
+    // Page ids are fetched 32 at a time by the whole warp (one coalesced load)
+    // and handed to lane 0 by shuffles, so the issue loop never waits on a
+    // dependent global load.
+    const uint32_t tx = STAGE;
+    bool stop = false;
+    int j = 0;
+    for (int base = 0; base < npg && !stop; base += 32) {
+      const int jj = base + lane;
+      const int my_page = jj < npg ? p.kvlist[w.kv_off + first_page + jj] : -1;
+      const int cnt = min(32, npg - base);
+      for (int k = 0; k < cnt; ++k) {
+        const int page = __shfl_sync(0xffffffffu, my_page, k);
+        j = base + k;
+        int go = 1;
+        if (lane == 0) {
+          const int s = j % TMA_NS;
+          if (j >= TMA_NS && !mbar_wait(&empty[s], ((j / TMA_NS) - 1) & 1)) {
+            *abort_flag = 1;
+            go = 0;
+          } else if (*abort_flag) {
+            go = 0;
+          } else if (page < 0 || page >= p.num_pages) {
+            flag_range_error();
+            mbar_arrive(&full[s]);  // consumers see stale data; the status records the error
+          } else {
+            mbar_expect_tx(&full[s], tx);
+            const uint32_t dst = smem_u32(sStage + s * STAGE);
+#pragma unroll
+            for (int pl = 0; pl < 2; ++pl)
+#pragma unroll
+              for (int h = 0; h < D / 64; ++h)
+                tma_load5(dst + (pl * (D / 64) + h) * TMA_BOX_BYTES, tmap, &full[s], h * 64, kvh,
+                          0, pl, page);
+          }
+        }
+        go = __shfl_sync(0xffffffffu, go, 0);
+        if (!go) {
+          stop = true;
           break;
         }
-        if (*abort_flag) break;
-        const int page = p.kvlist[w.kv_off + first_page + j];
-        if (page < 0 || page >= p.num_pages) {
-          flag_range_error();
-          mbar_arrive(&full[s]);  // consumers see stale data; the status records the error
-          continue;
-        }
-        mbar_expect_tx(&full[s], tx);
-        const uint32_t dst = smem_u32(sStage + s * STAGE);
-#pragma unroll
-        for (int pl = 0; pl < 2; ++pl)
-#pragma unroll
-          for (int h = 0; h < D / 64; ++h)
-            tma_load5(dst + (pl * (D / 64) + h) * TMA_BOX_BYTES, tmap, &full[s], h * 64, kvh, 0, pl,
-                      page);
+        ++j;
       }
-      *issued_ptr = j;
     }
+    if (lane == 0) *issued_ptr = stop ? j : npg;
   } else {
     // ---------------- consumers ----------------
     uint32_t qf[KSTEPS][4];
@@ -209,39 +250,71 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
       if (r0 < rows) lim0 = min(w.kv_end, w.kv_total - w.q_len + r0 / g + 1);
       if (r1 < rows) lim1 = min(w.kv_end, w.kv_total - w.q_len + r1 / g + 1);
     }
-    for (int j = warp_k; j < npg; j += NWK) {
-      const int s = j % TMA_NS;
-      if (*abort_flag || !mbar_wait(&full[s], (j / TMA_NS) & 1)) {
+    // Each step takes PG consecutive pages (16*PG tokens): PG*2 independent
+    // n-tiles per k-step for S, one softmax pass, PG k-steps per d-tile for PV.
+    const int ngroups = (npg + PG - 1) / PG;
+    for (int gi = warp_k; gi < ngroups; gi += NWK) {
+      const int j0 = gi * PG;
+      bool ok = !*abort_flag;
+#pragma unroll
+      for (int pi = 0; pi < PG; ++pi) {
+        const int j = j0 + pi;
+        if (ok && j < npg && !mbar_wait(&full[j % TMA_NS], (j / TMA_NS) & 1)) ok = false;
+      }
+      if (!ok) {
         *abort_flag = 1;
         break;
       }
-      char* st = sStage + s * STAGE;
-      const int t0 = w.kv_begin + (pa + j) * ps;
-      const int valid = min(ps, w.kv_end - t0);
-      if (valid < 16) {  // zero V rows past the range (stale pool data may be non-finite)
-        for (int idx = lane; idx < (16 - valid) * (D / 8); idx += 32) {
-          const int r = valid + idx / (D / 8), c = idx % (D / 8);
-          *reinterpret_cast<int4*>(st + stage_off<D>(1, r, c)) = make_int4(0, 0, 0, 0);
-        }
+      if (gi == warp_k) stamp(p, 2);
+      if (p.debug & 1) {
         __syncwarp();
+        if (lane == 0)
+          for (int pi = 0; pi < PG; ++pi)
+            if (j0 + pi < npg) mbar_arrive(&empty[(j0 + pi) % TMA_NS]);
+        continue;
       }
-      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      float sc[2 * PG][4];
+#pragma unroll
+      for (int n = 0; n < 2 * PG; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+      for (int pi = 0; pi < PG; ++pi) {
+        const int j = j0 + pi;
+        if (j >= npg) break;
+        char* st = sStage + (j % TMA_NS) * STAGE;
+        const int valid = min(ps, w.kv_end - (w.kv_begin + (pa + j) * ps));
+        if (valid < 16) {  // zero V rows past the range (stale pool data may be non-finite)
+          for (int idx = lane; idx < (16 - valid) * (D / 8); idx += 32) {
+            const int r = valid + idx / (D / 8), c = idx % (D / 8);
+            *reinterpret_cast<int4*>(st + stage_off<D>(1, r, c)) = make_int4(0, 0, 0, 0);
+          }
+        }
+      }
+      __syncwarp();
 #pragma unroll
       for (int kk = 0; kk < KSTEPS; ++kk) {
-        const int mi = lane / 8;
-        const int tok = ((mi >> 1) << 3) + (lane % 8);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(smem_u32(st + stage_off<D>(0, tok, kk * 2 + (mi & 1))), b0, b1, b2, b3);
-        mma16816<T>(sc[0], qf[kk], b0, b1);
-        mma16816<T>(sc[1], qf[kk], b2, b3);
+#pragma unroll
+        for (int pi = 0; pi < PG; ++pi) {
+          const int j = j0 + pi;
+          if (j < npg) {
+            const char* st = sStage + (j % TMA_NS) * STAGE;
+            const int mi = lane / 8;
+            const int tok = ((mi >> 1) << 3) + (lane % 8);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(smem_u32(st + stage_off<D>(0, tok, kk * 2 + (mi & 1))), b0, b1, b2, b3);
+            mma16816<T>(sc[2 * pi], qf[kk], b0, b1);
+            mma16816<T>(sc[2 * pi + 1], qf[kk], b2, b3);
+          }
+        }
       }
+      const int tbase = w.kv_begin + (pa + j0) * ps;
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int n = 0; n < 2; ++n)
+      for (int n = 0; n < 2 * PG; ++n)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const int t = t0 + n * 8 + 2 * (lane % 4) + (c & 1);
-          const float x = t < (c < 2 ? lim0 : lim1) ? sc[n][c] * p.scale_log2 : -INFINITY;
+          const int t = tbase + n * 8 + 2 * (lane % 4) + (c & 1);
+          const bool in = (j0 + n / 2) < npg && t < (c < 2 ? lim0 : lim1);
+          const float x = in ? sc[n][c] * p.scale_log2 : -INFINITY;
           sc[n][c] = x;
           if (c < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
         }
@@ -254,7 +327,7 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
       const float a1 = (mn1 == -INFINITY) ? 1.f : exp2f(m1 - mn1);
       float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
-      for (int n = 0; n < 2; ++n)
+      for (int n = 0; n < 2 * PG; ++n)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const float mref = c < 2 ? mn0 : mn1;
@@ -270,24 +343,37 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
       for (int i = 0; i < D / 8; ++i) {
         o[i][0] *= a0; o[i][1] *= a0; o[i][2] *= a1; o[i][3] *= a1;
       }
-      uint32_t pa4[4] = {pack2<T>(sc[0][0], sc[0][1]), pack2<T>(sc[0][2], sc[0][3]),
-                         pack2<T>(sc[1][0], sc[1][1]), pack2<T>(sc[1][2], sc[1][3])};
 #pragma unroll
-      for (int dn = 0; dn < D / 16; ++dn) {
-        const int mi = lane / 8;
-        const int tok = ((mi & 1) << 3) + (lane % 8);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(smem_u32(st + stage_off<D>(1, tok, dn * 2 + (mi >> 1))), b0, b1, b2, b3);
-        mma16816<T>(o[2 * dn], pa4, b0, b1);
-        mma16816<T>(o[2 * dn + 1], pa4, b2, b3);
+      for (int pi = 0; pi < PG; ++pi) {
+        const int j = j0 + pi;
+        if (j >= npg) break;
+        const char* st = sStage + (j % TMA_NS) * STAGE;
+        uint32_t pa4[4] = {pack2<T>(sc[2 * pi][0], sc[2 * pi][1]),
+                           pack2<T>(sc[2 * pi][2], sc[2 * pi][3]),
+                           pack2<T>(sc[2 * pi + 1][0], sc[2 * pi + 1][1]),
+                           pack2<T>(sc[2 * pi + 1][2], sc[2 * pi + 1][3])};
+#pragma unroll
+        for (int dn = 0; dn < D / 16; ++dn) {
+          const int mi = lane / 8;
+          const int tok = ((mi & 1) << 3) + (lane % 8);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(smem_u32(st + stage_off<D>(1, tok, dn * 2 + (mi >> 1))), b0, b1, b2, b3);
+          mma16816<T>(o[2 * dn], pa4, b0, b1);
+          mma16816<T>(o[2 * dn + 1], pa4, b2, b3);
+        }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (lane == 0) {
+#pragma unroll
+        for (int pi = 0; pi < PG; ++pi)
+          if (j0 + pi < npg) mbar_arrive(&empty[(j0 + pi) % TMA_NS]);
+      }
     }
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    stamp(p, 3);
   }
   // Drain: after an abort, wait (bounded) for every issued TMA before the ring
   // memory is reused; normally every issued page was consumed already.
@@ -301,17 +387,21 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
   }
   __syncthreads();
 
+  stamp(p, 4);
+  if (p.debug & 2) return;
   // ---- fold the warps' states: slot k holds the rows of warp column k ----
-  float* sO = reinterpret_cast<float*>(sStage);          // [NWK][MT][D]
-  float* sM = sO + NWK * MT * D;                         // [NWK][MT]
+  // (row pitch D + 4 floats keeps the fragment stores free of bank conflicts)
+  constexpr int OS = D + 4;
+  float* sO = reinterpret_cast<float*>(sStage);          // [NWK][MT][OS]
+  float* sM = sO + NWK * MT * OS;                        // [NWK][MT]
   float* sL = sM + NWK * MT;
-  float* sW = sL + NWK * MT;                             // [MT][8] cluster fold weights
+  float* sW = sL + NWK * MT;                             // [MT][8] fold weights
   if (warp < 4) {
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) {
       const int d = i * 8 + 2 * (lane % 4);
-      *reinterpret_cast<float2*>(&sO[(warp_k * MT + r0) * D + d]) = make_float2(o[i][0], o[i][1]);
-      *reinterpret_cast<float2*>(&sO[(warp_k * MT + r1) * D + d]) = make_float2(o[i][2], o[i][3]);
+      *reinterpret_cast<float2*>(&sO[(warp_k * MT + r0) * OS + d]) = make_float2(o[i][0], o[i][1]);
+      *reinterpret_cast<float2*>(&sO[(warp_k * MT + r1) * OS + d]) = make_float2(o[i][2], o[i][3]);
     }
     if (lane % 4 == 0) {
       sM[warp_k * MT + r0] = m0; sL[warp_k * MT + r0] = l0;
@@ -320,29 +410,38 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
   }
   __syncthreads();
   const int nthr = blockDim.x;
-  if (NWK > 1) {  // fold slots into slot 0; weights from the unmodified m of each slot
-    for (int idx = tid; idx < MT * D; idx += nthr) {
-      const int r = idx / D, d = idx % D;
-      float mt = -INFINITY;
-#pragma unroll
-      for (int k = 0; k < NWK; ++k) mt = fmaxf(mt, sM[k * MT + r]);
-      float acc = 0.f;
-#pragma unroll
-      for (int k = 0; k < NWK; ++k)
-        acc += (mt == -INFINITY ? 0.f : exp2f(sM[k * MT + r] - mt)) * sO[(k * MT + r) * D + d];
-      sO[r * D + d] = acc;
-    }
-    __syncthreads();
+  if (NWK > 1) {  // fold slots into slot 0 with per-row weights computed once
     if (tid < MT) {
       float mt = -INFINITY, lt = 0.f;
       for (int k = 0; k < NWK; ++k) mt = fmaxf(mt, sM[k * MT + tid]);
-      for (int k = 0; k < NWK; ++k)
-        lt += (mt == -INFINITY ? 0.f : exp2f(sM[k * MT + tid] - mt)) * sL[k * MT + tid];
-      sM[tid] = mt;   // row tid of slot 0 is touched only by this thread here
-      sL[tid] = lt;
+      for (int k = 0; k < NWK; ++k) {
+        const float wk = mt == -INFINITY ? 0.f : exp2f(sM[k * MT + tid] - mt);
+        sW[tid * 8 + k] = wk;
+        lt += wk * sL[k * MT + tid];
+      }
+      sW[tid * 8 + 4] = mt;
+      sW[tid * 8 + 5] = lt;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < MT * (D / 4); idx += nthr) {
+      const int r = idx / (D / 4), d = (idx % (D / 4)) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < NWK; ++k) {
+        const float4 v = *reinterpret_cast<const float4*>(&sO[(k * MT + r) * OS + d]);
+        const float wk = sW[r * 8 + k];
+        acc.x += wk * v.x; acc.y += wk * v.y; acc.z += wk * v.z; acc.w += wk * v.w;
+      }
+      *reinterpret_cast<float4*>(&sO[r * OS + d]) = acc;
+    }
+    __syncthreads();
+    if (tid < MT) {
+      sM[tid] = sW[tid * 8 + 4];
+      sL[tid] = sW[tid * 8 + 5];
     }
     __syncthreads();
   }
+  stamp(p, 5);
   // ---- fold the cluster's CTAs: rank 0 reads the peers over DSMEM ----
   if (cs > 1) cluster_sync();
   if (rank == 0) {
@@ -375,9 +474,9 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
       for (int c = 0; c < cs; ++c) {
         float4 v;
         if (c == 0) {
-          v = *reinterpret_cast<const float4*>(&sO[r * D + d]);
+          v = *reinterpret_cast<const float4*>(&sO[r * OS + d]);
         } else {
-          const uint32_t a = map_peer(aO + (r * D + d) * 4, c);
+          const uint32_t a = map_peer(aO + (r * OS + d) * 4, c);
           asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
                        : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                        : "r"(a)
@@ -399,15 +498,16 @@ __device__ void tma_tile(const CUtensorMap* tmap, const AttnParams& p, const Wor
     }
   }
   if (cs > 1) cluster_sync();  // peers keep their shared memory until rank 0 is done
+  stamp(p, 6);
 }
 
 template <typename T, int D>
 __global__ void __launch_bounds__(160) attn_tma_kernel(const __grid_constant__ CUtensorMap tmap,
-                                                       AttnParams p, int cs) {
+                                                       AttnParams p, int cs, int w0) {
   extern __shared__ char smem_raw[];
   char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~uintptr_t(1023));
-  const int wi = blockIdx.x / cs;
+  const int wi = w0 + blockIdx.x / cs;
   const int rank = cs > 1 ? (int)cluster_rank() : 0;
   const Work w = p.work[wi];
   if (wi < p.n_wide)
@@ -505,7 +605,7 @@ static int pick_cluster(const be_attn_plan_info* info, int hkv, int ps) {
 }
 
 template <typename T, int D>
-int launch_tma(const AttnParams& p, const CUtensorMap& map, int cs, cudaStream_t st) {
+int launch_tma(const AttnParams& p, const CUtensorMap& map, int cs, int w0, cudaStream_t st) {
   const size_t smem = tma_smem_bytes<D>();
   static bool set = false;
   if (!set) {
@@ -514,7 +614,7 @@ int launch_tma(const AttnParams& p, const CUtensorMap& map, int cs, cudaStream_t
     set = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.n_work * cs, p.hkv, 1);
+  cfg.gridDim = dim3((p.n_work - w0) * cs, p.hkv, 1);
   cfg.blockDim = dim3(160, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -525,7 +625,7 @@ int launch_tma(const AttnParams& p, const CUtensorMap& map, int cs, cudaStream_t
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  BE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, attn_tma_kernel<T, D>, map, p, cs));
+  BE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, attn_tma_kernel<T, D>, map, p, cs, w0));
   return BE_OK;
 }
 

@@ -18,7 +18,18 @@ int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t
         rc = get_pool_map(p.pool, p.num_pages, p.page_size, p.hkv, D, DT<T>::id, &map);
         if (rc != BE_OK) return rc;
         const int cs = pick_cluster(info, p.hkv, p.page_size);
-        rc = D == 128 ? launch_tma<T, 128>(p, map, cs, st) : launch_tma<T, 64>(p, map, cs, st);
+        // wide tiles (shared prefixes) on tcgen05 when their chunks fit TMEM/smem
+        const bool umma = umma_enabled() && p.n_wide > 0 && info->max_wide_tokens <= UM_MAX_TOK &&
+                          ((uintptr_t)p.out % 16 == 0) && (p.out_row_stride % 8 == 0);
+        int w0 = 0;
+        if (umma) {
+          rc = D == 128 ? launch_umma<T, 128>(p, map, st) : launch_umma<T, 64>(p, map, st);
+          if (rc != BE_OK) return rc;
+          w0 = p.n_wide;
+        }
+        if (p.n_work > w0)
+          rc = D == 128 ? launch_tma<T, 128>(p, map, cs, w0, st)
+                        : launch_tma<T, 64>(p, map, cs, w0, st);
       } else if (D == 128) rc = launch_tc<T, 128>(p, st);
       else if (D == 64) rc = launch_tc<T, 64>(p, st);
       else {
@@ -97,6 +108,10 @@ extern "C" int be_attn_run(const int32_t* plan_dev, const be_attn_plan_info* inf
   p.mid_lse = mid_lse;
   p.n_work = info->n_work;
   p.n_wide = info->n_work_wide;
+  {
+    const char* e = getenv("BE_ATTN_DEBUG");
+    p.debug = e ? atoi(e) : 0;
+  }
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
     case BE_BF16: return launch_all<__nv_bfloat16>(p, info, plan_dev, head_dim, st);

@@ -105,6 +105,7 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
     const int len = it.w.kv_end - it.w.kv_begin;
     in.max_item_tokens = std::max(in.max_item_tokens, len);
     in.total_tokens += len;
+    if (it.wide) in.max_wide_tokens = std::max(in.max_wide_tokens, len);
     if (it.w.flags & BE_WORK_SLOTS) in.any_slots = 1;
   }
   *info = in;
@@ -209,6 +210,8 @@ extern "C" int be_cascade_plan(int num_levels, const int32_t* const* qo_indptr,
     } else {
       const int min_chunk = round_pages((int64_t)std::min(gr.qlen, tq) * g * 8);
       chunk = std::max(min_chunk, balanced);
+      // wide tiles run as one resident tensor-core tile of at most 256 tokens
+      if (wide) chunk = std::min(chunk, 256);
       const int nsplit = (gr.kv_len + chunk - 1) / chunk;
       chunk = round_pages((gr.kv_len + nsplit - 1) / nsplit);
     }
@@ -312,6 +315,7 @@ extern "C" int be_tree_plan(int num_vnodes, const int32_t* q_entries, int num_q_
     const int len = it.w.kv_end - it.w.kv_begin;
     in.max_item_tokens = std::max(in.max_item_tokens, len);
     in.total_tokens += len;
+    if (it.wide) in.max_wide_tokens = std::max(in.max_wide_tokens, len);
   }
   *info = in;
   if (off > plan_capacity || !plan) {

@@ -4,5 +4,6 @@
 #include "page_ops.cu"
 #include "attention.cu"
 #include "attention_tma.cu"
+#include "attention_umma.cu"
 #include "attn_api.cu"
 #include "model_ops.cu"

@@ -408,18 +408,26 @@ def run_op_bench(args):
     hbm, _, src = peaks()
 
     def timeit(fn, iters):
+        """Differential timing: (flush + op) x iters minus flush x iters, both
+        enqueued behind a GPU sleep so host launch gaps are not timed."""
         for _ in range(3):
             fn()
-        ts = []
-        for _ in range(iters):
-            flush.zero_()
+
+        def run(with_op):
+            torch.cuda.synchronize()
+            torch.cuda._sleep(2_000_000)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
-            fn()
+            for _ in range(iters):
+                flush.zero_()
+                if with_op:
+                    fn()
             e.record()
             torch.cuda.synchronize()
-            ts.append(s.elapsed_time(e))
-        return statistics.median(ts) * 1e3
+            return s.elapsed_time(e)
+        base = min(run(False) for _ in range(3))
+        tot = min(run(True) for _ in range(3))
+        return max(tot - base, 0.0) / iters * 1e3
     out = torch.empty_like(q)
     attn_us = timeit(lambda: w.run(q, pt.kv_cache_at_layer[0], out=out), args.iters)
     kv_tokens = prefix + sum(suf)

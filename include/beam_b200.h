@@ -116,6 +116,7 @@ typedef struct {
   int32_t any_slots;     /* some item lists slot ids (BE_WORK_SLOTS)           */
   int32_t max_item_tokens; /* longest work item (tokens)                      */
   int32_t total_tokens;  /* sum of work-item token ranges                      */
+  int32_t max_wide_tokens; /* longest wide (> 16-row) work item (tokens)      */
 } be_attn_plan_info;
 
 /* Plans MultiLevelCascadeAttentionWrapper.plan + .run
