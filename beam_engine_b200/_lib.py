@@ -28,6 +28,10 @@ class AttnPlanInfo(C.Structure):
         "page_size", "group_size", "any_slots", "max_item_tokens", "total_tokens", "max_wide_tokens")]
 
 
+class AttnCaps(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("max_work", "max_wide", "max_merge", "cluster")]
+
+
 _SIGS = {
     "be_last_error": (C.c_char_p, []),
     "be_version": (C.c_int, []),
@@ -48,6 +52,8 @@ _SIGS = {
     "be_rope_qkv_append": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp,
                                      C.c_int, C.c_int, vp, vp, C.c_int, C.c_int, vp]),
     "be_silu_mul": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
+    "be_attn_run_fixed": (C.c_int, [vp, vp, C.c_int, vp, i64, vp, C.c_int, C.c_int, C.c_int,
+                                    C.c_int, C.c_int, f32, vp, i64, vp, vp, vp, vp, vp]),
     # host page manager
     "be_trie_create": (vp, [C.c_int, C.c_int]),
     "be_trie_destroy": (None, [vp]),

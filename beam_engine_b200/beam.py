@@ -93,12 +93,93 @@ class PlannedAttention:
             t.append((s, e))
 
 
+class StepGraph:
+    """One beam decode step (forward over all layers, log-softmax, top-k, D2H
+    of the top-k) recorded once as a CUDA graph and replayed every step.
+
+    Everything that changes per step lives in one static device buffer
+    [query ids | positions | append pages | append slots | attention plan]
+    filled by one H2D copy before the replay; attention runs through
+    ``be_attn_run_fixed``, whose launch shape depends only on the capacities
+    (the kernels read the plan's counts from its device-side header)."""
+
+    def __init__(self, gen, n, k, temperature, caps):
+        self.gen, self.n, self.k, self.temp = gen, n, k, temperature
+        m = gen.model
+        self.caps = dict(caps)
+        dev = gen.device
+        self.plan_off = -(-4 * n // 32) * 32
+        self.total = self.plan_off + self.caps["ints"]
+        self.dev_buf = torch.zeros(self.total, dtype=torch.int32, device=dev)
+        self.host_buf = torch.empty(self.total, dtype=torch.int32).pin_memory()
+        self.mid_o = torch.empty(max(1, self.caps["parts"]) * m.Hq * m.D, dtype=torch.float32,
+                                 device=dev)
+        self.mid_lse = torch.empty(max(1, self.caps["parts"]) * m.Hq, dtype=torch.float32,
+                                   device=dev)
+        self.vals_h = torch.empty(n * k, dtype=torch.float32).pin_memory()
+        self.idx_h = torch.empty(n * k, dtype=torch.int64).pin_memory()
+        self.ccaps = _lib.AttnCaps(self.caps["work"], self.caps["wide"], self.caps["merge"], 1)
+        self.graph = None
+
+    def fits(self, n, k, temperature, info):
+        c = self.caps
+        return (n == self.n and k == self.k and temperature == self.temp
+                and info.n_work <= c["work"] and info.n_work_wide <= c["wide"]
+                and info.n_merge <= c["merge"] and info.n_parts <= c["parts"]
+                and info.total_ints <= c["ints"] and info.max_wide_tokens <= 256)
+
+    def run(self, layer, qkv, out):  # attention of one layer (the model calls this)
+        m, pt = self.gen.model, self.gen.page_table
+        rc = lib().be_attn_run_fixed(
+            self.dev_buf.data_ptr() + 4 * self.plan_off, C.byref(self.ccaps), pt.page_size,
+            qkv.data_ptr(), qkv.stride(0), pt.kv_cache[layer].data_ptr(), pt.max_num_pages, m.Hq,
+            m.Hkv, m.D, m.dt, m.D ** -0.5, out.data_ptr(), out.stride(0), None,
+            self.mid_o.data_ptr(), self.mid_lse.data_ptr(), None, stream_ptr(qkv.device))
+        check(rc, "be_attn_run_fixed")
+
+    def _body(self):
+        n = self.n
+        d = self.dev_buf
+        logits = self.gen.model.forward(d[0:n], d[n:2 * n], self.gen.page_table, d[2 * n:3 * n],
+                                        d[3 * n:4 * n], self)
+        if self.temp != 1.0:
+            logits = logits / self.temp
+        lp = torch.log_softmax(logits, dim=-1)
+        v, i = torch.topk(lp, self.k, dim=-1)
+        self.vals_h.copy_(v.reshape(-1), non_blocking=True)
+        self.idx_h.copy_(i.reshape(-1), non_blocking=True)
+
+    def step(self, q, pos, wp, wpos, plan):
+        n = self.n
+        h = self.host_buf.numpy()
+        h[0:n], h[n:2 * n], h[2 * n:3 * n], h[3 * n:4 * n] = q, pos, wp, wpos
+        h[self.plan_off:self.plan_off + len(plan)] = plan
+        used = self.plan_off + len(plan)
+        self.dev_buf[:used].copy_(self.host_buf[:used], non_blocking=True)
+        if self.graph is None:
+            cur = torch.cuda.current_stream(self.gen.device)
+            side = torch.cuda.Stream(self.gen.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                self._body()            # warm-up (writes the same K/V the replay will)
+            cur.wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._body()
+            self.graph = g
+        self.graph.replay()
+        torch.cuda.current_stream(self.gen.device).synchronize()
+        k = self.k
+        return (self.vals_h.numpy()[:n * k].reshape(n, k).astype(np.float64),
+                self.idx_h.numpy()[:n * k].reshape(n, k).astype(np.int32))
+
+
 class BeamSearchGenerator:
     """beam.py:17-352.  ``model`` is a :class:`BeamLlama`."""
 
     def __init__(self, model, tokenizer, strategy, page_size: int = 8, kernel_type: str = "cascade",
                  max_num_pages: int = 1024, store_dtype: Optional[torch.dtype] = None,
-                 workspace_bytes: int = 128 << 20):
+                 workspace_bytes: int = 128 << 20, use_graph: bool = True):
         if kernel_type not in ("cascade", "fasttree"):
             raise ValueError(f"Unknown kernel_type: {kernel_type}. Must be 'cascade' or 'fasttree'.")
         self.model = model
@@ -117,6 +198,10 @@ class BeamSearchGenerator:
         self.meta_host = torch.empty(0, dtype=torch.int32).pin_memory()
         self.topk_host = None
         self.step_timer = None
+        # cascade decode steps replay one CUDA graph (bf16/fp16 pools, page size 16)
+        self.use_graph = (use_graph and kernel_type == "cascade" and page_size == 16
+                          and self.page_table.store_dtype != torch.float32)
+        self.step_graph = None
 
     # ------------------------------------------------------------------
     def generate(self, input_text: str, beam_size: int = 4, max_length: int = 50,
@@ -215,6 +300,29 @@ class BeamSearchGenerator:
             self.attn.plan_tree(v, len(q), dev[4])
         return self.model.forward(dev[0].long(), dev[1], self.page_table, dev[2], dev[3], self.attn)
 
+    def decode_topk(self, state: BeamState, k: int, temperature: float):
+        """One decode step through to the host: (log-prob top-k [beams, k], ids)."""
+        if not self.use_graph:
+            return self._topk(self.decode_step(state), k, temperature)
+        from .cascade import cascade_plan_host
+        q, wp, wpos, pos = state.step_inputs()
+        levels = state.cascade_levels()
+        m = self.model
+        info, plan = cascade_plan_host(levels, len(q), self.page_table.page_size, m.Hq, m.Hkv,
+                                       causal=True, num_sms=self.attn.plan.num_sms)
+        sg = self.step_graph
+        if sg is None or not sg.fits(len(q), k, temperature, info):
+            if info.max_wide_tokens > 256:      # plan outside the fixed kernels' range
+                return self._topk(self.decode_step(state), k, temperature)
+            caps = dict(work=2 * info.n_work + 64, wide=2 * info.n_work_wide + 16,
+                        merge=max(len(q), 1), parts=2 * info.n_parts + 256,
+                        ints=2 * info.total_ints + 4096)
+            if sg is not None:
+                for key in caps:
+                    caps[key] = max(caps[key], sg.caps[key])
+            self.step_graph = sg = StepGraph(self, len(q), k, temperature, caps)
+        return sg.step(q, pos, wp, wpos, plan)
+
     def generate_ids(self, prompts: List[List[int]], beam_size: int = 4,
                      max_length: Optional[int] = None, max_new_tokens: Optional[int] = None,
                      num_return_sequences: int = 1, temperature: float = 1.0, on_step=None):
@@ -249,9 +357,8 @@ class BeamSearchGenerator:
                     break
                 if on_step is not None:
                     on_step(step)
-                logits = self.decode_step(state)
                 k = min(2 * W, V) if W != 1 else 1
-                vals, idx = self._topk(logits, k, temperature)
+                vals, idx = self.decode_topk(state, k, temperature)
                 ptr_all, tok_all, sc_all = [0], [], []
                 new_seg = [0]
                 for p in range(len(prompts)):

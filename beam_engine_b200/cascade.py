@@ -99,7 +99,9 @@ def cascade_plan_host(levels, num_queries, page_size, num_qo_heads, num_kv_heads
                       split_tokens=0, num_sms=148, plan_buf=None):
     """Host planner call on python/numpy level arrays; returns (info, plan ints)."""
     L = len(levels)
-    arrs = [[_i32(lv[k]) for lv in levels] for k in range(4)]
+    keys = ("qo_indptr", "kv_indptr", "kv_indices", "kv_last_page_len")
+    arrs = [[_i32(lv[k] if isinstance(lv, dict) else lv[i]) for lv in levels]
+            for i, k in enumerate(keys)]
     ng = np.asarray([len(a) - 1 for a in arrs[0]], np.int32)
     ptrs = [(_lib.P32 * max(L, 1))(*[_lib.ptr32(a) for a in group]) for group in arrs]
     info = AttnPlanInfo()

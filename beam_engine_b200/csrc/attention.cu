@@ -42,7 +42,22 @@ struct AttnParams {
   float* mid_lse;
   int n_work, n_wide;
   int debug;             // profiling switches (BE_ATTN_DEBUG), 0 in normal runs
+  const int32_t* hdr;    // plan header on the device (fixed-grid launches), else null
 };
+
+// Work / wide-item counts: from the launch when the grid was sized to the
+// plan, from the plan header on the device for fixed (capturable) grids.
+__device__ __forceinline__ int plan_n_work(const AttnParams& p) { return p.hdr ? p.hdr[0] : p.n_work; }
+__device__ __forceinline__ int plan_n_wide(const AttnParams& p) { return p.hdr ? p.hdr[1] : p.n_wide; }
+// Fixed-grid launches pass only the plan base: list pointers come from the
+// header offsets (a kv list override, if any, is already in p.kvlist).
+__device__ __forceinline__ void resolve_plan(AttnParams& p) {
+  if (p.hdr) {
+    p.work = reinterpret_cast<const Work*>(p.hdr + p.hdr[5]);
+    p.qlist = p.hdr + p.hdr[6];
+    if (!p.kvlist) p.kvlist = p.hdr + p.hdr[7];
+  }
+}
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -384,9 +399,11 @@ __device__ void attn_tile(const AttnParams& p, const Work& w, int kvh, char* sme
 template <typename T, int D>
 __global__ void __launch_bounds__(128) attn_tc_kernel(AttnParams p) {
   extern __shared__ __align__(128) char smem[];
+  resolve_plan(p);
+  if ((int)blockIdx.x >= plan_n_work(p)) return;
   const Work w = p.work[blockIdx.x];
   const int kvh = blockIdx.y;
-  if ((int)blockIdx.x < p.n_wide)
+  if ((int)blockIdx.x < plan_n_wide(p))
     attn_tile<T, D, 64>(p, w, kvh, smem);
   else
     attn_tile<T, D, 16>(p, w, kvh, smem);
@@ -395,6 +412,8 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(AttnParams p) {
 // CUDA-core path (fp32 pool): a warp per row, lanes across head_dim.
 template <typename T>
 __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p, int D) {
+  resolve_plan(p);
+  if ((int)blockIdx.x >= plan_n_work(p)) return;
   const Work w = p.work[blockIdx.x];
   const int kvh = blockIdx.y;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -466,15 +485,26 @@ __global__ void __launch_bounds__(128) merge_kernel(const int32_t* __restrict__ 
                                                     const int32_t* __restrict__ mparts, int n_merge,
                                                     const float* __restrict__ mid_o,
                                                     const float* __restrict__ mid_lse, int hq, int D,
-                                                    char* out, int64_t out_row_stride, float* lse) {
+                                                    char* out, int64_t out_row_stride, float* lse,
+                                                    const int32_t* __restrict__ hdr) {
   const int item = blockIdx.x * 4 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  if (hdr) {
+    n_merge = hdr[4];
+    mq = hdr + hdr[8];
+    mptr = hdr + hdr[9];
+    mparts = hdr + hdr[10];
+  }
   if (item >= n_merge * hq) return;
   const int b = item / hq, head = item % hq;
   const int qi = mq[b];
   const int p0 = mptr[b], p1 = mptr[b + 1];
-  float mx = -INFINITY;
-  for (int k = p0 + lane; k < p1; k += 32) mx = fmaxf(mx, mid_lse[(int64_t)mparts[k] * hq + head]);
+  // lane k holds part k's row index and lse (parts beyond 32 are re-read)
+  const int np = p1 - p0;
+  const int my_row = lane < np ? mparts[p0 + lane] : 0;
+  const float my_lse = lane < np ? mid_lse[(int64_t)my_row * hq + head] : -INFINITY;
+  float mx = my_lse;
+  for (int k = p0 + 32 + lane; k < p1; k += 32) mx = fmaxf(mx, mid_lse[(int64_t)mparts[k] * hq + head]);
 #pragma unroll
   for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
   T* dst = reinterpret_cast<T*>(out) + qi * out_row_stride + (int64_t)head * D;
@@ -483,38 +513,43 @@ __global__ void __launch_bounds__(128) merge_kernel(const int32_t* __restrict__ 
     if (lse && lane == 0) lse[(int64_t)qi * hq + head] = -INFINITY;
     return;
   }
-  float den = 0.f;
-  for (int k = p0 + lane; k < p1; k += 32) den += expf(mid_lse[(int64_t)mparts[k] * hq + head] - mx);
+  const float my_w = lane < np ? expf(my_lse - mx) : 0.f;
+  float den = my_w;
+  for (int k = p0 + 32 + lane; k < p1; k += 32) den += expf(mid_lse[(int64_t)mparts[k] * hq + head] - mx);
 #pragma unroll
   for (int off = 16; off; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
   const int nv = D / 4;                 // float4 chunks per row (<= 64)
   float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-  for (int k0 = p0; k0 < p1; k0 += 4) {
-    float wgt[4];
-    const float* src[4];
+  for (int k0 = 0; k0 < np; k0 += 8) {
+    float wgt[8];
+    int64_t row[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 8; ++u) {
       const int k = k0 + u;
-      if (k < p1) {
-        const int64_t pr = (int64_t)mparts[k] * hq + head;
-        wgt[u] = expf(mid_lse[pr] - mx);
-        src[u] = mid_o + pr * D;
+      if (k < 32) {
+        wgt[u] = __shfl_sync(0xffffffffu, my_w, k & 31);
+        row[u] = __shfl_sync(0xffffffffu, my_row, k & 31);
+      } else if (k < np) {
+        row[u] = mparts[p0 + k];
+        wgt[u] = expf(mid_lse[row[u] * hq + head] - mx);
       } else {
         wgt[u] = 0.f;
-        src[u] = nullptr;
+        row[u] = 0;
       }
+      if (k >= np) wgt[u] = 0.f;
     }
-    float4 v[4][2];
+    float4 v[8][2];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < 8; ++u)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = lane + 32 * h;
-        v[u][h] = (src[u] && c < nv) ? __ldg(reinterpret_cast<const float4*>(src[u]) + c)
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[u][h] = (k0 + u < np && c < nv)
+                      ? __ldg(reinterpret_cast<const float4*>(mid_o + (row[u] * hq + head) * D) + c)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < 8; ++u)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         acc[h].x += wgt[u] * v[u][h].x; acc[h].y += wgt[u] * v[u][h].y;
@@ -535,7 +570,7 @@ __global__ void __launch_bounds__(128) merge_kernel(const int32_t* __restrict__ 
 }
 
 template <typename T, int D>
-int launch_tc(const AttnParams& p, cudaStream_t st) {
+int launch_tc(const AttnParams& p, int n_items, cudaStream_t st) {
   const size_t smem = 64 * D * 2 + 2 * 2 * KT * D * 2;
   static bool attr_set = false;  // per process; the attribute is per function
   if (!attr_set) {
@@ -543,7 +578,7 @@ int launch_tc(const AttnParams& p, cudaStream_t st) {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set = true;
   }
-  dim3 grid(p.n_work, p.hkv);
+  dim3 grid(n_items, p.hkv);
   attn_tc_kernel<T, D><<<grid, 128, smem, st>>>(p);
   BE_LAUNCH_CHECK();
   return BE_OK;

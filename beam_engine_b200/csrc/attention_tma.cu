@@ -507,10 +507,17 @@ __global__ void __launch_bounds__(160) attn_tma_kernel(const __grid_constant__ C
   extern __shared__ char smem_raw[];
   char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~uintptr_t(1023));
-  const int wi = w0 + blockIdx.x / cs;
+  resolve_plan(p);
+  // w0 < 0: the wide items ran on the tensor-core kernel; skip them (count from the plan)
+  const int wi = (w0 < 0 ? plan_n_wide(p) : w0) + blockIdx.x / cs;
+  if (wi >= plan_n_work(p)) return;  // whole clusters leave together (same wi)
   const int rank = cs > 1 ? (int)cluster_rank() : 0;
   const Work w = p.work[wi];
-  if (wi < p.n_wide)
+  if (w.flags & BE_WORK_SLOTS) {     // slot lists are not page lists: not for this kernel
+    if (threadIdx.x == 0) flag_range_error();
+    return;
+  }
+  if (wi < plan_n_wide(p))
     tma_tile<T, D, 64>(&tmap, p, w, blockIdx.y, cs, rank, smem);
   else
     tma_tile<T, D, 16>(&tmap, p, w, blockIdx.y, cs, rank, smem);
@@ -605,7 +612,8 @@ static int pick_cluster(const be_attn_plan_info* info, int hkv, int ps) {
 }
 
 template <typename T, int D>
-int launch_tma(const AttnParams& p, const CUtensorMap& map, int cs, int w0, cudaStream_t st) {
+int launch_tma(const AttnParams& p, const CUtensorMap& map, int cs, int w0, int n_items,
+               cudaStream_t st) {
   const size_t smem = tma_smem_bytes<D>();
   static bool set = false;
   if (!set) {
@@ -614,7 +622,7 @@ int launch_tma(const AttnParams& p, const CUtensorMap& map, int cs, int w0, cuda
     set = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.n_work - w0) * cs, p.hkv, 1);
+  cfg.gridDim = dim3(n_items * cs, p.hkv, 1);
   cfg.blockDim = dim3(160, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;

@@ -94,7 +94,13 @@ __global__ void __launch_bounds__(160) attn_umma_kernel(const __grid_constant__ 
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 5);
 
+  resolve_plan(p);
+  if ((int)blockIdx.x >= plan_n_wide(p)) return;  // before any barrier or TMEM use
   const Work w = p.work[blockIdx.x];
+  if (w.kv_end - w.kv_begin > UM_MAX_TOK || (w.flags & BE_WORK_SLOTS)) {  // not made for this kernel
+    if (threadIdx.x == 0) flag_range_error();
+    return;
+  }
   const int kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = p.g, rows = w.q_len * g, ps = p.page_size;
@@ -313,7 +319,7 @@ __global__ void __launch_bounds__(160) attn_umma_kernel(const __grid_constant__ 
 }
 
 template <typename T, int D>
-int launch_umma(const AttnParams& p, const CUtensorMap& map, cudaStream_t st) {
+int launch_umma(const AttnParams& p, const CUtensorMap& map, int n_items, cudaStream_t st) {
   const size_t smem = um_smem_bytes();
   static bool set = false;
   if (!set) {
@@ -321,7 +327,7 @@ int launch_umma(const AttnParams& p, const CUtensorMap& map, cudaStream_t st) {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     set = true;
   }
-  attn_umma_kernel<T, D><<<dim3(p.n_wide, p.hkv), 160, smem, st>>>(map, p);
+  attn_umma_kernel<T, D><<<dim3(n_items, p.hkv), 160, smem, st>>>(map, p);
   BE_LAUNCH_CHECK();
   return BE_OK;
 }

@@ -1,57 +1,109 @@
-// be_attn_run: dispatch between the TMA-fed kernel (bf16/fp16, page lists,
-// page size 16, head_dim 64/128), the cp.async tensor-core kernel (other
-// 2-byte cases, slot lists) and the CUDA-core kernel (fp32), then the LSE merge.
+// be_attn_run / be_attn_run_fixed: dispatch between the tcgen05 kernel (wide
+// tiles, bf16/fp16, page lists, page size 16, head_dim 64/128), the TMA-fed
+// mma.sync kernel (narrow tiles), the cp.async tensor-core kernel (other 2-byte
+// cases, slot lists) and the CUDA-core kernel (fp32), then the LSE merge.
 #include "common.cuh"
 
 namespace be {
 
+struct Caps {                // grid sizes; fixed = true: counts come from the plan header
+  int work, wide, merge, cluster;
+  bool fixed;
+};
+
 template <typename T>
 int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t* plan, int D,
-               cudaStream_t st) {
-  if (p.n_work > 0) {
+               const Caps& c, cudaStream_t st) {
+  if (c.work > 0) {
     int rc = BE_OK;
     if constexpr (sizeof(T) == 2) {
-      const bool tma_ok = !info->any_slots && info->page_size == 16 && (D == 128 || D == 64) &&
-                          !force_cp_async();
+      const bool tma_ok = (c.fixed || (!info->any_slots && info->page_size == 16)) &&
+                          p.page_size == 16 && (D == 128 || D == 64) && !force_cp_async();
       if (tma_ok) {
         CUtensorMap map;
         rc = get_pool_map(p.pool, p.num_pages, p.page_size, p.hkv, D, DT<T>::id, &map);
         if (rc != BE_OK) return rc;
-        const int cs = pick_cluster(info, p.hkv, p.page_size);
+        const int cs = c.fixed ? std::max(1, c.cluster) : pick_cluster(info, p.hkv, p.page_size);
         // wide tiles (shared prefixes) on tcgen05 when their chunks fit TMEM/smem
-        const bool umma = umma_enabled() && p.n_wide > 0 && info->max_wide_tokens <= UM_MAX_TOK &&
-                          ((uintptr_t)p.out % 16 == 0) && (p.out_row_stride % 8 == 0);
-        int w0 = 0;
+        const bool aligned = ((uintptr_t)p.out % 16 == 0) && (p.out_row_stride % 8 == 0);
+        const bool umma = umma_enabled() && aligned && c.wide > 0 &&
+                          (c.fixed || info->max_wide_tokens <= UM_MAX_TOK);
+        int w0 = 0, n_items = c.work;
         if (umma) {
-          rc = D == 128 ? launch_umma<T, 128>(p, map, st) : launch_umma<T, 64>(p, map, st);
+          rc = D == 128 ? launch_umma<T, 128>(p, map, c.wide, st)
+                        : launch_umma<T, 64>(p, map, c.wide, st);
           if (rc != BE_OK) return rc;
-          w0 = p.n_wide;
+          w0 = c.fixed ? -1 : p.n_wide;
+          n_items = c.fixed ? c.work : p.n_work - p.n_wide;
         }
-        if (p.n_work > w0)
-          rc = D == 128 ? launch_tma<T, 128>(p, map, cs, w0, st)
-                        : launch_tma<T, 64>(p, map, cs, w0, st);
-      } else if (D == 128) rc = launch_tc<T, 128>(p, st);
-      else if (D == 64) rc = launch_tc<T, 64>(p, st);
-      else {
-        dim3 grid(p.n_work, p.hkv);
-        attn_simt_kernel<T><<<grid, 128, 0, st>>>(p, D);
+        if (n_items > 0)
+          rc = D == 128 ? launch_tma<T, 128>(p, map, cs, w0, n_items, st)
+                        : launch_tma<T, 64>(p, map, cs, w0, n_items, st);
+      } else if (D == 128) {
+        rc = launch_tc<T, 128>(p, c.work, st);
+      } else if (D == 64) {
+        rc = launch_tc<T, 64>(p, c.work, st);
+      } else {
+        attn_simt_kernel<T><<<dim3(c.work, p.hkv), 128, 0, st>>>(p, D);
         BE_LAUNCH_CHECK();
       }
     } else {
-      dim3 grid(p.n_work, p.hkv);
-      attn_simt_kernel<T><<<grid, 128, 0, st>>>(p, D);
+      attn_simt_kernel<T><<<dim3(c.work, p.hkv), 128, 0, st>>>(p, D);
       BE_LAUNCH_CHECK();
     }
     if (rc != BE_OK) return rc;
   }
-  if (info->n_merge > 0) {
-    const int items = info->n_merge * p.hq;
+  if (c.merge > 0) {
+    const int items = c.merge * p.hq;
+    const bool dev = c.fixed;
     merge_kernel<T><<<(items + 3) / 4, 128, 0, st>>>(
-        plan + info->off_merge_q, plan + info->off_merge_ptr, plan + info->off_merge_parts,
-        info->n_merge, p.mid_o, p.mid_lse, p.hq, D, p.out, p.out_row_stride, p.lse);
+        dev ? nullptr : plan + info->off_merge_q, dev ? nullptr : plan + info->off_merge_ptr,
+        dev ? nullptr : plan + info->off_merge_parts, c.merge, p.mid_o, p.mid_lse, p.hq, D, p.out,
+        p.out_row_stride, p.lse, dev ? plan : nullptr);
     BE_LAUNCH_CHECK();
   }
   return BE_OK;
+}
+
+static int check_heads(int num_qo_heads, int num_kv_heads, int head_dim, int dtype) {
+  if (num_kv_heads < 1 || num_qo_heads % num_kv_heads || head_dim < 8 || head_dim > 256 ||
+      head_dim % 8 || dtype < BE_F32 || dtype > BE_BF16) {
+    set_error("be_attn_run: bad head configuration (Hq %d, Hkv %d, D %d)", num_qo_heads,
+              num_kv_heads, head_dim);
+    return BE_EINVAL;
+  }
+  return BE_OK;
+}
+
+static void fill_params(AttnParams& p, const void* q, int64_t q_row_stride,
+                        const void* paged_kv_cache, int num_pages, int page_size, int hq, int hkv,
+                        float sm_scale, void* out, int64_t out_row_stride, float* lse,
+                        float* mid_o, float* mid_lse) {
+  p.q = (const char*)q;
+  p.q_row_stride = q_row_stride;
+  p.pool = (const char*)paged_kv_cache;
+  p.num_pages = num_pages;
+  p.page_size = page_size;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.g = hq / hkv;
+  p.scale_log2 = sm_scale * kLog2e;
+  p.out = (char*)out;
+  p.out_row_stride = out_row_stride;
+  p.lse = lse;
+  p.mid_o = mid_o;
+  p.mid_lse = mid_lse;
+  const char* e = getenv("BE_ATTN_DEBUG");
+  p.debug = e ? atoi(e) : 0;
+}
+
+template <typename... A>
+static int dispatch(int dtype, A&&... a) {
+  switch (dtype) {
+    case BE_BF16: return launch_all<__nv_bfloat16>(a...);
+    case BE_F16: return launch_all<__half>(a...);
+    default: return launch_all<float>(a...);
+  }
 }
 
 }  // namespace be
@@ -68,12 +120,8 @@ extern "C" int be_attn_run(const int32_t* plan_dev, const be_attn_plan_info* inf
     set_error("be_attn_run: null pointer");
     return BE_EINVAL;
   }
-  if (num_kv_heads < 1 || num_qo_heads % num_kv_heads || head_dim < 8 || head_dim > 256 ||
-      head_dim % 8 || dtype < BE_F32 || dtype > BE_BF16) {
-    set_error("be_attn_run: bad head configuration (Hq %d, Hkv %d, D %d)", num_qo_heads,
-              num_kv_heads, head_dim);
-    return BE_EINVAL;
-  }
+  int rc = check_heads(num_qo_heads, num_kv_heads, head_dim, dtype);
+  if (rc) return rc;
   if (info->group_size != num_qo_heads / num_kv_heads) {
     set_error("be_attn_run: plan group size %d != Hq/Hkv %d", info->group_size,
               num_qo_heads / num_kv_heads);
@@ -89,33 +137,49 @@ extern "C" int be_attn_run(const int32_t* plan_dev, const be_attn_plan_info* inf
     return BE_EINVAL;
   }
   AttnParams p;
+  fill_params(p, q, q_row_stride, paged_kv_cache, num_pages, info->page_size, num_qo_heads,
+              num_kv_heads, sm_scale, out, out_row_stride, lse, mid_o, mid_lse);
+  p.hdr = nullptr;
   p.work = reinterpret_cast<const Work*>(plan_dev + info->off_work);
   p.qlist = plan_dev + info->off_qlist;
   p.kvlist = kv_list_override ? kv_list_override : plan_dev + info->off_kvlist;
-  p.q = (const char*)q;
-  p.q_row_stride = q_row_stride;
-  p.pool = (const char*)paged_kv_cache;
-  p.num_pages = num_pages;
-  p.page_size = info->page_size;
-  p.hq = num_qo_heads;
-  p.hkv = num_kv_heads;
-  p.g = num_qo_heads / num_kv_heads;
-  p.scale_log2 = sm_scale * kLog2e;
-  p.out = (char*)out;
-  p.out_row_stride = out_row_stride;
-  p.lse = lse;
-  p.mid_o = mid_o;
-  p.mid_lse = mid_lse;
   p.n_work = info->n_work;
   p.n_wide = info->n_work_wide;
-  {
-    const char* e = getenv("BE_ATTN_DEBUG");
-    p.debug = e ? atoi(e) : 0;
+  const Caps c{info->n_work, info->n_work_wide, info->n_merge, 0, false};
+  return dispatch(dtype, p, info, plan_dev, head_dim, c, (cudaStream_t)stream);
+}
+
+extern "C" int be_attn_run_fixed(const int32_t* plan_dev, const be_attn_caps* caps, int page_size,
+                                 const void* q, int64_t q_row_stride, const void* paged_kv_cache,
+                                 int num_pages, int num_qo_heads, int num_kv_heads, int head_dim,
+                                 int dtype, float sm_scale, void* out, int64_t out_row_stride,
+                                 float* lse, float* mid_o, float* mid_lse,
+                                 const int32_t* kv_list_override, void* stream) {
+  if (!plan_dev || !caps || !q || !paged_kv_cache || !out || !mid_o || !mid_lse) {
+    set_error("be_attn_run_fixed: null pointer");
+    return BE_EINVAL;
   }
-  cudaStream_t st = (cudaStream_t)stream;
-  switch (dtype) {
-    case BE_BF16: return launch_all<__nv_bfloat16>(p, info, plan_dev, head_dim, st);
-    case BE_F16: return launch_all<__half>(p, info, plan_dev, head_dim, st);
-    default: return launch_all<float>(p, info, plan_dev, head_dim, st);
+  int rc = check_heads(num_qo_heads, num_kv_heads, head_dim, dtype);
+  if (rc) return rc;
+  if (caps->max_work < 0 || caps->max_wide < 0 || caps->max_wide > caps->max_work ||
+      caps->max_merge < 0 || caps->cluster < 0 || caps->cluster > 8 || page_size < 1) {
+    set_error("be_attn_run_fixed: invalid caps");
+    return BE_EINVAL;
   }
+  if (dtype != BE_F32 && (((uintptr_t)q | (uintptr_t)paged_kv_cache) % 16 ||
+                          (q_row_stride * 2) % 16)) {
+    set_error("be_attn_run_fixed: q and the pool must be 16-byte aligned");
+    return BE_EINVAL;
+  }
+  AttnParams p;
+  fill_params(p, q, q_row_stride, paged_kv_cache, num_pages, page_size, num_qo_heads,
+              num_kv_heads, sm_scale, out, out_row_stride, lse, mid_o, mid_lse);
+  p.hdr = plan_dev;
+  p.work = nullptr;
+  p.qlist = nullptr;
+  p.kvlist = kv_list_override;  // null: the plan's own list
+  p.n_work = caps->max_work;
+  p.n_wide = caps->max_wide;
+  const Caps c{caps->max_work, caps->max_wide, caps->max_merge, caps->cluster, true};
+  return dispatch(dtype, p, nullptr, plan_dev, head_dim, c, (cudaStream_t)stream);
 }

@@ -13,6 +13,8 @@
 
 #include "beam_b200.h"
 
+static_assert(sizeof(be_attn_plan_info) <= BE_PLAN_HEADER_INTS * sizeof(int32_t), "header");
+
 namespace be {
 
 static thread_local char g_err[512] = "";
@@ -81,8 +83,8 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
   in.n_queries = num_queries;
   in.n_parts = n_parts;
   in.n_merge = (int32_t)mq.size();
-  int64_t off = 0;
-  in.off_work = 0;
+  int64_t off = BE_PLAN_HEADER_INTS;   // the header (this struct) leads the buffer
+  in.off_work = (int32_t)off;
   off += (int64_t)items.size() * 8;
   in.off_qlist = (int32_t)off;
   off += qlist.size();
@@ -113,7 +115,9 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
     set_error("plan buffer too small: need %lld ints, have %lld", (long long)off, (long long)cap);
     return BE_ECAPACITY;
   }
-  int32_t* p = plan;
+  std::memset(plan, 0, BE_PLAN_HEADER_INTS * sizeof(int32_t));
+  std::memcpy(plan, &in, sizeof(in));
+  int32_t* p = plan + BE_PLAN_HEADER_INTS;
   for (auto& it : items) {
     std::memcpy(p, &it.w, sizeof(be_attn_work));
     p += 8;
@@ -210,8 +214,8 @@ extern "C" int be_cascade_plan(int num_levels, const int32_t* const* qo_indptr,
     } else {
       const int min_chunk = round_pages((int64_t)std::min(gr.qlen, tq) * g * 8);
       chunk = std::max(min_chunk, balanced);
-      // wide tiles run as one resident tensor-core tile of at most 256 tokens
-      if (wide) chunk = std::min(chunk, 256);
+      // decode-time wide tiles run as one resident tensor-core tile of <= 256 tokens
+      if (wide && !causal) chunk = std::min(chunk, 256);
       const int nsplit = (gr.kv_len + chunk - 1) / chunk;
       chunk = round_pages((gr.kv_len + nsplit - 1) / nsplit);
     }
@@ -296,8 +300,8 @@ extern "C" int be_tree_plan(int num_vnodes, const int32_t* q_entries, int num_q_
   in.n_queries = batch_size;
   in.n_parts = num_q_entries;
   in.n_merge = batch_size;
-  int64_t off = (int64_t)items.size() * 8;
-  in.off_work = 0;
+  int64_t off = BE_PLAN_HEADER_INTS + (int64_t)items.size() * 8;
+  in.off_work = BE_PLAN_HEADER_INTS;
   in.off_qlist = (int32_t)off;
   off += qlist.size();
   in.off_kvlist = (int32_t)off;
@@ -323,7 +327,9 @@ extern "C" int be_tree_plan(int num_vnodes, const int32_t* q_entries, int num_q_
               (long long)plan_capacity);
     return BE_ECAPACITY;
   }
-  int32_t* p = plan;
+  std::memset(plan, 0, BE_PLAN_HEADER_INTS * sizeof(int32_t));
+  std::memcpy(plan, &in, sizeof(in));
+  int32_t* p = plan + BE_PLAN_HEADER_INTS;
   for (auto& it : items) {
     it.w.part_base = it.w.q_off;
     std::memcpy(p, &it.w, sizeof(be_attn_work));

@@ -95,6 +95,10 @@ typedef struct {
   int32_t flags;     /* BE_WORK_CAUSAL | BE_WORK_SLOTS                         */
 } be_attn_work;
 
+/* Every plan buffer starts with a copy of its be_attn_plan_info, padded to
+ * BE_PLAN_HEADER_INTS ints, so kernels can read the counts on the device. */
+#define BE_PLAN_HEADER_INTS 32
+
 #define BE_WORK_CAUSAL 1 /* query i sees tokens t < kv_total - q_len + i + 1 */
 #define BE_WORK_SLOTS 2  /* KV list holds slot ids (page*page_size+i), else page ids */
 
@@ -159,6 +163,31 @@ int be_attn_run(const int32_t* plan_dev, const be_attn_plan_info* info, const vo
                 int num_qo_heads, int num_kv_heads, int head_dim, int dtype, float sm_scale,
                 void* out, int64_t out_row_stride, float* lse, float* mid_o, float* mid_lse,
                 const int32_t* kv_list_override, void* stream);
+
+/* Grid capacities of be_attn_run_fixed.  The launch configuration depends on
+ * these only, so the call can be recorded once (e.g. in a CUDA graph) and
+ * replayed with any plan that fits: the kernels read the plan's real counts
+ * from its device-side header and idle the surplus CTAs.                     */
+typedef struct {
+  int32_t max_work;   /* >= n_work of every plan run this way                  */
+  int32_t max_wide;   /* >= n_work_wide                                         */
+  int32_t max_merge;  /* >= n_merge                                             */
+  int32_t cluster;    /* CTAs per work item for narrow tiles (1..8)             */
+} be_attn_caps;
+
+/* be_attn_run with a launch shape fixed by `caps` instead of a host-side plan
+ * description: the plan at plan_dev (header included) may change between
+ * calls without any host involvement.  Page-list plans with page size 16 use
+ * the tensor-core kernels; wide items must span <= 256 tokens (the planner's
+ * decode chunks do); a plan that breaks the caps is flagged in the device
+ * status and its surplus items are skipped.  Same contract as
+ * MultiLevelCascadeAttentionWrapper.run (modeling_llama.py:362).            */
+int be_attn_run_fixed(const int32_t* plan_dev, const be_attn_caps* caps, int page_size,
+                      const void* q, int64_t q_row_stride, const void* paged_kv_cache,
+                      int num_pages, int num_qo_heads, int num_kv_heads, int head_dim, int dtype,
+                      float sm_scale, void* out, int64_t out_row_stride, float* lse,
+                      float* mid_o, float* mid_lse, const int32_t* kv_list_override,
+                      void* stream);
 
 /* ------------------------------------------------------------------------
  * Decoder-layer kernels of the model runner (the reference runs these as
