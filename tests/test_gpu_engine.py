@@ -87,3 +87,27 @@ def test_multi_prompt_batch_matches_single_runs():
         outs.append(gen.generate_ids(prompts, 4, max_new_tokens=20, num_return_sequences=4))
     assert [s for s, _ in outs[0][0]] == [s for s, _ in outs[1][0]]
     assert [s for s, _ in outs[0][1]] == [s for s, _ in outs[2][0]]
+
+
+def test_graph_step_matches_eager_bf16():
+    """The CUDA-graph decode step (fixed-shape attention launches, plan on the
+    device) selects the same beams as the eager step."""
+    from beam_engine_b200.beam import BeamSearchGenerator
+    from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy
+    from beam_engine_b200.configs import TINY
+    from beam_engine_b200.llama import BeamLlama
+    cfg = dict(TINY, head_dim=128, num_attention_heads=4, num_key_value_heads=2, hidden_size=512)
+    model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=dev(), seed=3)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, 1024, (70,), generator=g).tolist() for _ in range(3)]
+    outs = []
+    for graph in (False, True):
+        gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=16,
+                                  max_num_pages=512, use_graph=graph)
+        outs.append(gen.generate_ids(prompts, 8, max_new_tokens=24, num_return_sequences=8))
+        assert gen.use_graph == graph
+        if graph:
+            assert gen.step_graph is not None and gen.step_graph.graph is not None
+    for a, b in zip(*outs):
+        assert [s for s, _ in a] == [s for s, _ in b]
+        np.testing.assert_allclose([x for _, x in a], [x for _, x in b], rtol=1e-6)
