@@ -6,4 +6,5 @@
 #include "attention_tma.cu"
 #include "attention_umma.cu"
 #include "attn_api.cu"
+#include "attn_noalloc.cu"
 #include "model_ops.cu"

@@ -164,6 +164,25 @@ int be_attn_run(const int32_t* plan_dev, const be_attn_plan_info* info, const vo
                 void* out, int64_t out_row_stride, float* lse, float* mid_o, float* mid_lse,
                 const int32_t* kv_list_override, void* stream);
 
+/* be_attn_run for callers that cannot allocate device memory.  No counterpart
+ * in the reference (which always lets FlashInfer use a caller workspace).
+ * Same arguments as be_attn_run minus mid_o / mid_lse: the partial rows go to
+ * an array compiled into this library, BE_NOALLOC_SCRATCH_BYTES per device,
+ * reserved on every GPU that loads the library until the process exits.
+ *   - Plans needing more partial-row space (n_parts * Hq * (D + 1) * 4 bytes,
+ *     roughly) fail with BE_ECAPACITY and a message; nothing is allocated.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls share the one array: calls whose work overlaps on the GPU
+ *     (different streams, or devices sharing a context) race and corrupt each
+ *     other's results; serialise them.                                        */
+#define BE_NOALLOC_SCRATCH_BYTES (16u << 20)
+int be_attn_run_noalloc(const int32_t* plan_dev, const be_attn_plan_info* info, const void* q,
+                        int64_t q_row_stride, const void* paged_kv_cache, int num_pages,
+                        int num_qo_heads, int num_kv_heads, int head_dim, int dtype, float sm_scale,
+                        void* out, int64_t out_row_stride, float* lse,
+                        const int32_t* kv_list_override, void* stream);
+
 /* Grid capacities of be_attn_run_fixed.  The launch configuration depends on
  * these only, so the call can be recorded once (e.g. in a CUDA graph) and
  * replayed with any plan that fits: the kernels read the plan's real counts
