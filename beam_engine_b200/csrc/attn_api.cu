@@ -28,6 +28,7 @@ int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t
         const bool aligned = ((uintptr_t)p.out % 16 == 0) && (p.out_row_stride % 8 == 0);
         const bool umma = umma_enabled() && aligned && c.wide > 0 &&
                           (c.fixed || info->max_wide_tokens <= UM_MAX_TOK);
+        const bool narrow = narrow_enabled() && p.hkv <= 8 && (umma || !c.fixed);
         int w0 = 0, n_items = c.work;
         if (umma) {
           rc = D == 128 ? launch_umma<T, 128>(p, map, c.wide, st)
@@ -35,8 +36,20 @@ int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t
           if (rc != BE_OK) return rc;
           w0 = c.fixed ? -1 : p.n_wide;
           n_items = c.fixed ? c.work : p.n_work - p.n_wide;
+        } else if (narrow) {   // host-sized grid: wide items [0, n_wide) on the mma.sync kernel
+          if (p.n_wide > 0) {
+            rc = D == 128 ? launch_tma<T, 128>(p, map, cs, 0, p.n_wide, st)
+                          : launch_tma<T, 64>(p, map, cs, 0, p.n_wide, st);
+            if (rc != BE_OK) return rc;
+          }
+          w0 = p.n_wide;
+          n_items = p.n_work - p.n_wide;
         }
-        if (n_items > 0)
+        // narrow tiles: one CTA per item with every KV head
+        if (n_items > 0 && narrow)
+          rc = D == 128 ? launch_narrow<T, 128>(p, map, w0, n_items, st)
+                        : launch_narrow<T, 64>(p, map, w0, n_items, st);
+        else if (n_items > 0)
           rc = D == 128 ? launch_tma<T, 128>(p, map, cs, w0, n_items, st)
                         : launch_tma<T, 64>(p, map, cs, w0, n_items, st);
       } else if (D == 128) {
