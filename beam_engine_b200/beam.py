@@ -120,6 +120,16 @@ class StepGraph:
         self.idx_h = torch.empty(n * k, dtype=torch.int64).pin_memory()
         self.ccaps = _lib.AttnCaps(self.caps["work"], self.caps["wide"], self.caps["merge"], 1)
         self.graph = None
+        # optional per-layer attention timing inside the graph (external event nodes)
+        self.timing = bool(getattr(gen, "time_attention", False))
+        self.events = None
+        if self.timing:
+            from cuda.bindings import runtime as rt
+            self._rt = rt
+            self.events = []
+            for _ in range(2 * m.L):
+                err, ev = rt.cudaEventCreate()
+                self.events.append(ev)
 
     def fits(self, n, k, temperature, info):
         c = self.caps
@@ -128,14 +138,30 @@ class StepGraph:
                 and info.n_merge <= c["merge"] and info.n_parts <= c["parts"]
                 and info.total_ints <= c["ints"] and info.max_wide_tokens <= 256)
 
+    def _mark(self, idx, qkv):
+        if self.timing and torch.cuda.is_current_stream_capturing():
+            self._rt.cudaEventRecordWithFlags(self.events[idx],
+                                              torch.cuda.current_stream(qkv.device).cuda_stream,
+                                              self._rt.cudaEventRecordExternal)
+
+    def attention_ms(self):
+        """Per-layer attention durations (ms) of the last replay."""
+        out = []
+        for i in range(len(self.events) // 2):
+            err, ms = self._rt.cudaEventElapsedTime(self.events[2 * i], self.events[2 * i + 1])
+            out.append(float(ms))
+        return out
+
     def run(self, layer, qkv, out):  # attention of one layer (the model calls this)
         m, pt = self.gen.model, self.gen.page_table
+        self._mark(2 * layer, qkv)
         rc = lib().be_attn_run_fixed(
             self.dev_buf.data_ptr() + 4 * self.plan_off, C.byref(self.ccaps), pt.page_size,
             qkv.data_ptr(), qkv.stride(0), pt.kv_cache[layer].data_ptr(), pt.max_num_pages, m.Hq,
             m.Hkv, m.D, m.dt, m.D ** -0.5, out.data_ptr(), out.stride(0), None,
             self.mid_o.data_ptr(), self.mid_lse.data_ptr(), None, stream_ptr(qkv.device))
         check(rc, "be_attn_run_fixed")
+        self._mark(2 * layer + 1, qkv)
 
     def _body(self):
         n = self.n
@@ -169,6 +195,8 @@ class StepGraph:
             self.graph = g
         self.graph.replay()
         torch.cuda.current_stream(self.gen.device).synchronize()
+        if self.timing and self.gen.attn_times is not None:
+            self.gen.attn_times.extend(self.attention_ms())
         k = self.k
         return (self.vals_h.numpy()[:n * k].reshape(n, k).astype(np.float64),
                 self.idx_h.numpy()[:n * k].reshape(n, k).astype(np.int32))
@@ -202,6 +230,9 @@ class BeamSearchGenerator:
         self.use_graph = (use_graph and kernel_type == "cascade" and page_size == 16
                           and self.page_table.store_dtype != torch.float32)
         self.step_graph = None
+        self.time_attention = False   # record per-layer attention events in the step graph
+        self.attn_times = None        # list to collect them into (ms per launch) when set
+        self.plan_hook = None         # called with (levels, plan info) per graph step
 
     # ------------------------------------------------------------------
     def generate(self, input_text: str, beam_size: int = 4, max_length: int = 50,
@@ -310,6 +341,8 @@ class BeamSearchGenerator:
         m = self.model
         info, plan = cascade_plan_host(levels, len(q), self.page_table.page_size, m.Hq, m.Hkv,
                                        causal=True, num_sms=self.attn.plan.num_sms)
+        if self.plan_hook is not None:
+            self.plan_hook(levels, info)
         sg = self.step_graph
         if sg is None or not sg.fits(len(q), k, temperature, info):
             if info.max_wide_tokens > 256:      # plan outside the fixed kernels' range
