@@ -28,6 +28,7 @@ from .cascade import _Plan
 from .page_table import PageTable, stream_ptr
 
 logger = logging.getLogger(__name__)
+UMMA_MAX_TOKENS = 128   # BE_UMMA_MAX_TOKENS in include/beam_b200.h
 
 
 def _i32(a):
@@ -136,7 +137,7 @@ class StepGraph:
         return (n == self.n and k == self.k and temperature == self.temp
                 and info.n_work <= c["work"] and info.n_work_wide <= c["wide"]
                 and info.n_merge <= c["merge"] and info.n_parts <= c["parts"]
-                and info.total_ints <= c["ints"] and info.max_wide_tokens <= 256)
+                and info.total_ints <= c["ints"] and info.max_wide_tokens <= UMMA_MAX_TOKENS)
 
     def _mark(self, idx, qkv):
         if self.timing and torch.cuda.is_current_stream_capturing():
@@ -345,7 +346,7 @@ class BeamSearchGenerator:
             self.plan_hook(levels, info)
         sg = self.step_graph
         if sg is None or not sg.fits(len(q), k, temperature, info):
-            if info.max_wide_tokens > 256:      # plan outside the fixed kernels' range
+            if info.max_wide_tokens > UMMA_MAX_TOKENS:   # plan outside the fixed kernels' range
                 return self._topk(self.decode_step(state), k, temperature)
             caps = dict(work=2 * info.n_work + 64, wide=2 * info.n_work_wide + 16,
                         merge=max(len(q), 1), parts=2 * info.n_parts + 256,

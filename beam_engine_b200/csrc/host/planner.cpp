@@ -214,8 +214,8 @@ extern "C" int be_cascade_plan(int num_levels, const int32_t* const* qo_indptr,
     } else {
       const int min_chunk = round_pages((int64_t)std::min(gr.qlen, tq) * g * 8);
       chunk = std::max(min_chunk, balanced);
-      // decode-time wide tiles run as one resident tensor-core tile of <= 256 tokens
-      if (wide && !causal) chunk = std::min(chunk, 256);
+      // decode-time wide tiles run as one resident tensor-core tile
+      if (wide && !causal) chunk = std::min(chunk, BE_UMMA_MAX_TOKENS);
       const int nsplit = (gr.kv_len + chunk - 1) / chunk;
       chunk = round_pages((gr.kv_len + nsplit - 1) / nsplit);
     }

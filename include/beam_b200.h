@@ -99,6 +99,10 @@ typedef struct {
  * BE_PLAN_HEADER_INTS ints, so kernels can read the counts on the device. */
 #define BE_PLAN_HEADER_INTS 32
 
+/* Longest wide (shared-prefix) work item the tensor-core kernel takes; the
+ * cascade planner cuts decode-time prefix chunks to this length. */
+#define BE_UMMA_MAX_TOKENS 128
+
 #define BE_WORK_CAUSAL 1 /* query i sees tokens t < kv_total - q_len + i + 1 */
 #define BE_WORK_SLOTS 2  /* KV list holds slot ids (page*page_size+i), else page ids */
 
