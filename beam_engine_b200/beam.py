@@ -176,12 +176,9 @@ class StepGraph:
         self.vals_h.copy_(v.reshape(-1), non_blocking=True)
         self.idx_h.copy_(i.reshape(-1), non_blocking=True)
 
-    def step(self, q, pos, wp, wpos, plan):
+    def step_filled(self, used):
+        """Replay with host_buf[:used] already holding [q | pos | pages | slots | plan]."""
         n = self.n
-        h = self.host_buf.numpy()
-        h[0:n], h[n:2 * n], h[2 * n:3 * n], h[3 * n:4 * n] = q, pos, wp, wpos
-        h[self.plan_off:self.plan_off + len(plan)] = plan
-        used = self.plan_off + len(plan)
         self.dev_buf[:used].copy_(self.host_buf[:used], non_blocking=True)
         if self.graph is None:
             cur = torch.cuda.current_stream(self.gen.device)
@@ -233,7 +230,7 @@ class BeamSearchGenerator:
         self.step_graph = None
         self.time_attention = False   # record per-layer attention events in the step graph
         self.attn_times = None        # list to collect them into (ms per launch) when set
-        self.plan_hook = None         # called with (levels, plan info) per graph step
+        self.plan_hook = None         # called with (queries, plan info) per graph step
 
     # ------------------------------------------------------------------
     def generate(self, input_text: str, beam_size: int = 4, max_length: int = 50,
@@ -336,26 +333,45 @@ class BeamSearchGenerator:
         """One decode step through to the host: (log-prob top-k [beams, k], ids)."""
         if not self.use_graph:
             return self._topk(self.decode_step(state), k, temperature)
-        from .cascade import cascade_plan_host
-        q, wp, wpos, pos = state.step_inputs()
-        levels = state.cascade_levels()
         m = self.model
-        info, plan = cascade_plan_host(levels, len(q), self.page_table.page_size, m.Hq, m.Hkv,
-                                       causal=True, num_sms=self.attn.plan.num_sms)
-        if self.plan_hook is not None:
-            self.plan_hook(levels, info)
+        n = len(state.leaves)
+        leaves = np.ascontiguousarray(state.leaves, np.int32)
+        info = _lib.AttnPlanInfo()
         sg = self.step_graph
-        if sg is None or not sg.fits(len(q), k, temperature, info):
-            if info.max_wide_tokens > UMMA_MAX_TOKENS:   # plan outside the fixed kernels' range
+
+        def fill(buf_ptr, cap, plan_off):
+            rc = lib().be_beam_decode_inputs(self.page_table._trie, n, _lib.ptr32(leaves), m.Hq,
+                                             m.Hkv, self.attn.plan.num_sms, C.c_void_p(buf_ptr),
+                                             cap, plan_off, C.byref(info))
+            if rc not in (_lib.BE_OK, _lib.BE_ECAPACITY):
+                check(rc, "be_beam_decode_inputs")
+            return rc == _lib.BE_OK
+
+        if not (sg is not None and sg.n == n and sg.k == k and sg.temp == temperature
+                and fill(sg.host_buf.data_ptr(), sg.total, sg.plan_off)
+                and sg.fits(n, k, temperature, info)):
+            # size a new graph from this step's plan (grow the probe buffer until it fits)
+            off = -(-4 * n // 32) * 32
+            size = off + 65536
+            while True:
+                probe = np.empty(size, np.int32)
+                if fill(probe.ctypes.data, size, off):
+                    break
+                size *= 4
+            if info.max_wide_tokens > UMMA_MAX_TOKENS:   # outside the fixed kernels' range
                 return self._topk(self.decode_step(state), k, temperature)
             caps = dict(work=2 * info.n_work + 64, wide=2 * info.n_work_wide + 16,
-                        merge=max(len(q), 1), parts=2 * info.n_parts + 256,
+                        merge=max(n, 1), parts=2 * info.n_parts + 256,
                         ints=2 * info.total_ints + 4096)
-            if sg is not None:
+            if sg is not None and sg.n == n and sg.k == k and sg.temp == temperature:
                 for key in caps:
                     caps[key] = max(caps[key], sg.caps[key])
-            self.step_graph = sg = StepGraph(self, len(q), k, temperature, caps)
-        return sg.step(q, pos, wp, wpos, plan)
+            self.step_graph = sg = StepGraph(self, n, k, temperature, caps)
+            if not fill(sg.host_buf.data_ptr(), sg.total, sg.plan_off):
+                raise RuntimeError("decode step graph sized too small for its own plan")
+        if self.plan_hook is not None:
+            self.plan_hook(n, info)
+        return sg.step_filled(sg.plan_off + info.total_ints)
 
     def generate_ids(self, prompts: List[List[int]], beam_size: int = 4,
                      max_length: Optional[int] = None, max_new_tokens: Optional[int] = None,
@@ -393,17 +409,22 @@ class BeamSearchGenerator:
                     on_step(step)
                 k = min(2 * W, V) if W != 1 else 1
                 vals, idx = self.decode_topk(state, k, temperature)
-                ptr_all, tok_all, sc_all = [0], [], []
-                new_seg = [0]
-                for p in range(len(prompts)):
-                    a, b = seg[p], seg[p + 1]
-                    cp, ct, cs = self.strategy.select_arrays(state.scores[a:b], idx[a:b], vals[a:b], W)
-                    ptr_all.extend((cp[1:] + len(tok_all)).tolist())
-                    tok_all.extend(ct.tolist())
-                    sc_all.extend(cs.tolist())
-                    new_seg.append(new_seg[-1] + int(cp[-1]))
-                self._apply(state, np.asarray(ptr_all, np.int32), np.asarray(tok_all, np.int32),
-                            np.asarray(sc_all, np.float64))
+                if hasattr(self.strategy, "select_segments"):
+                    cp, ct, cs, new_seg = self.strategy.select_segments(seg, state.scores, idx, vals, W)
+                    self._apply(state, cp, ct, cs)
+                else:
+                    ptr_all, tok_all, sc_all = [0], [], []
+                    new_seg = [0]
+                    for p in range(len(prompts)):
+                        a, b = seg[p], seg[p + 1]
+                        cp, ct, cs = self.strategy.select_arrays(state.scores[a:b], idx[a:b],
+                                                                 vals[a:b], W)
+                        ptr_all.extend((cp[1:] + len(tok_all)).tolist())
+                        tok_all.extend(ct.tolist())
+                        sc_all.extend(cs.tolist())
+                        new_seg.append(new_seg[-1] + int(cp[-1]))
+                    self._apply(state, np.asarray(ptr_all, np.int32), np.asarray(tok_all, np.int32),
+                                np.asarray(sc_all, np.float64))
                 seg = np.asarray(new_seg)
             if on_step is not None:
                 on_step(n_steps)

@@ -81,6 +81,29 @@ class VanillaBeamSearchStrategy(BeamStrategy):
                                              for j in range(ptr[i], ptr[i + 1])])
                 for i, x in enumerate(new_candidates)]
 
+    def select_segments(self, seg, parent_scores, tokens, logps, beam_size):
+        """select_candidates for several prompts at once (candidates seg[s]:seg[s+1]
+        compete within prompt s).  Returns (child_ptr, tokens, scores, new_seg)."""
+        seg = np.ascontiguousarray(seg, np.int32)
+        n = int(seg[-1])
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        logps = np.ascontiguousarray(logps, np.float64)
+        k = tokens.shape[1] if tokens.ndim == 2 else 0
+        ps = np.ascontiguousarray(parent_scores, np.float64)
+        cap = max(1, (len(seg) - 1) * beam_size)
+        ptr = np.zeros(n + 1, np.int32)
+        ct = np.zeros(cap, np.int32)
+        cs = np.zeros(cap, np.float64)
+        ns = np.zeros(len(seg), np.int32)
+        D = C.POINTER(C.c_double)
+        check(lib().be_vanilla_select_segments(len(seg) - 1, _lib.ptr32(seg), k, ps.ctypes.data_as(D),
+                                               _lib.ptr32(tokens), logps.ctypes.data_as(D),
+                                               beam_size, _lib.ptr32(ptr), _lib.ptr32(ct),
+                                               cs.ctypes.data_as(D), _lib.ptr32(ns)),
+              "select_segments")
+        m = int(ptr[-1])
+        return ptr, ct[:m], cs[:m], ns
+
     def select_arrays(self, parent_scores, tokens, logps, beam_size):
         return vanilla_select_arrays(parent_scores, tokens, logps, beam_size)
 

@@ -678,3 +678,88 @@ int be_vanilla_select(int n, int k, const double* parent_scores, const int32_t* 
 }
 
 }  // extern "C"
+
+extern "C" {
+
+// Vanilla selection for several independent prompts in one call: candidates
+// seg_ptr[s]..seg_ptr[s+1] belong to prompt s and compete only with each other
+// (each prompt keeps its own beam_size).  Outputs cover all candidates:
+// child_ptr [ncand + 1], child_tokens / child_scores [<= nseg * beam_size],
+// new_seg_ptr [nseg + 1] (new candidates per prompt, in order).
+int be_vanilla_select_segments(int nseg, const int32_t* seg_ptr, int k,
+                               const double* parent_scores, const int32_t* tokens,
+                               const double* logps, int beam_size, int32_t* child_ptr,
+                               int32_t* child_tokens, double* child_scores,
+                               int32_t* new_seg_ptr) {
+  int out = 0;
+  child_ptr[0] = 0;
+  new_seg_ptr[0] = 0;
+  std::vector<int32_t> ptr;
+  for (int s = 0; s < nseg; ++s) {
+    const int a = seg_ptr[s], b = seg_ptr[s + 1];
+    const int n = b - a;
+    ptr.assign(n + 1, 0);
+    int rc = be_vanilla_select(n, k, parent_scores + a, tokens + (int64_t)a * k,
+                               logps + (int64_t)a * k, beam_size, ptr.data(), child_tokens + out,
+                               child_scores + out);
+    if (rc) return rc;
+    for (int i = 0; i < n; ++i) child_ptr[a + i + 1] = out + ptr[i + 1];
+    out += ptr[n];
+    new_seg_ptr[s + 1] = out;
+  }
+  return BE_OK;
+}
+
+// Everything one cascade decode step needs from the host, in one call: the
+// per-candidate inputs (query token, RoPE position, append page, append slot)
+// at out[0 .. 4 * ncand) and the attention plan (header included) at
+// out[plan_offset ..).  Semantics: be_beam_step_inputs + be_cascade_build +
+// be_cascade_plan.  BE_ECAPACITY reports the plan size in info->total_ints.
+int be_beam_decode_inputs(be_trie* t, int ncand, const int32_t* cand_leaf, int num_qo_heads,
+                          int num_kv_heads, int num_sms, int32_t* out, int64_t cap,
+                          int32_t plan_offset, be_attn_plan_info* info) {
+  if ((int64_t)4 * ncand > plan_offset || plan_offset > cap) {
+    set_error("be_beam_decode_inputs: plan_offset %d too small for %d candidates", plan_offset,
+              ncand);
+    return BE_EINVAL;
+  }
+  int rc = be_beam_step_inputs(t, ncand, cand_leaf, out, out + 2 * ncand, out + 3 * ncand,
+                               out + ncand);
+  if (rc) return rc;
+  // cascade levels into growable scratch
+  static thread_local std::vector<int32_t> lg, lp, qo, kvp, kvi, last;
+  int cap_l = 64, cap_g = 64 * (ncand + 1), cap_p = 8192;
+  int nlev;
+  for (;;) {
+    lg.resize(cap_l + 1);
+    lp.resize(cap_l + 1);
+    qo.resize(cap_g + cap_l);
+    kvp.resize(cap_g + cap_l);
+    kvi.resize(cap_p);
+    last.resize(cap_g);
+    nlev = be_cascade_build(t, ncand, cand_leaf, cap_l, cap_g, cap_p, lg.data(), lp.data(),
+                            qo.data(), kvp.data(), kvi.data(), last.data());
+    if (nlev == -BE_ECAPACITY) {
+      cap_l *= 2;
+      cap_g *= 2;
+      cap_p *= 4;
+      continue;
+    }
+    if (nlev < 0) return -nlev;
+    break;
+  }
+  std::vector<const int32_t*> a_qo(nlev), a_kvp(nlev), a_kvi(nlev), a_last(nlev);
+  std::vector<int32_t> ng(nlev);
+  for (int l = 0; l < nlev; ++l) {
+    a_qo[l] = qo.data() + lg[l] + l;
+    a_kvp[l] = kvp.data() + lg[l] + l;
+    a_kvi[l] = kvi.data() + lp[l];
+    a_last[l] = last.data() + lg[l];
+    ng[l] = lg[l + 1] - lg[l];
+  }
+  return be_cascade_plan(nlev, a_qo.data(), a_kvp.data(), a_kvi.data(), a_last.data(), ng.data(),
+                         ncand, t->page_size, num_qo_heads, num_kv_heads, 1, 0, num_sms,
+                         out + plan_offset, cap - plan_offset, info);
+}
+
+}  // extern "C"

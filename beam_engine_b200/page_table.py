@@ -73,7 +73,10 @@ class PageTable:
     def __del__(self):
         t = getattr(self, "_trie", None)
         if t:
-            lib().be_trie_destroy(t)
+            try:
+                lib().be_trie_destroy(t)
+            except Exception:   # interpreter shutdown: the library may already be gone
+                pass
             self._trie = None
 
     # -- allocator (page_table.py:77-124) ---------------------------------

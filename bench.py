@@ -93,21 +93,6 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def attn_plan_bytes(levels, hkv, d, hq, elt=2):
-    """Algorithmic bytes of one cascade attention launch: every group's K and V
-    read once (2 * kv_len * Hkv * D * elt) plus q in and o out."""
-    kv = 0
-    nq = 0
-    for lv in levels:
-        kvp, last, ps = lv["kv_indptr"], lv["kv_last_page_len"], PAGE
-        for g in range(len(kvp) - 1):
-            npg = int(kvp[g + 1] - kvp[g])
-            if npg:
-                kv += (npg - 1) * ps + int(last[g])
-        nq = int(lv["qo_indptr"][-1])
-    return kv * 2 * hkv * d * elt + 2 * nq * hq * d * elt
-
-
 def run_b200(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -140,10 +125,12 @@ def run_b200(args, rank, world, local_rank):
     timing = {"on": False}
     gen.time_attention = True          # per-layer attention events recorded inside the step graph
 
-    def plan_hook(levels, inf):
+    def plan_hook(nq, inf):
         if timing["on"]:
-            plan_bytes.append(attn_plan_bytes(levels, model.Hkv, model.D, model.Hq))
-            plan_stats.append((len(levels), inf.n_work, inf.n_work_wide, inf.n_parts, inf.n_merge))
+            # every work item's token range is read once: K and V of all its tokens, q in, o out
+            plan_bytes.append(inf.total_tokens * 2 * model.Hkv * model.D * 2
+                              + 2 * nq * model.Hq * model.D * 2)
+            plan_stats.append((nq, inf.n_work, inf.n_work_wide, inf.n_parts, inf.n_merge))
             # per layer: 2 add_rmsnorm, rope_append, silu_mul + attention (tcgen05 wide,
             # all-heads narrow, LSE merge); final norm
             launches["n"] += cfg["num_hidden_layers"] * (4 + 3) + 1

@@ -328,6 +328,23 @@ int be_vanilla_select(int n, int k, const double* parent_scores, const int32_t* 
                       const double* logps, int beam_size, int32_t* child_ptr,
                       int32_t* child_tokens, double* child_scores);
 
+/* Vanilla selection over several prompts at once (each prompt's candidates
+ * seg_ptr[s]..seg_ptr[s+1] keep their own beam_size), the batched form of
+ * VanillaBeamSearchStrategy.select_candidates (src/beam_engine/beam_strategy.py:433-488)
+ * that the reference calls once per generate().                              */
+int be_vanilla_select_segments(int nseg, const int32_t* seg_ptr, int k,
+                               const double* parent_scores, const int32_t* tokens,
+                               const double* logps, int beam_size, int32_t* child_ptr,
+                               int32_t* child_tokens, double* child_scores,
+                               int32_t* new_seg_ptr);
+/* One call for a cascade decode step's host inputs (beam.py:168-221 decode
+ * inputs + BeamState.get_cascade_input beam_state.py:211-412 + the attention
+ * plan): out[0..n) query tokens, [n..2n) RoPE positions, [2n..3n) append
+ * pages, [3n..4n) append slots, plan (with header) from out[plan_offset].    */
+int be_beam_decode_inputs(be_trie* t, int ncand, const int32_t* cand_leaf, int num_qo_heads,
+                          int num_kv_heads, int num_sms, int32_t* out, int64_t cap,
+                          int32_t plan_offset, be_attn_plan_info* info);
+
 #ifdef __cplusplus
 }
 #endif

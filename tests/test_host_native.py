@@ -10,7 +10,7 @@ import torch
 from conftest import ROOT, load_json
 from beam_engine_b200 import _lib
 from beam_engine_b200.beam_state import BeamCandidate, BeamState, TrieNode
-from beam_engine_b200.beam_strategy import vanilla_select_arrays
+from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy, vanilla_select_arrays
 from beam_engine_b200.fasttree import plan_vnodes
 from beam_engine_b200.page_table import PageTable
 
@@ -139,3 +139,52 @@ def test_object_api_select_and_update():
     assert [c.trie_node.tokens for c in bs.candidates] == [[5, 6, 8], [5, 6, 7]]
     assert [list(map(int, c)) for c in zip(*bs.last_copies)] == [[1, 2, 2]]
     assert bs.candidates[0].trie_node.parent == bs.candidates[1].trie_node.parent
+
+
+def test_fused_decode_inputs_match_separate_calls():
+    """be_beam_decode_inputs (one call per step) writes exactly what
+    step_inputs + cascade_levels + the cascade planner produce separately."""
+    import ctypes as C
+    from beam_engine_b200.cascade import cascade_plan_host
+    rng = np.random.default_rng(3)
+    pt = cpu_table(8, 4096)
+    bs = BeamState(6, pt)
+    bs.defer_copies = True
+    for p in range(3):
+        bs.add_root_sequence(rng.integers(0, 500, 40 + 13 * p).tolist())
+    W = 6
+    bs.update_native(bs.leaves, np.arange(4, dtype=np.int32) * W,
+                     rng.integers(0, 500, 3 * W).astype(np.int32), -rng.random(3 * W))
+    for step in range(12):
+        n = len(bs.leaves)
+        q, wp, wpos, pos = bs.step_inputs()
+        info_ref, plan_ref = cascade_plan_host(bs.cascade_levels(), n, 8, 32, 8)
+        off = -(-4 * n // 32) * 32
+        buf = np.full(off + (1 << 16), -7, np.int32)
+        info = _lib.AttnPlanInfo()
+        leaves = np.ascontiguousarray(bs.leaves, np.int32)
+        rc = _lib.lib().be_beam_decode_inputs(pt._trie, n, _lib.ptr32(leaves), 32, 8, 148,
+                                              C.c_void_p(buf.ctypes.data), len(buf), off,
+                                              C.byref(info))
+        assert rc == _lib.BE_OK
+        assert buf[:n].tolist() == list(q) and buf[n:2 * n].tolist() == list(pos)
+        assert buf[2 * n:3 * n].tolist() == list(wp) and buf[3 * n:4 * n].tolist() == list(wpos)
+        assert info.total_ints == info_ref.total_ints and info.n_work == info_ref.n_work
+        assert buf[off:off + info.total_ints].tolist() == plan_ref[:info.total_ints].tolist()
+        # three prompts' beams, selected together and one prompt at a time
+        seg = np.array([0, n // 3, 2 * n // 3, n], np.int32)
+        k = 2 * W
+        tok = rng.integers(0, 500, (n, k)).astype(np.int32)
+        lp = np.sort(-rng.random((n, k)) * 3, axis=1)[:, ::-1].copy()
+        ptr, ct, cs, ns = VanillaBeamSearchStrategy().select_segments(seg, bs.scores, tok, lp, W)
+        acc_p, acc_t, acc_s, acc_n = [0], [], [], [0]
+        for s in range(3):
+            a, b = seg[s], seg[s + 1]
+            p1, t1, s1 = vanilla_select_arrays(bs.scores[a:b], tok[a:b], lp[a:b], W)
+            acc_p += (p1[1:] + len(acc_t)).tolist()
+            acc_t += t1.tolist()
+            acc_s += s1.tolist()
+            acc_n.append(acc_n[-1] + int(p1[-1]))
+        assert ptr.tolist() == acc_p and ct.tolist() == acc_t and cs.tolist() == acc_s
+        assert ns.tolist() == acc_n
+        bs.update_native(bs.leaves, ptr, ct, cs)
