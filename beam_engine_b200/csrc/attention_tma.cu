@@ -56,18 +56,38 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait; false (and the device status set) on timeout.
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or about `ns` nanoseconds pass (no issue slots burnt spinning).
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* b, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false (and the device status set) on timeout.  The clock is
+// read once every 256 polls: %globaltimer reads are slow and a warp that spins
+// on them steals issue slots from the warps doing the work.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
   if (mbar_try(b, parity)) return true;
-  const uint64_t t0 = gtimer();
-  while (!mbar_try(b, parity)) {
-    if (gtimer() - t0 > kWaitNs) {
-      atomicCAS(&g_device_status, 0, BE_EDEVICE_TIMEOUT);
-      return false;
+  uint64_t t0 = 0;
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try(b, parity)) return true;
+    if ((n & 255) == 0) {
+      const uint64_t t = gtimer();
+      if (t0 == 0) {
+        t0 = t;
+      } else if (t - t0 > kWaitNs) {
+        atomicCAS(&g_device_status, 0, BE_EDEVICE_TIMEOUT);
+        return false;
+      }
     }
   }
-  return true;
 }
+
 __device__ __forceinline__ void tma_load5(uint32_t dst, const CUtensorMap* map, uint64_t* bar,
                                           int c0, int c1, int c2, int c3, int c4) {
   asm volatile(

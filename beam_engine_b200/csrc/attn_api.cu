@@ -31,7 +31,8 @@ int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t
         const bool narrow = narrow_enabled() && p.hkv <= 8 && (umma || !c.fixed);
         int w0 = 0, n_items = c.work;
         if (umma) {
-          rc = D == 128 ? launch_umma<T, 128>(p, map, c.wide, st)
+          rc = D == 128 ? (wide_enabled() ? launch_wide<T>(p, map, c.wide, st)
+                                          : launch_umma<T, 128>(p, map, c.wide, st))
                         : launch_umma<T, 64>(p, map, c.wide, st);
           if (rc != BE_OK) return rc;
           w0 = c.fixed ? -1 : p.n_wide;

@@ -5,6 +5,7 @@
 #include "attention.cu"
 #include "attention_tma.cu"
 #include "attention_umma.cu"
+#include "attention_wide.cu"
 #include "attention_narrow.cu"
 #include "attn_api.cu"
 #include "attn_noalloc.cu"
