@@ -26,6 +26,7 @@ from ._lib import check, lib
 from .beam_state import BeamState
 from .cascade import _Plan
 from .page_table import PageTable, stream_ptr
+from .parallel import vocab_parallel_log_softmax_topk
 
 logger = logging.getLogger(__name__)
 UMMA_MAX_TOKENS = 128   # BE_UMMA_MAX_TOKENS in include/beam_b200.h
@@ -169,10 +170,7 @@ class StepGraph:
         d = self.dev_buf
         logits = self.gen.model.forward(d[0:n], d[n:2 * n], self.gen.page_table, d[2 * n:3 * n],
                                         d[3 * n:4 * n], self)
-        if self.temp != 1.0:
-            logits = logits / self.temp
-        lp = torch.log_softmax(logits, dim=-1)
-        v, i = torch.topk(lp, self.k, dim=-1)
+        v, i = self.gen._logprob_topk(logits, self.k, self.temp)
         self.vals_h.copy_(v.reshape(-1), non_blocking=True)
         self.idx_h.copy_(i.reshape(-1), non_blocking=True)
 
@@ -265,11 +263,16 @@ class BeamSearchGenerator:
             off += len(a)
         return out
 
-    def _topk(self, logits, k, temperature):
+    def _logprob_topk(self, logits, k, temperature):
+        """log_softmax over the full vocabulary, then top-k (beam.py:266-317);
+        vocab-parallel across the tensor-parallel group when the model is sharded."""
         if temperature != 1.0:
             logits = logits / temperature
-        lp = torch.log_softmax(logits, dim=-1)
-        vals, idx = torch.topk(lp, k, dim=-1)
+        m = self.model
+        return vocab_parallel_log_softmax_topk(logits, k, getattr(m, "v0", 0), getattr(m, "tp", None))
+
+    def _topk(self, logits, k, temperature):
+        vals, idx = self._logprob_topk(logits, k, temperature)
         n = vals.shape[0]
         if self.topk_host is None or self.topk_host[0].shape[0] < n * k:
             self.topk_host = (torch.empty(n * k * 2, dtype=torch.float32).pin_memory(),

@@ -1,0 +1,76 @@
+"""Tensor parallelism for the beam-decode model step (one process per GPU).
+
+The reference runs one GPU and has no parallel runtime; its config only
+carries HF's TP plan metadata (``configuration_llama.py:146-154``).  Here the
+decoder is sharded the Megatron way inside :class:`beam_engine_b200.llama.BeamLlama`:
+q/k/v heads and gate/up columns are split across ranks, the O and down
+projections are row-parallel and followed by one all-reduce each.  The paged
+KV cache is sharded by KV head (each rank's pool holds its Hkv / TP heads), so
+attention itself needs no exchange; the block tables, the allocator and the
+beam trie are replicated -- every rank runs the same deterministic host
+scheduler on the same top-k results.
+
+The lm_head is vocab-parallel.  ``log_softmax -> topk(k)`` over the full
+vocabulary (``beam.py:266-317``) becomes: per rank the row max and sum of
+exponentials of its slice (two all-reduces give the global log-sum-exp) and
+its local top-k with global ids; one all-gather of the k candidates per rank
+and a top-k over the gathered ``TP * k`` gives the global top-k.  The result
+equals the single-GPU one up to the order of floating-point summation in the
+log-sum-exp.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+class TensorParallel:
+    """A tensor-parallel group over ``torch.distributed`` (NCCL on GPUs, gloo on
+    CPU for tests).  ``size == 1`` makes every collective a no-op."""
+
+    def __init__(self, group=None):
+        self.group = group
+        if dist.is_available() and dist.is_initialized():
+            self.size = dist.get_world_size(group)
+            self.rank = dist.get_rank(group)
+        else:
+            self.size, self.rank = 1, 0
+
+    def all_reduce(self, t: torch.Tensor, op=None):
+        if self.size > 1:
+            dist.all_reduce(t, op=op or dist.ReduceOp.SUM, group=self.group)
+        return t
+
+    def all_gather_cat(self, t: torch.Tensor, dim: int) -> torch.Tensor:
+        """Concatenate every rank's ``t`` along ``dim`` (rank order)."""
+        if self.size == 1:
+            return t
+        t = t.contiguous()
+        out = torch.empty((self.size * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype,
+                          device=t.device)
+        dist.all_gather_into_tensor(out, t, group=self.group)
+        return torch.cat(out.view((self.size,) + tuple(t.shape)).unbind(0), dim=dim)
+
+
+def vocab_parallel_log_softmax_topk(logits: torch.Tensor, k: int, vocab_offset: int,
+                                    tp: TensorParallel | None):
+    """``topk(log_softmax(logits_full), k)`` from a vocabulary slice per rank.
+
+    ``logits`` is [n, V_local] float32 holding columns [vocab_offset,
+    vocab_offset + V_local) of the full logits.  Returns (values [n, k] f32,
+    global ids [n, k] int64), identical on every rank."""
+    if tp is None or tp.size == 1:
+        lp = torch.log_softmax(logits, dim=-1)
+        return torch.topk(lp, k, dim=-1)
+    m = logits.amax(dim=-1)
+    tp.all_reduce(m, op=dist.ReduceOp.MAX)
+    s = torch.exp(logits - m[:, None]).sum(dim=-1)
+    tp.all_reduce(s)
+    lse = m + torch.log(s)
+    kl = min(k, logits.shape[1])
+    v, i = torch.topk(logits, kl, dim=-1)
+    i = i + vocab_offset
+    vg = tp.all_gather_cat(v, dim=1)           # [n, TP * kl], rank-major = vocabulary order
+    ig = tp.all_gather_cat(i, dim=1)
+    v2, sel = torch.topk(vg, k, dim=-1)
+    return v2 - lse[:, None], torch.gather(ig, 1, sel)

@@ -106,10 +106,18 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     cfg = dict(LLAMA3_8B)
-    model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=dev, seed=1234 + rank)
+    tp_mode = world > 1 and args.parallel == "tp"
+    tp = None
+    if tp_mode:
+        from beam_engine_b200.parallel import TensorParallel
+        tp = TensorParallel()
+    # tensor parallel: every rank builds the same full weights and keeps its shard;
+    # replicas: independent models and prompts per rank
+    seed = 1234 if tp_mode else 1234 + rank
+    model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=dev, seed=seed, tp=tp)
     gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=PAGE,
                               max_num_pages=args.pages)
-    g = torch.Generator().manual_seed(rank)
+    g = torch.Generator().manual_seed(0 if tp_mode else rank)
     prompts = [torch.randint(0, cfg["vocab_size"], (PROMPT_LEN,), generator=g).tolist()
                for _ in range(PROMPTS)]
     W, K = args.warmup, args.steps
@@ -172,7 +180,8 @@ def run_b200(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    tokens = PROMPTS * BEAM * K * world
+    replicas = 1 if tp_mode else world         # independent beam searches in the job
+    tokens = PROMPTS * BEAM * K * replicas
     value = tokens / (ms_max / 1e3)
     # attention roofline: algorithmic bytes / launch duration, live events
     attn_ms = list(attn_events)
@@ -210,7 +219,7 @@ def run_b200(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
-    e2e_tokens = PROMPTS * BEAM * NEW_TOKENS * world
+    e2e_tokens = PROMPTS * BEAM * NEW_TOKENS * replicas
     steps_e2e = NEW_TOKENS
     d2h = PROMPTS * BEAM * 2 * BEAM * (4 + 8)   # top-2W values (f32) + ids (i64) per beam
     assert len(out) == PROMPTS and all(len(o) == 1 for o in out)
@@ -223,14 +232,16 @@ def run_b200(args, rank, world, local_rank):
         "warmup": W,
         "ms_per_step": round(ms_max / K, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if tp_mode else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded uniform token ids, random-init N(0,0.02) weights)",
         "config": {"workload": "cfg3: Llama-3-8B shape, 8 prompts x 1024 tokens, beam width 16, "
                                "128 new tokens, page size 16, cascade attention",
-                   "model": "Llama-3-8B-shape (random init)", "global_batch": PROMPTS * BEAM * world,
-                   "seq_len": PROMPT_LEN, "parallelism": f"replicas x{world}",
+                   "model": "Llama-3-8B-shape (random init)", "global_batch": PROMPTS * BEAM * replicas,
+                   "seq_len": PROMPT_LEN,
+                   "parallelism": f"tp{world}" if tp_mode else (f"replicas x{world}" if world > 1
+                                                                else "tp1"),
                    "l2": "no flush needed: each step reads 15 GB of weights (> 126 MB L2)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None,
@@ -239,7 +250,7 @@ def run_b200(args, rank, world, local_rank):
                      "peak_source": src,
                      "avg_launch_us": round(attn_total_ms / max(len(attn_ms), 1) * 1e3, 2),
                      "bytes_per_launch": round(bytes_total / max(len(attn_ms), 1)),
-                     "plan_avg": dict(zip(("levels", "work_items", "wide_items", "partial_rows",
+                     "plan_avg": dict(zip(("queries", "work_items", "wide_items", "partial_rows",
                                            "merged_queries"),
                                           [round(float(np.mean([p[i] for p in plan_stats])), 1)
                                            for i in range(5)])) if plan_stats else None},
@@ -493,6 +504,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--pages", type=int, default=4096)
+    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
+                    help="N > 1: tensor parallel over the N GPUs (default) or N independent replicas")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default=None, choices=["cfg2"],
                     help="op-level microbench instead of the decode benchmark")
@@ -521,7 +534,7 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     res = run_b200(args, rank, world, local_rank)
     if rank == 0:
-        if not args.no_cpu_baseline and not args.no_e2e:
+        if not args.no_cpu_baseline and not args.no_e2e and world == 1:
             res["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(res), flush=True)
     if world > 1:
