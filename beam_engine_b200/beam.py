@@ -266,10 +266,9 @@ class BeamSearchGenerator:
     def _logprob_topk(self, logits, k, temperature):
         """log_softmax over the full vocabulary, then top-k (beam.py:266-317);
         vocab-parallel across the tensor-parallel group when the model is sharded."""
-        if temperature != 1.0:
-            logits = logits / temperature
         m = self.model
-        return vocab_parallel_log_softmax_topk(logits, k, getattr(m, "v0", 0), getattr(m, "tp", None))
+        return vocab_parallel_log_softmax_topk(logits, k, getattr(m, "v0", 0), getattr(m, "tp", None),
+                                               temperature)
 
     def _topk(self, logits, k, temperature):
         vals, idx = self._logprob_topk(logits, k, temperature)

@@ -10,3 +10,4 @@
 #include "attn_api.cu"
 #include "attn_noalloc.cu"
 #include "model_ops.cu"
+#include "select_ops.cu"

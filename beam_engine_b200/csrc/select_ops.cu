@@ -1,0 +1,230 @@
+// Beam scoring on the device: logits -> log_softmax -> top-k in one launch.
+//
+// The reference scores every beam as `logits / temperature -> log_softmax ->
+// topk(2W)` (beam.py:266-317) with three library ops; torch's top-k alone is
+// ~10 launches per call on a [128, 128256] block.  Here one CTA owns one row:
+//   * every thread streams its part of the row with 16-byte loads, keeping a
+//     running max / sum of exponentials (online rescale) for the log-sum-exp;
+//   * every warp keeps the top KMAX (value, id) pairs of its chunk as a list
+//     sorted by (value desc, id asc), KMAX / 32 entries per lane; a candidate
+//     enters only if it beats the current k-th entry (ballot), so after the
+//     first few hundred elements almost nothing is inserted;
+//   * the warps' lists meet in shared memory and warp 0 merges them the same way;
+//   * out: log-probabilities (x - max) - log(sum) of the k best with global
+//     vocabulary ids, or -- for a vocabulary slice under tensor parallelism --
+//     the raw scaled logits plus the slice's max and sum for a cross-rank
+//     log-sum-exp.
+// HBM-bound: rows x vocab x 4 bytes read once.
+#include "common.cuh"
+
+namespace be {
+
+constexpr int TK_THREADS = 1024;
+constexpr int TK_WARPS = TK_THREADS / 32;
+constexpr int TK_KMAX = 64;            // entries per list (k <= 64)
+constexpr int TK_PER_LANE = TK_KMAX / 32;
+
+// (value, id) order: larger value first, equal values by smaller id
+__device__ __forceinline__ bool tk_better(float a, int ia, float b, int ib) {
+  return a > b || (a == b && ia < ib);
+}
+
+// Warp-wide sorted list: entry e = slot * 32 + lane (slot 0 holds entries 0-31).
+struct WarpTopK {
+  float v[TK_PER_LANE];
+  int id[TK_PER_LANE];
+
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int s = 0; s < TK_PER_LANE; ++s) {
+      v[s] = -INFINITY;
+      id[s] = INT_MAX;
+    }
+  }
+  // value / id of entry k - 1 (the admission threshold), on every lane
+  __device__ __forceinline__ void kth(int k, float& tv, int& ti) const {
+    const int e = k - 1, s = e >> 5, l = e & 31;
+    float vv = v[0];
+    int ii = id[0];
+#pragma unroll
+    for (int q = 1; q < TK_PER_LANE; ++q)
+      if (s == q) {
+        vv = v[q];
+        ii = id[q];
+      }
+    tv = __shfl_sync(0xffffffffu, vv, l);
+    ti = __shfl_sync(0xffffffffu, ii, l);
+  }
+  // insert (x, ix) -- warp-uniform arguments -- keeping the list sorted
+  __device__ __forceinline__ void insert(float x, int ix) {
+    const int lane = threadIdx.x & 31;
+    // position = number of entries better than the candidate
+    int pos = 0;
+#pragma unroll
+    for (int s = 0; s < TK_PER_LANE; ++s)
+      pos += __popc(__ballot_sync(0xffffffffu, tk_better(v[s], id[s], x, ix)));
+    // shift entries >= pos down by one (entry e takes entry e - 1)
+    float carry_v = -INFINITY;
+    int carry_i = INT_MAX;
+#pragma unroll
+    for (int s = 0; s < TK_PER_LANE; ++s) {
+      float up_v = __shfl_up_sync(0xffffffffu, v[s], 1);
+      int up_i = __shfl_up_sync(0xffffffffu, id[s], 1);
+      const float last_v = __shfl_sync(0xffffffffu, v[s], 31);
+      const int last_i = __shfl_sync(0xffffffffu, id[s], 31);
+      if (lane == 0) {
+        up_v = carry_v;
+        up_i = carry_i;
+      }
+      const int e = s * 32 + lane;
+      if (e > pos) {
+        v[s] = up_v;
+        id[s] = up_i;
+      } else if (e == pos) {
+        v[s] = x;
+        id[s] = ix;
+      }
+      carry_v = last_v;
+      carry_i = last_i;
+    }
+  }
+  // offer one candidate per lane; those that beat entry k - 1 go in, lowest lane first
+  __device__ __forceinline__ void offer(float x, int ix, int k, float& tv, int& ti) {
+    unsigned m = __ballot_sync(0xffffffffu, tk_better(x, ix, tv, ti));
+    while (m) {
+      const int src = __ffs(m) - 1;
+      const float cx = __shfl_sync(0xffffffffu, x, src);
+      const int ci = __shfl_sync(0xffffffffu, ix, src);
+      insert(cx, ci);
+      kth(k, tv, ti);
+      m &= ~(1u << src);
+      m &= __ballot_sync(0xffffffffu, tk_better(x, ix, tv, ti));
+    }
+  }
+};
+
+__global__ void __launch_bounds__(TK_THREADS) logsoftmax_topk_kernel(
+    const float* __restrict__ logits, int64_t ld, int v, float temperature, int k,
+    int64_t vocab_offset, int full_vocab, float* __restrict__ out_val, int64_t* __restrict__ out_idx,
+    float* __restrict__ row_max, float* __restrict__ row_sum) {
+  __shared__ float s_v[TK_WARPS][TK_KMAX];
+  __shared__ int s_i[TK_WARPS][TK_KMAX];
+  __shared__ float s_m[TK_WARPS], s_s[TK_WARPS];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float* x = logits + (int64_t)row * ld;
+  const bool scale = temperature != 1.0f;
+  // contiguous chunk per warp (multiple of 128 elements so float4 loads stay aligned)
+  const int per_warp = ((v + TK_WARPS - 1) / TK_WARPS + 127) / 128 * 128;
+  const int c0 = min(v, warp * per_warp), c1 = min(v, c0 + per_warp);
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  WarpTopK tk;
+  tk.init();
+  float tv = -INFINITY;
+  int ti = INT_MAX;
+  float m = -INFINITY, s = 0.f;
+  auto consume = [&](float val, int col, bool valid) {
+    if (scale) val = val / temperature;
+    if (valid) {
+      if (val > m) {
+        s = s * __expf(m - val) + 1.f;
+        m = val;
+      } else {
+        s += __expf(val - m);
+      }
+    }
+    tk.offer(valid ? val : -INFINITY, valid ? col : INT_MAX, k, tv, ti);
+  };
+  for (int base = c0; base < c1; base += 128) {
+    const int col = base + lane * 4;
+    float e[4];
+    if (vec && col + 3 < c1) {
+      const float4 q = *reinterpret_cast<const float4*>(x + col);
+      e[0] = q.x;
+      e[1] = q.y;
+      e[2] = q.z;
+      e[3] = q.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) e[j] = col + j < c1 ? x[col + j] : -INFINITY;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) consume(e[j], col + j, col + j < c1);
+  }
+  // log-sum-exp: warp, then block
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mm = fmaxf(m, m2);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+    m = mm;
+  }
+#pragma unroll
+  for (int q = 0; q < TK_PER_LANE; ++q) {
+    s_v[warp][q * 32 + lane] = tk.v[q];
+    s_i[warp][q * 32 + lane] = tk.id[q];
+  }
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_s[warp] = s;
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  m = s_m[lane];
+  s = s_s[lane];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mm = fmaxf(m, m2);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+    m = mm;
+  }
+  // merge the other warps' lists into warp 0's (only their first k entries matter)
+  for (int w = 1; w < TK_WARPS; ++w)
+    for (int e0 = 0; e0 < k; e0 += 32) {
+      const int e = e0 + lane;
+      const bool in = e < k;
+      tk.offer(in ? s_v[w][e] : -INFINITY, in ? s_i[w][e] : INT_MAX, k, tv, ti);
+    }
+  const float log_s = logf(s);
+#pragma unroll
+  for (int q = 0; q < TK_PER_LANE; ++q) {
+    const int e = q * 32 + lane;
+    if (e < k) {
+      const float val = tk.v[q];
+      out_val[(int64_t)row * k + e] = full_vocab ? (val - m) - log_s : val;
+      out_idx[(int64_t)row * k + e] = (int64_t)tk.id[q] + vocab_offset;
+    }
+  }
+  if (!full_vocab && lane == 0) {
+    row_max[row] = m;
+    row_sum[row] = s;
+  }
+}
+
+}  // namespace be
+
+using namespace be;
+
+extern "C" int be_logsoftmax_topk(const float* logits, int64_t ld, int rows, int v, float temperature,
+                                  int k, int64_t vocab_offset, int full_vocab, float* out_val,
+                                  int64_t* out_idx, float* row_max, float* row_sumexp, void* stream) {
+  if (!logits || !out_val || !out_idx || rows < 0 || v < 1 || k < 1 || k > TK_KMAX || k > v ||
+      ld < v || !(temperature > 0.f)) {
+    set_error("be_logsoftmax_topk: invalid arguments (rows %d, v %d, k %d <= %d, ld %lld)", rows, v,
+              k, TK_KMAX, (long long)ld);
+    return BE_EINVAL;
+  }
+  if (!full_vocab && (!row_max || !row_sumexp)) {
+    set_error("be_logsoftmax_topk: a vocabulary slice needs row_max and row_sumexp");
+    return BE_EINVAL;
+  }
+  if (rows == 0) return BE_OK;
+  logsoftmax_topk_kernel<<<rows, TK_THREADS, 0, (cudaStream_t)stream>>>(
+      logits, ld, v, temperature, k, vocab_offset, full_vocab, out_val, out_idx, row_max,
+      row_sumexp);
+  BE_LAUNCH_CHECK();
+  return BE_OK;
+}

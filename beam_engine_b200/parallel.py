@@ -53,13 +53,21 @@ class TensorParallel:
 
 
 def vocab_parallel_log_softmax_topk(logits: torch.Tensor, k: int, vocab_offset: int,
-                                    tp: TensorParallel | None):
-    """``topk(log_softmax(logits_full), k)`` from a vocabulary slice per rank.
+                                    tp: TensorParallel | None, temperature: float = 1.0):
+    """``topk(log_softmax(logits_full / temperature), k)`` from a vocabulary
+    slice per rank.
 
     ``logits`` is [n, V_local] float32 holding columns [vocab_offset,
     vocab_offset + V_local) of the full logits.  Returns (values [n, k] f32,
-    global ids [n, k] int64), identical on every rank."""
-    if tp is None or tp.size == 1:
+    global ids [n, k] int64), identical on every rank.  CUDA tensors go through
+    the fused ``be_logsoftmax_topk`` kernel; CPU tensors (gloo tests) through
+    torch."""
+    sharded = tp is not None and tp.size > 1
+    if logits.is_cuda:
+        return _fused(logits, k, vocab_offset, tp if sharded else None, temperature)
+    if temperature != 1.0:
+        logits = logits / temperature
+    if not sharded:
         lp = torch.log_softmax(logits, dim=-1)
         return torch.topk(lp, k, dim=-1)
     m = logits.amax(dim=-1)
@@ -72,5 +80,37 @@ def vocab_parallel_log_softmax_topk(logits: torch.Tensor, k: int, vocab_offset: 
     i = i + vocab_offset
     vg = tp.all_gather_cat(v, dim=1)           # [n, TP * kl], rank-major = vocabulary order
     ig = tp.all_gather_cat(i, dim=1)
+    v2, sel = torch.topk(vg, k, dim=-1)
+    return v2 - lse[:, None], torch.gather(ig, 1, sel)
+
+
+def _fused(logits, k, vocab_offset, tp, temperature):
+    import ctypes as C
+    from ._lib import check, lib
+    if logits.dtype != torch.float32 or logits.stride(1) != 1:
+        raise ValueError("be_logsoftmax_topk takes row-major float32 logits")
+    n, v = logits.shape
+    dev = logits.device
+    kl = min(k, v)
+    vals = torch.empty((n, kl), dtype=torch.float32, device=dev)
+    idx = torch.empty((n, kl), dtype=torch.int64, device=dev)
+    st = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    if tp is None:
+        check(lib().be_logsoftmax_topk(logits.data_ptr(), logits.stride(0), n, v, float(temperature),
+                                       kl, vocab_offset, 1, vals.data_ptr(), idx.data_ptr(), None,
+                                       None, st), "be_logsoftmax_topk")
+        return vals, idx
+    m = torch.empty(n, dtype=torch.float32, device=dev)
+    s = torch.empty(n, dtype=torch.float32, device=dev)
+    check(lib().be_logsoftmax_topk(logits.data_ptr(), logits.stride(0), n, v, float(temperature), kl,
+                                   vocab_offset, 0, vals.data_ptr(), idx.data_ptr(), m.data_ptr(),
+                                   s.data_ptr(), st), "be_logsoftmax_topk")
+    gm = m.clone()
+    tp.all_reduce(gm, op=dist.ReduceOp.MAX)
+    gs = s * torch.exp(m - gm)
+    tp.all_reduce(gs)
+    lse = gm + torch.log(gs)
+    vg = tp.all_gather_cat(vals, dim=1)
+    ig = tp.all_gather_cat(idx, dim=1)
     v2, sel = torch.topk(vg, k, dim=-1)
     return v2 - lse[:, None], torch.gather(ig, 1, sel)

@@ -240,6 +240,17 @@ int be_rope_qkv_append(void* qkv, int64_t row_stride, int n, int num_qo_heads, i
  * fused [n][2*ffn] gate|up projection.                                       */
 int be_silu_mul(const void* gate_up, void* out, int n, int ffn, int dtype, void* stream);
 
+/* Beam scoring (beam.py:266-317: logits / temperature -> log_softmax ->
+ * topk(k)) in one launch.  logits [rows][ld] f32, first v columns used.
+ * full_vocab != 0: out_val[rows][k] = log-probabilities of the k largest,
+ * out_idx = vocab_offset + column (order: value desc, then id asc).
+ * full_vocab == 0 (a vocabulary slice under tensor parallelism): out_val =
+ * the slice's k largest scaled logits, row_max / row_sumexp = the slice's
+ * max and sum(exp(x - max)) for a cross-rank log-sum-exp.  k <= 64.         */
+int be_logsoftmax_topk(const float* logits, int64_t ld, int rows, int v, float temperature,
+                       int k, int64_t vocab_offset, int full_vocab, float* out_val,
+                       int64_t* out_idx, float* row_max, float* row_sumexp, void* stream);
+
 /* ------------------------------------------------------------------------
  * Host page manager (no CUDA): FIFO page allocator + beam trie.  One
  * be_trie backs one PageTable and the BeamState objects over it.

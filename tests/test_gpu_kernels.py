@@ -334,3 +334,50 @@ def test_out_of_range_page_is_flagged_not_faulted():
     assert st.value == _lib.BE_EDEVICE_RANGE
     L.be_device_status_clear(None)
     torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("rows,v,k,temp", [(128, 128256, 32, 1.0), (5, 1000, 64, 0.7),
+                                           (3, 97, 1, 1.0), (7, 4099, 8, 1.3)])
+def test_logsoftmax_topk_matches_torch(rows, v, k, temp):
+    """be_logsoftmax_topk against torch log_softmax -> topk (fp32): values
+    within 1e-5, the same ids (the draws have no ties)."""
+    import ctypes as C
+    from beam_engine_b200 import _lib
+    d = dev()
+    g = torch.Generator(device=d).manual_seed(rows + v)
+    logits = torch.randn((rows, v), generator=g, device=d) * 3
+    ref_v, ref_i = torch.topk(torch.log_softmax(logits / temp, -1), k, -1)
+    vals = torch.empty((rows, k), device=d)
+    idx = torch.empty((rows, k), dtype=torch.int64, device=d)
+    _lib.check(_lib.lib().be_logsoftmax_topk(logits.data_ptr(), v, rows, v, temp, k, 0, 1,
+                                             vals.data_ptr(), idx.data_ptr(), None, None, None))
+    torch.cuda.synchronize()
+    assert torch.equal(idx, ref_i)
+    assert (vals - ref_v).abs().max().item() < 1e-5
+
+
+def test_logsoftmax_topk_ties_and_slice():
+    """Equal logits come out by smaller id first; a vocabulary slice returns raw
+    logits with global ids and the slice's max / sum of exponentials."""
+    import ctypes as C
+    from beam_engine_b200 import _lib
+    d = dev()
+    logits = torch.zeros((2, 300), device=d)
+    logits[0, [7, 3, 250, 100]] = 5.0          # four-way tie
+    logits[1, 17] = 2.0
+    k = 6
+    vals = torch.empty((2, k), device=d)
+    idx = torch.empty((2, k), dtype=torch.int64, device=d)
+    m = torch.empty(2, device=d)
+    s = torch.empty(2, device=d)
+    _lib.check(_lib.lib().be_logsoftmax_topk(logits.data_ptr(), 300, 2, 300, 1.0, k, 1000, 0,
+                                             vals.data_ptr(), idx.data_ptr(), m.data_ptr(),
+                                             s.data_ptr(), None))
+    torch.cuda.synchronize()
+    assert idx[0].tolist() == [1003, 1007, 1100, 1250, 1000, 1001]
+    assert vals[0].tolist() == [5.0, 5.0, 5.0, 5.0, 0.0, 0.0]
+    assert idx[1, 0].item() == 1017 and idx[1, 1:].tolist() == [1000, 1001, 1002, 1003, 1004]
+    ref_m = logits.amax(-1)
+    ref_s = torch.exp(logits - ref_m[:, None]).sum(-1)
+    assert torch.allclose(m, ref_m) and torch.allclose(s, ref_s, rtol=1e-5)
