@@ -58,6 +58,8 @@ _SIGS = {
                                       C.c_int, C.c_int, C.c_int, f32, vp, i64, vp, vp, vp]),
     "be_attn_run_fixed": (C.c_int, [vp, vp, C.c_int, vp, i64, vp, C.c_int, C.c_int, C.c_int,
                                     C.c_int, C.c_int, f32, vp, i64, vp, vp, vp, vp, vp]),
+    "be_attn_run_fixed_2s": (C.c_int, [vp, vp, C.c_int, vp, i64, vp, C.c_int, C.c_int, C.c_int,
+                                    C.c_int, C.c_int, f32, vp, i64, vp, vp, vp, vp, vp, vp]),
     # host page manager
     "be_trie_create": (vp, [C.c_int, C.c_int]),
     "be_trie_destroy": (None, [vp]),

@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import ctypes as C
 import logging
+import os
 from typing import List, Optional, Sequence
 
 import numpy as np
@@ -121,6 +122,9 @@ class StepGraph:
         self.vals_h = torch.empty(n * k, dtype=torch.float32).pin_memory()
         self.idx_h = torch.empty(n * k, dtype=torch.int64).pin_memory()
         self.ccaps = _lib.AttnCaps(self.caps["work"], self.caps["wide"], self.caps["merge"], 1)
+        # suffix tiles on a second stream, overlapping the shared-prefix tiles
+        self.side = (torch.cuda.Stream(dev) if os.environ.get("BE_ATTN_TWO_STREAMS", "1") != "0"
+                     else None)
         self.graph = None
         # optional per-layer attention timing inside the graph (external event nodes)
         self.timing = bool(getattr(gen, "time_attention", False))
@@ -157,12 +161,13 @@ class StepGraph:
     def run(self, layer, qkv, out):  # attention of one layer (the model calls this)
         m, pt = self.gen.model, self.gen.page_table
         self._mark(2 * layer, qkv)
-        rc = lib().be_attn_run_fixed(
+        rc = lib().be_attn_run_fixed_2s(
             self.dev_buf.data_ptr() + 4 * self.plan_off, C.byref(self.ccaps), pt.page_size,
             qkv.data_ptr(), qkv.stride(0), pt.kv_cache[layer].data_ptr(), pt.max_num_pages, m.Hq,
             m.Hkv, m.D, m.dt, m.D ** -0.5, out.data_ptr(), out.stride(0), None,
-            self.mid_o.data_ptr(), self.mid_lse.data_ptr(), None, stream_ptr(qkv.device))
-        check(rc, "be_attn_run_fixed")
+            self.mid_o.data_ptr(), self.mid_lse.data_ptr(), None, stream_ptr(qkv.device),
+            C.c_void_p(self.side.cuda_stream) if self.side is not None else None)
+        check(rc, "be_attn_run_fixed_2s")
         self._mark(2 * layer + 1, qkv)
 
     def _body(self):
@@ -204,8 +209,9 @@ class BeamSearchGenerator:
     def __init__(self, model, tokenizer, strategy, page_size: int = 8, kernel_type: str = "cascade",
                  max_num_pages: int = 1024, store_dtype: Optional[torch.dtype] = None,
                  workspace_bytes: int = 128 << 20, use_graph: bool = True):
-        if kernel_type not in ("cascade", "fasttree"):
-            raise ValueError(f"Unknown kernel_type: {kernel_type}. Must be 'cascade' or 'fasttree'.")
+        if kernel_type not in ("cascade", "fasttree", "auto"):
+            raise ValueError(f"Unknown kernel_type: {kernel_type}. "
+                             "Must be 'cascade', 'fasttree' or 'auto'.")
         self.model = model
         self.tokenizer = tokenizer
         self.strategy = strategy
@@ -223,12 +229,13 @@ class BeamSearchGenerator:
         self.topk_host = None
         self.step_timer = None
         # cascade decode steps replay one CUDA graph (bf16/fp16 pools, page size 16)
-        self.use_graph = (use_graph and kernel_type == "cascade" and page_size == 16
+        self.use_graph = (use_graph and kernel_type in ("cascade", "auto") and page_size == 16
                           and self.page_table.store_dtype != torch.float32)
         self.step_graph = None
         self.time_attention = False   # record per-layer attention events in the step graph
         self.attn_times = None        # list to collect them into (ms per launch) when set
         self.plan_hook = None         # called with (queries, plan info) per graph step
+        self.picks = []               # kernel_type "auto": the choice of every decode step
 
     # ------------------------------------------------------------------
     def generate(self, input_text: str, beam_size: int = 4, max_length: int = 50,
@@ -310,31 +317,55 @@ class BeamSearchGenerator:
                                     logits_rows=d_rows.long())
         return logits
 
-    def decode_step(self, state: BeamState):
+    def _tree_vnodes(self, state: BeamState, n: int):
+        from .fasttree import plan_vnodes
+        par, seql, kids, rptr, rl, r2t = state.tree_arrays(per_node=True)
+        v = plan_vnodes(par, seql, kids, rptr, np.ascontiguousarray(rl) if len(rl) else
+                        np.zeros(1, np.int32), r2t.shape[1], n, self.model.Hq_total,
+                        self.model.Hkv_total)
+        return v, r2t
+
+    def pick_kernel(self, state: BeamState) -> str:
+        """kernel_type "auto": cascade or tree attention for this step (picker.py)."""
+        from .cascade import cascade_plan_host
+        from .fasttree import build_tree_plan
+        from .picker import choose
+        m, ps = self.model, self.page_table.page_size
+        n = len(state.leaves)
+        levels = state.cascade_levels()
+        cinfo, _ = cascade_plan_host(levels, n, ps, m.Hq, m.Hkv, causal=True,
+                                     num_sms=self.attn.plan.num_sms)
+        v, _ = self._tree_vnodes(state, n)
+        tinfo, _ = build_tree_plan(v, n, ps, m.Hq, m.Hkv)
+        elt = 4 if self.page_table.store_dtype == torch.float32 else 2
+        kind = choose(levels, cinfo, tinfo, m.Hkv, m.Hq, m.D, elt=elt)
+        self.picks.append(kind)
+        return kind
+
+    def decode_step(self, state: BeamState, kind: Optional[str] = None):
         """One beam step's forward: returns logits [beams, vocab]."""
+        if kind is None:
+            kind = self.pick_kernel(state) if self.kernel_type == "auto" else self.kernel_type
         q, wp, wpos, pos = state.step_inputs()
-        if self.kernel_type == "cascade":
+        if kind == "cascade":
             levels = state.cascade_levels()
             self.attn.plan_levels(levels, len(q), causal=True)
         else:
-            from .fasttree import plan_vnodes
-            par, seql, kids, rptr, rl, r2t = state.tree_arrays(per_node=True)
-            v = plan_vnodes(par, seql, kids, rptr, np.ascontiguousarray(rl) if len(rl) else
-                            np.zeros(1, np.int32), r2t.shape[1], len(q), self.model.Hq_total,
-                            self.model.Hkv_total)
+            v, r2t = self._tree_vnodes(state, len(q))
             flat = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)])
         arrays = [q, pos, wp, wpos]
-        if self.kernel_type != "cascade":
+        if kind != "cascade":
             arrays.append(_i32(flat))
         dev = self._to_device(arrays)
-        if self.kernel_type != "cascade":
+        if kind != "cascade":
             self.attn.plan_tree(v, len(q), dev[4])
         return self.model.forward(dev[0].long(), dev[1], self.page_table, dev[2], dev[3], self.attn)
 
     def decode_topk(self, state: BeamState, k: int, temperature: float):
         """One decode step through to the host: (log-prob top-k [beams, k], ids)."""
-        if not self.use_graph:
-            return self._topk(self.decode_step(state), k, temperature)
+        kind = self.pick_kernel(state) if self.kernel_type == "auto" else self.kernel_type
+        if not self.use_graph or kind != "cascade":
+            return self._topk(self.decode_step(state, kind), k, temperature)
         m = self.model
         n = len(state.leaves)
         leaves = np.ascontiguousarray(state.leaves, np.int32)
@@ -361,7 +392,7 @@ class BeamSearchGenerator:
                     break
                 size *= 4
             if info.max_wide_tokens > UMMA_MAX_TOKENS:   # outside the fixed kernels' range
-                return self._topk(self.decode_step(state), k, temperature)
+                return self._topk(self.decode_step(state, "cascade"), k, temperature)
             caps = dict(work=2 * info.n_work + 64, wide=2 * info.n_work_wide + 16,
                         merge=max(n, 1), parts=2 * info.n_parts + 256,
                         ints=2 * info.total_ints + 4096)

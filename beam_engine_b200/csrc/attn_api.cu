@@ -9,7 +9,29 @@ namespace be {
 struct Caps {                // grid sizes; fixed = true: counts come from the plan header
   int work, wide, merge, cluster;
   bool fixed;
+  cudaStream_t side = nullptr;   // narrow tiles on this stream (fork / join by events)
 };
+
+// Fork / join events for the two-stream launch, one pair per device, created
+// once (timing off).  Re-recording the same events is fine, also in a capture.
+static int side_events(cudaEvent_t* fork, cudaEvent_t* join) {
+  static std::mutex mu;
+  static cudaEvent_t ev[64][2] = {};
+  int dev = 0;
+  BE_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    set_error("device ordinal %d out of range", dev);
+    return BE_EINVAL;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ev[dev][0]) {
+    BE_CUDA_CHECK(cudaEventCreateWithFlags(&ev[dev][0], cudaEventDisableTiming));
+    BE_CUDA_CHECK(cudaEventCreateWithFlags(&ev[dev][1], cudaEventDisableTiming));
+  }
+  *fork = ev[dev][0];
+  *join = ev[dev][1];
+  return BE_OK;
+}
 
 template <typename T>
 int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t* plan, int D,
@@ -30,6 +52,13 @@ int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t
                           (c.fixed || info->max_wide_tokens <= UM_MAX_TOK);
         const bool narrow = narrow_enabled() && p.hkv <= 8 && (umma || !c.fixed);
         int w0 = 0, n_items = c.work;
+        if (umma && c.side) {   // fork point before the wide tiles: both start together
+          cudaEvent_t f = nullptr, j = nullptr;
+          rc = side_events(&f, &j);
+          if (rc != BE_OK) return rc;
+          BE_CUDA_CHECK(cudaEventRecord(f, st));
+          BE_CUDA_CHECK(cudaStreamWaitEvent(c.side, f, 0));
+        }
         if (umma) {
           rc = D == 128 ? (wide_enabled() ? launch_wide<T>(p, map, c.wide, st)
                                           : launch_umma<T, 128>(p, map, c.wide, st))
@@ -46,10 +75,23 @@ int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t
           w0 = p.n_wide;
           n_items = p.n_work - p.n_wide;
         }
-        // narrow tiles: one CTA per item with every KV head
-        if (n_items > 0 && narrow)
-          rc = D == 128 ? launch_narrow<T, 128>(p, map, w0, n_items, st)
-                        : launch_narrow<T, 64>(p, map, w0, n_items, st);
+        // narrow tiles: one CTA per item with every KV head (on the side stream
+        // when there is one, so they overlap the tail of the wide tiles)
+        if (n_items > 0 && narrow) {
+          cudaStream_t ns = st;
+          cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+          if (c.side && umma) {   // the side stream already waits on the fork point
+            rc = side_events(&ev_fork, &ev_join);
+            if (rc != BE_OK) return rc;
+            ns = c.side;
+          }
+          rc = D == 128 ? launch_narrow<T, 128>(p, map, w0, n_items, ns)
+                        : launch_narrow<T, 64>(p, map, w0, n_items, ns);
+          if (ns != st) {
+            BE_CUDA_CHECK(cudaEventRecord(ev_join, ns));
+            BE_CUDA_CHECK(cudaStreamWaitEvent(st, ev_join, 0));
+          }
+        }
         else if (n_items > 0)
           rc = D == 128 ? launch_tma<T, 128>(p, map, cs, w0, n_items, st)
                         : launch_tma<T, 64>(p, map, cs, w0, n_items, st);
@@ -195,5 +237,41 @@ extern "C" int be_attn_run_fixed(const int32_t* plan_dev, const be_attn_caps* ca
   p.n_work = caps->max_work;
   p.n_wide = caps->max_wide;
   const Caps c{caps->max_work, caps->max_wide, caps->max_merge, caps->cluster, true};
+  return dispatch(dtype, p, nullptr, plan_dev, head_dim, c, (cudaStream_t)stream);
+}
+
+extern "C" int be_attn_run_fixed_2s(const int32_t* plan_dev, const be_attn_caps* caps, int page_size,
+                                    const void* q, int64_t q_row_stride, const void* paged_kv_cache,
+                                    int num_pages, int num_qo_heads, int num_kv_heads, int head_dim,
+                                    int dtype, float sm_scale, void* out, int64_t out_row_stride,
+                                    float* lse, float* mid_o, float* mid_lse,
+                                    const int32_t* kv_list_override, void* stream, void* side_stream) {
+  if (!plan_dev || !caps || !q || !paged_kv_cache || !out || !mid_o || !mid_lse) {
+    set_error("be_attn_run_fixed_2s: null pointer");
+    return BE_EINVAL;
+  }
+  int rc = check_heads(num_qo_heads, num_kv_heads, head_dim, dtype);
+  if (rc) return rc;
+  if (caps->max_work < 0 || caps->max_wide < 0 || caps->max_wide > caps->max_work ||
+      caps->max_merge < 0 || caps->cluster < 0 || caps->cluster > 8 || page_size < 1) {
+    set_error("be_attn_run_fixed_2s: invalid caps");
+    return BE_EINVAL;
+  }
+  if (dtype != BE_F32 && (((uintptr_t)q | (uintptr_t)paged_kv_cache) % 16 ||
+                          (q_row_stride * 2) % 16)) {
+    set_error("be_attn_run_fixed_2s: q and the pool must be 16-byte aligned");
+    return BE_EINVAL;
+  }
+  AttnParams p;
+  fill_params(p, q, q_row_stride, paged_kv_cache, num_pages, page_size, num_qo_heads,
+              num_kv_heads, sm_scale, out, out_row_stride, lse, mid_o, mid_lse);
+  p.hdr = plan_dev;
+  p.work = nullptr;
+  p.qlist = nullptr;
+  p.kvlist = kv_list_override;
+  p.n_work = caps->max_work;
+  p.n_wide = caps->max_wide;
+  Caps c{caps->max_work, caps->max_wide, caps->max_merge, caps->cluster, true};
+  c.side = (cudaStream_t)side_stream;
   return dispatch(dtype, p, nullptr, plan_dev, head_dim, c, (cudaStream_t)stream);
 }

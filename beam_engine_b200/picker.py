@@ -1,0 +1,83 @@
+"""Tree-vs-cascade attention picker (``kernel_type="auto"``).
+
+The reference has no picker: ``kernel_type`` is a fixed user choice
+(``beam.py:20,34,168-206``), and its only cost model is FastTree's per-edge
+split decision (``preparation.py:11-225``, alpha 0.6 / beta 0.3 / gamma 0.1),
+which this build keeps inside the tree planner.  Here the choice is made per
+decode step from the two plans the host builds anyway:
+
+* exactness first: the reference's cascade metadata lists some pages at
+  several levels when the beam tree is uneven (a candidate whose branch ends
+  above the deepest level re-uses its deepest nodes at every later level,
+  ``beam_state.py:299-302``), so those pages enter the softmax twice.  When a
+  step's cascade levels do that, the tree plan (one vnode per trie node, each
+  page once) is taken;
+* otherwise the cheaper plan by a launch-level model of these kernels:
+  ``time = launches * t_launch + waves * t_cta + bytes / HBM``, where a wave
+  is one CTA per SM (two for the tcgen05 prefix tiles), the bytes are every
+  work item's K/V plus the partial rows written and merged.  The per-CTA times
+  are the measured lifetimes of the kernels on B200 (decode shapes, Hkv 8,
+  D 128): ~15 us for a tcgen05 prefix tile, ~11 us for an all-heads suffix
+  tile, ~18 us for a slot-list (tree) tile.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass
+class PickerModel:
+    num_sms: int = 148
+    hbm_gbs: float = 6500.0
+    t_launch_us: float = 3.0
+    t_wide_cta_us: float = 15.0      # tcgen05 prefix tile (two CTAs per SM)
+    t_narrow_cta_us: float = 11.0    # all-heads suffix tile (one CTA per SM)
+    t_slot_cta_us: float = 18.0      # slot-list tile of the tree plan (two CTAs per SM)
+
+    def cascade_us(self, info, hkv, hq, d, elt=2):
+        narrow = info.n_work - info.n_work_wide
+        waves = (math.ceil(info.n_work_wide * hkv / (2 * self.num_sms)) * self.t_wide_cta_us
+                 + math.ceil(narrow / self.num_sms) * self.t_narrow_cta_us)
+        return 3 * self.t_launch_us + waves + self._bytes_us(info, hkv, hq, d, elt)
+
+    def tree_us(self, info, hkv, hq, d, elt=2):
+        waves = math.ceil(info.n_work * hkv / (2 * self.num_sms)) * self.t_slot_cta_us
+        return 2 * self.t_launch_us + waves + self._bytes_us(info, hkv, hq, d, elt)
+
+    def _bytes_us(self, info, hkv, hq, d, elt):
+        kv = info.total_tokens * 2 * hkv * d * elt
+        parts = info.n_parts * hq * (d + 1) * 4 * 2          # written, then read by the merge
+        return (kv + parts) / (self.hbm_gbs * 1e3)
+
+
+def cascade_counts_pages_twice(levels) -> bool:
+    """True when some query attends one page at two levels (uneven trees)."""
+    seen = {}
+    for lv in levels:
+        qo = np.asarray(lv["qo_indptr"])
+        kvp = np.asarray(lv["kv_indptr"])
+        kvi = np.asarray(lv["kv_indices"])
+        for g in range(len(qo) - 1):
+            pages = kvi[kvp[g]:kvp[g + 1]]
+            if len(pages) == 0:
+                continue
+            for q in range(int(qo[g]), int(qo[g + 1])):
+                s = seen.setdefault(q, set())
+                for p in pages.tolist():
+                    if p in s:
+                        return True
+                    s.add(p)
+    return False
+
+
+def choose(cascade_levels, cascade_info, tree_info, hkv, hq, d, model: PickerModel | None = None,
+           elt=2) -> str:
+    """'cascade' or 'fasttree' for one decode step."""
+    if cascade_counts_pages_twice(cascade_levels):
+        return "fasttree"
+    m = model or PickerModel()
+    return ("cascade" if m.cascade_us(cascade_info, hkv, hq, d, elt)
+            <= m.tree_us(tree_info, hkv, hq, d, elt) else "fasttree")

@@ -528,10 +528,15 @@ def main():
             print(json.dumps(res), flush=True)
         return
     if world > 1:
+        import datetime
         import torch
         import torch.distributed as dist
+        # NVLS off: multicast objects outlive a failed rank on this kind of box
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        # a short process-group timeout turns a stuck collective into an error
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=180))
     res = run_b200(args, rank, world, local_rank)
     if rank == 0:
         if not args.no_cpu_baseline and not args.no_e2e and world == 1:

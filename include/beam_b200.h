@@ -212,6 +212,18 @@ int be_attn_run_fixed(const int32_t* plan_dev, const be_attn_caps* caps, int pag
                       float* mid_o, float* mid_lse, const int32_t* kv_list_override,
                       void* stream);
 
+/* be_attn_run_fixed with the narrow (per-beam suffix) tiles on a second
+ * stream: they start as soon as SMs free up from the shared-prefix tiles
+ * instead of after them; the LSE merge waits for both on `stream`.  Both
+ * streams must belong to the current device; inside a stream capture the
+ * fork and join become graph dependencies.  side_stream NULL = one stream.  */
+int be_attn_run_fixed_2s(const int32_t* plan_dev, const be_attn_caps* caps, int page_size,
+                         const void* q, int64_t q_row_stride, const void* paged_kv_cache,
+                         int num_pages, int num_qo_heads, int num_kv_heads, int head_dim,
+                         int dtype, float sm_scale, void* out, int64_t out_row_stride, float* lse,
+                         float* mid_o, float* mid_lse, const int32_t* kv_list_override,
+                         void* stream, void* side_stream);
+
 /* ------------------------------------------------------------------------
  * Decoder-layer kernels of the model runner (the reference runs these as
  * separate PyTorch ops inside src/beam_engine/models/modeling_llama.py).

@@ -111,3 +111,24 @@ def test_graph_step_matches_eager_bf16():
     for a, b in zip(*outs):
         assert [s for s, _ in a] == [s for s, _ in b]
         np.testing.assert_allclose([x for _, x in a], [x for _, x in b], rtol=1e-6)
+
+
+def test_auto_picker_runs_and_agrees_when_it_picks_cascade():
+    """kernel_type="auto" decides per step; its beams equal the cascade run's
+    when every pick was cascade, and equal the tree run's when every pick was
+    the tree (fp32, cfg1)."""
+    from beam_engine_b200.beam import BeamSearchGenerator
+    from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy
+    model, g, _ = cfg1_model()
+    runs = {}
+    for kt in ("auto", "cascade", "fasttree"):
+        gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=16,
+                                  kernel_type=kt, max_num_pages=512)
+        runs[kt] = (gen.generate_ids([g["prompt"]], 4, max_new_tokens=16, num_return_sequences=4)[0],
+                    list(gen.picks))
+    out, picks = runs["auto"]
+    assert len(picks) == 15 and set(picks) <= {"cascade", "fasttree"}
+    if set(picks) == {"cascade"}:
+        assert [s for s, _ in out] == [s for s, _ in runs["cascade"][0]]
+    if set(picks) == {"fasttree"}:
+        assert [s for s, _ in out] == [s for s, _ in runs["fasttree"][0]]

@@ -188,3 +188,30 @@ def test_fused_decode_inputs_match_separate_calls():
         assert ptr.tolist() == acc_p and ct.tolist() == acc_t and cs.tolist() == acc_s
         assert ns.tolist() == acc_n
         bs.update_native(bs.leaves, ptr, ct, cs)
+
+
+def test_picker_exactness_and_cost(cascade_trees):
+    """kernel_type "auto": an uneven tree (whose cascade levels list pages twice)
+    goes to the tree plan; otherwise the cheaper plan by the launch model."""
+    from beam_engine_b200.picker import PickerModel, cascade_counts_pages_twice, choose
+    assert cascade_counts_pages_twice(cascade_trees["uneven"]["expect"]["levels"])
+    assert not cascade_counts_pages_twice(cascade_trees["example"]["expect"]["levels"])
+    assert not cascade_counts_pages_twice(cascade_trees["swapped"]["expect"]["levels"])
+
+    def info(**kw):
+        i = _lib.AttnPlanInfo()
+        for k, v in kw.items():
+            setattr(i, k, v)
+        return i
+    lv = cascade_trees["example"]["expect"]["levels"]
+    shared = info(n_work=40, n_work_wide=8, total_tokens=9000, n_parts=200)
+    tree_dup = info(n_work=300, n_work_wide=0, total_tokens=9000, n_parts=900)
+    assert choose(lv, shared, tree_dup, 8, 32, 128) == "cascade"
+    # a cascade that re-reads much more KV than the tree loses
+    heavy = info(n_work=400, n_work_wide=300, total_tokens=400000, n_parts=3000)
+    light = info(n_work=60, n_work_wide=0, total_tokens=20000, n_parts=200)
+    assert choose(lv, heavy, light, 8, 32, 128) == "fasttree"
+    m = PickerModel()
+    assert m.cascade_us(shared, 8, 32, 128) < m.tree_us(tree_dup, 8, 32, 128)
+    assert choose(cascade_trees["uneven"]["expect"]["levels"], shared, tree_dup, 8, 32, 128) == \
+        "fasttree"
