@@ -191,7 +191,9 @@ class StepGraph:
                 self._body()            # warm-up (writes the same K/V the replay will)
             cur.wait_stream(side)
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            # thread-local capture: other threads (NCCL's watchdog polling its
+            # events) may keep making CUDA calls while this one records
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
                 self._body()
             self.graph = g
         self.graph.replay()

@@ -11,9 +11,13 @@ CUDA events (barrier + synchronize on both sides); W + K <= 127 (the 128th
 token comes from the prefill).  Every step streams the 15 GB of weights, far
 more than L2, so no flush is needed between steps.
 
-Multi-GPU (torchrun, one process per GPU): every rank decodes its own 8
-prompts (independent replicas, weak scaling, no collective on the data path);
-value = all ranks' beam tokens / max-over-ranks time.
+Multi-GPU (torchrun, one process per GPU): tensor parallel over the N GPUs
+(default; the same 8 prompts, heads / MLP columns / vocabulary sharded, NCCL
+all-reduces; strong scaling; value = the job's beam tokens / max-over-ranks
+time), or ``--parallel replicas`` (every rank decodes its own 8 prompts, weak
+scaling, no collective on the data path).  ``BENCH_WATCHDOG_S`` > 0 dumps
+every thread's Python stack if a rank is still running after that many
+seconds (diagnosis of a stuck collective).
 
 ``--impl reference`` times the CPU restatement of the reference engine (the
 oracle; the reference's own GPU path needs FlashInfer 0.2.8, and its Python
@@ -516,6 +520,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end pass and print a short line (for profiling)")
     args = ap.parse_args()
+    wd = float(os.environ.get("BENCH_WATCHDOG_S", "0") or 0)
+    if wd > 0:
+        import faulthandler
+        faulthandler.dump_traceback_later(wd, repeat=True, exit=False)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
