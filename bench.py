@@ -553,7 +553,11 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
-        dist.destroy_process_group()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        # destroy_process_group() can block on communicators that captured CUDA
+        # graphs still reference; the process is done, so leave without it
+        os._exit(0)
 
 
 if __name__ == "__main__":
