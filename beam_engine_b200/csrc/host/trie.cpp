@@ -40,6 +40,9 @@ struct be_trie {
   std::vector<int32_t> level_memo;  // per call scratch
   std::vector<int32_t> memo_gen;
   int32_t gen = 0;
+  std::vector<int32_t> level_stack;  // scratch of level()
+  std::vector<int32_t> node_mark, node_val, page_mark;   // stamped scratch of the builders
+  int32_t stamp = 0;
   int64_t warnings = 0;
 
   int alloc(int32_t* out) {
@@ -85,7 +88,8 @@ struct be_trie {
   }
   int32_t level(int32_t n) {
     // level(root) = 0; level(n) = level(parent) + (parent has > 1 children)
-    std::vector<int32_t> stack;
+    auto& stack = level_stack;
+    stack.clear();
     int32_t cur = n;
     while (cur >= 0 && memo_gen[cur] != gen) {
       stack.push_back(cur);
@@ -106,6 +110,15 @@ struct be_trie {
       level_memo.resize(nodes.size(), 0);
       memo_gen.resize(nodes.size(), 0);
     }
+  }
+  // fresh stamp for node_mark / page_mark (a mark equals `stamp` = set in this pass)
+  int32_t next_stamp() {
+    if (node_mark.size() < nodes.size()) {
+      node_mark.resize(nodes.size(), 0);
+      node_val.resize(nodes.size(), 0);
+    }
+    if ((int)page_mark.size() < max_pages) page_mark.resize(max_pages, 0);
+    return ++stamp;
   }
 };
 
@@ -337,8 +350,13 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
   struct Seg {
     int32_t first, last;  // indices into the candidate's path
   };
-  std::vector<std::vector<int32_t>> paths(ncand);
-  std::vector<std::vector<Seg>> segs(ncand);  // by level
+  static thread_local std::vector<std::vector<int32_t>> paths;
+  static thread_local std::vector<std::vector<Seg>> segs;  // by level
+  if ((int)paths.size() < ncand) {
+    paths.resize(ncand);
+    segs.resize(ncand);
+  }
+  for (int c = 0; c < ncand; ++c) segs[c].clear();
   int top = 0;
   for (int c = 0; c < ncand; ++c) {
     if (!t->valid(cand_leaf[c])) {
@@ -361,17 +379,17 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
     return -BE_ECAPACITY;
   }
   int gbase = 0, pbase = 0;
-  std::unordered_map<int32_t, int> key_to_group;
-  std::vector<int32_t> seen;
+  struct G {
+    int cand0, count;
+    Seg seg;
+  };
+  static thread_local std::vector<G> groups;
   for (int lv = 0; lv < nlev; ++lv) {
     level_group_ptr[lv] = gbase;
     level_page_ptr[lv] = pbase;
-    key_to_group.clear();
-    struct G {
-      int cand0, count;
-      Seg seg;
-    };
-    std::vector<G> groups;
+    // group of a key node this level: node_val[key] when node_mark[key] == stamp
+    const int32_t kst = t->next_stamp();
+    groups.clear();
     for (int c = 0; c < ncand; ++c) {
       const auto& sg = segs[c];
       Seg s = (lv < (int)sg.size() && sg[lv].first >= 0) ? sg[lv] : sg.back();
@@ -380,12 +398,12 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
           if (sg[k].first >= 0) { s = sg[k]; break; }
       }
       const int32_t key = paths[c][s.last];
-      auto it = key_to_group.find(key);
-      if (it == key_to_group.end()) {
-        key_to_group[key] = (int)groups.size();
+      if (t->node_mark[key] != kst) {
+        t->node_mark[key] = kst;
+        t->node_val[key] = (int32_t)groups.size();
         groups.push_back({c, 1, s});
       } else {
-        groups[it->second].count++;
+        groups[t->node_val[key]].count++;
       }
     }
     if (gbase + (int)groups.size() > cap_groups) {
@@ -402,11 +420,13 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
     for (size_t gi = 0; gi < groups.size(); ++gi) {
       const auto& g = groups[gi];
       const auto& p = paths[g.cand0];
-      seen.clear();
+      const int32_t pst = t->next_stamp();   // pages already listed for this group
       for (int i = g.seg.first; i <= g.seg.last; ++i) {
         const int32_t pg = t->nodes[p[i]].page;
-        if (std::find(seen.begin(), seen.end(), pg) != seen.end()) continue;
-        seen.push_back(pg);
+        if (pg >= 0 && pg < t->max_pages) {
+          if (t->page_mark[pg] == pst) continue;
+          t->page_mark[pg] = pst;
+        }
         if (pbase + npages >= cap_pages) {
           set_error("be_cascade_build: page capacity %d exceeded", cap_pages);
           return -BE_ECAPACITY;
@@ -653,26 +673,34 @@ int be_fasttree_prepare(int num_nodes, const int32_t* node_parent, const int32_t
 int be_vanilla_select(int n, int k, const double* parent_scores, const int32_t* tokens,
                       const double* logps, int beam_size, int32_t* child_ptr,
                       int32_t* child_tokens, double* child_scores) {
+  // Global top-beam_size of parent + logp in the order of a stable sort by
+  // score (ties: candidate order, then top-k order), then grouped by parent.
+  // Only the first beam_size of that order matter, so a partial sort with the
+  // index as the tie-break gives the same result as the full stable sort.
   const int64_t total = (int64_t)n * k;
-  std::vector<int64_t> idx(total);
-  std::vector<double> sc(total);
+  static thread_local std::vector<int64_t> idx;
+  static thread_local std::vector<double> sc;
+  static thread_local std::vector<int32_t> cnt;
+  idx.resize(total);
+  sc.resize(total);
   for (int64_t e = 0; e < total; ++e) {
     idx[e] = e;
     sc[e] = parent_scores[e / k] + logps[e];
   }
-  std::stable_sort(idx.begin(), idx.end(), [&](int64_t a, int64_t b) { return sc[a] > sc[b]; });
   const int64_t keep = std::min<int64_t>(beam_size, total);
-  std::vector<std::vector<int64_t>> per(n);
-  for (int64_t r = 0; r < keep; ++r) per[idx[r] / k].push_back(idx[r]);
-  int o = 0;
-  child_ptr[0] = 0;
-  for (int i = 0; i < n; ++i) {
-    for (int64_t e : per[i]) {
-      child_tokens[o] = tokens[e];
-      child_scores[o] = sc[e];
-      ++o;
-    }
-    child_ptr[i + 1] = o;
+  std::partial_sort(idx.begin(), idx.begin() + keep, idx.end(), [&](int64_t a, int64_t b) {
+    return sc[a] > sc[b] || (!(sc[b] > sc[a]) && a < b);
+  });
+  // group the kept candidates by parent, each parent's in score order
+  cnt.assign(n + 1, 0);
+  for (int64_t r = 0; r < keep; ++r) cnt[idx[r] / k + 1]++;
+  for (int i = 0; i < n; ++i) cnt[i + 1] += cnt[i];
+  for (int i = 0; i <= n; ++i) child_ptr[i] = cnt[i];
+  for (int64_t r = 0; r < keep; ++r) {
+    const int64_t e = idx[r];
+    const int o = cnt[e / k]++;
+    child_tokens[o] = tokens[e];
+    child_scores[o] = sc[e];
   }
   return BE_OK;
 }

@@ -37,6 +37,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "beam decode tokens/s, Llama-3-8B-shape W=16; paged attn HBM GB/s vs peak"
+# DRAM bytes per algorithmic byte of the attention launch, from one ncu capture of
+# the tcgen05 prefix kernel on the cfg2 op case (dram read+write 8.57 MB for
+# 8.39 MB of K+V; partial rows stay in L2); traffic scales with the tokens read
+TRAFFIC_RATIO = 8.57 / 8.388608
+TRAFFIC_SOURCE = ("scaled: ncu dram__bytes_read+write of attn_umma_kernel on the cfg2 op case "
+                  "(profiles/attn_umma_cfg2.md) x this launch's algorithmic bytes")
 PROMPTS, PROMPT_LEN, BEAM, NEW_TOKENS, PAGE = 8, 1024, 16, 128, 16
 
 
@@ -248,7 +254,9 @@ def run_b200(args, rank, world, local_rank):
                                                                 else "tp1"),
                    "l2": "no flush needed: each step reads 15 GB of weights (> 126 MB L2)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "frac": round(achieved / hbm, 4),
+                     "traffic": round(TRAFFIC_RATIO * bytes_total / max(len(attn_ms), 1)),
+                     "traffic_source": TRAFFIC_SOURCE,
                      "kernel": "be_attn_run_fixed per layer (tcgen05 prefix + all-heads suffix + "
                                "LSE merge), timed by event nodes inside the step graph",
                      "peak_source": src,
