@@ -150,8 +150,8 @@ def run_b200(args, rank, world, local_rank):
                               + 2 * nq * model.Hq * model.D * 2)
             plan_stats.append((nq, inf.n_work, inf.n_work_wide, inf.n_parts, inf.n_merge))
             # per layer: 2 add_rmsnorm, rope_append, silu_mul + attention (tcgen05 wide,
-            # all-heads narrow, LSE merge); final norm
-            launches["n"] += cfg["num_hidden_layers"] * (4 + 3) + 1
+            # all-heads narrow, LSE merge); final norm; fused log-softmax / top-k
+            launches["n"] += cfg["num_hidden_layers"] * (4 + 3) + 1 + 1
 
     gen.plan_hook = plan_hook
     orig_apply = gen._apply
@@ -257,8 +257,9 @@ def run_b200(args, rank, world, local_rank):
                      "frac": round(achieved / hbm, 4),
                      "traffic": round(TRAFFIC_RATIO * bytes_total / max(len(attn_ms), 1)),
                      "traffic_source": TRAFFIC_SOURCE,
-                     "kernel": "be_attn_run_fixed per layer (tcgen05 prefix + all-heads suffix + "
-                               "LSE merge), timed by event nodes inside the step graph",
+                     "kernel": "be_attn_run_fixed_2s per layer (tcgen05 prefix tiles, all-heads "
+                               "suffix tiles on a second stream, LSE merge), timed by event "
+                               "nodes inside the step graph",
                      "peak_source": src,
                      "avg_launch_us": round(attn_total_ms / max(len(attn_ms), 1) * 1e3, 2),
                      "bytes_per_launch": round(bytes_total / max(len(attn_ms), 1)),
