@@ -11,3 +11,4 @@
 #include "attn_noalloc.cu"
 #include "model_ops.cu"
 #include "select_ops.cu"
+#include "gemm.cu"

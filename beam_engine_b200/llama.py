@@ -4,17 +4,22 @@ Llama, ``src/beam_engine/models/modeling_llama.py``), B200 layout.
 Per layer: fused residual-add + RMSNorm -> one QKV GEMM -> fused RoPE + K/V
 append into the pages -> paged attention (cascade / prefill / tree plan) ->
 O GEMM -> fused add + RMSNorm -> one gate|up GEMM -> SiLU*up -> down GEMM.
-GEMMs are cuBLAS (torch.mm on pre-fused weights); every other op is a kernel
-of ``libbeam_b200.so``.  Tensor parallelism (``tp``) shards q/k/v heads, the
+GEMMs with at most 128 rows (the decode step) run on ``be_gemm_tn``, the
+library's weight-streaming tcgen05 GEMM (BE_GEMM=0 selects cuBLAS through
+torch.mm); larger ones (prefill) on cuBLAS.  Every other op is a kernel of
+``libbeam_b200.so``.  Tensor parallelism (``tp``) shards q/k/v heads, the
 O-projection rows, gate/up columns and down rows, with one all-reduce after
 the O and down projections.
 """
 from __future__ import annotations
 
 import ctypes as C
+import os
 from typing import Optional
 
 import torch
+
+from . import _lib
 
 from ._lib import check, lib
 from .page_table import dtype_code, stream_ptr
@@ -79,7 +84,30 @@ class BeamLlama:
         self.inv_freq = inv_freq_table(D, float(c["rope_theta"]), self.device)
         self.dt = dtype_code(dtype)
         self.qkv_width = (Hq + 2 * Hkv) * D
+        self.use_gemm = (os.environ.get("BE_GEMM", "1") != "0" and dtype == torch.bfloat16
+                         and self.device.type == "cuda")
+        self._gemm_ws = None
         del weights
+
+    def _mm(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor):
+        """out = a @ w.T (a [T, K], w [N, K] row-major, out [T, N])."""
+        T, K = a.shape
+        N = w.shape[0]
+        if (self.use_gemm and T <= 128 and N >= 128 and K % 64 == 0 and a.stride(1) == 1
+                and a.stride(0) % 8 == 0 and w.is_contiguous() and out.stride(1) == 1
+                and out.dtype in (torch.bfloat16, torch.float32)):
+            if self._gemm_ws is None:   # split-K partials: 8 M floats (32 MB)
+                self._gemm_ws = torch.empty(8 << 20, dtype=torch.float32, device=self.device)
+            check(lib().be_gemm_tn(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0),
+                                   out.data_ptr(), out.stride(0), T, N, K,
+                                   _lib.BE_BF16 if out.dtype == torch.bfloat16 else _lib.BE_F32,
+                                   0, self._gemm_ws.data_ptr(), self._gemm_ws.numel(),
+                                   stream_ptr(self.device)), "be_gemm_tn")
+            return out
+        if out.dtype == a.dtype:
+            return torch.mm(a, w.t(), out=out)
+        out.copy_(torch.mm(a, w.t()))
+        return out
 
     def parameters(self):
         yield self.embed
@@ -109,7 +137,7 @@ class BeamLlama:
             check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr() if have_delta else None,
                                    self.n_in[i].data_ptr(), h.data_ptr(), n, self.H, self.eps,
                                    self.dt, st), "add_rmsnorm")
-            torch.mm(h, self.w_qkv[i].t(), out=qkv)
+            self._mm(h, self.w_qkv[i], qkv)
             check(L.be_rope_qkv_append(qkv.data_ptr(), self.qkv_width, n, self.Hq, self.Hkv, self.D,
                                        positions.data_ptr(), self.inv_freq.data_ptr(),
                                        pool[i].data_ptr(), P, ps, write_pages.data_ptr(),
@@ -117,19 +145,20 @@ class BeamLlama:
             attention.run(i, qkv, att)
             if layer_hook is not None:
                 layer_hook(i)
-            torch.mm(att, self.w_o[i].t(), out=delta)
+            self._mm(att, self.w_o[i], delta)
             self._all_reduce(delta)
             check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.n_post[i].data_ptr(),
                                    h.data_ptr(), n, self.H, self.eps, self.dt, st), "add_rmsnorm")
-            torch.mm(h, self.w_gu[i].t(), out=gu)
+            self._mm(h, self.w_gu[i], gu)
             check(L.be_silu_mul(gu.data_ptr(), act.data_ptr(), n, self.F, self.dt, st), "silu_mul")
-            torch.mm(act, self.w_down[i].t(), out=delta)
+            self._mm(act, self.w_down[i], delta)
             self._all_reduce(delta)
             have_delta = True
         check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.norm.data_ptr(), h.data_ptr(),
                                n, self.H, self.eps, self.dt, st), "final norm")
         hs = h if logits_rows is None else h.index_select(0, logits_rows)
-        return torch.mm(hs, self.lm_head.t()).float()
+        logits = torch.empty((hs.shape[0], self.lm_head.shape[0]), dtype=torch.float32, device=dev)
+        return self._mm(hs, self.lm_head, logits)
 
     def _all_reduce(self, t):
         if self.tp is not None and self.tp.size > 1:

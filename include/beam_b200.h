@@ -263,6 +263,17 @@ int be_logsoftmax_topk(const float* logits, int64_t ld, int rows, int v, float t
                        int k, int64_t vocab_offset, int full_vocab, float* out_val,
                        int64_t* out_idx, float* row_max, float* row_sumexp, void* stream);
 
+/* Decode projection GEMM (the q/k/v, o, gate/up, down and lm_head matmuls of
+ * LlamaAttention / LlamaMLP, modeling_llama.py:428-562, 577-621, which the
+ * reference runs as torch linears): Y[T][N] = X[T][K] * W[N][K]^T, bf16
+ * operands, fp32 accumulate, Y bf16 (out_dtype BE_BF16) or f32.  T <= 128,
+ * N >= 128, K % 64 == 0, row strides ldx / ldw multiples of 8 elements.
+ * split_k 0 = automatic (about two CTAs per SM); split-K partials go to
+ * `workspace` (splits * T * N floats; a smaller workspace lowers the split). */
+int be_gemm_tn(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+               int T, int N, int K, int out_dtype, int split_k, float* workspace,
+               int64_t workspace_floats, void* stream);
+
 /* ------------------------------------------------------------------------
  * Host page manager (no CUDA): FIFO page allocator + beam trie.  One
  * be_trie backs one PageTable and the BeamState objects over it.

@@ -381,3 +381,39 @@ def test_logsoftmax_topk_ties_and_slice():
     ref_m = logits.amax(-1)
     ref_s = torch.exp(logits - ref_m[:, None]).sum(-1)
     assert torch.allclose(m, ref_m) and torch.allclose(s, ref_s, rtol=1e-5)
+
+
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("T,N,K,out", [(128, 4096, 4096, "bf16"), (128, 6144, 4096, "bf16"),
+                                       (128, 4096, 14336, "bf16"), (128, 28672, 4096, "bf16"),
+                                       (128, 12800, 4096, "f32"), (77, 384, 256, "bf16"),
+                                       (5, 256, 192, "f32"), (128, 200, 512, "bf16")])
+def test_gemm_tn_matches_torch(T, N, K, out):
+    """be_gemm_tn (tcgen05 weight-streaming GEMM, split-K) against torch.mm in
+    fp32 on the same bf16 operands: within bf16 output rounding."""
+    from beam_engine_b200 import _lib
+    d = dev()
+    g = torch.Generator(device=d).manual_seed(T + N + K)
+    x = (torch.randn((T, K), generator=g, device=d) * 0.5).to(torch.bfloat16)
+    w = (torch.randn((N, K), generator=g, device=d) * 0.02).to(torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    ot = torch.bfloat16 if out == "bf16" else torch.float32
+    y = torch.full((T, N), float("nan"), dtype=ot, device=d)
+    ws = torch.empty(8 << 20, dtype=torch.float32, device=d)
+    _lib.check(_lib.lib().be_gemm_tn(x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, T, N, K,
+                                     _lib.BE_BF16 if out == "bf16" else _lib.BE_F32, 0,
+                                     ws.data_ptr(), ws.numel(), None))
+    torch.cuda.synchronize()
+    err = (y.float() - ref).abs()
+    tol = (1e-2 if out == "bf16" else 1e-4) * ref.abs() + 1e-3
+    assert bool((err <= tol).all()), float(err.max())
+
+
+def test_gemm_tn_rejects_unsupported_shapes():
+    from beam_engine_b200 import _lib
+    d = dev()
+    x = torch.zeros((200, 128), dtype=torch.bfloat16, device=d)
+    w = torch.zeros((128, 128), dtype=torch.bfloat16, device=d)
+    y = torch.zeros((200, 128), dtype=torch.bfloat16, device=d)
+    assert _lib.lib().be_gemm_tn(x.data_ptr(), 128, w.data_ptr(), 128, y.data_ptr(), 128, 200, 128,
+                                 128, _lib.BE_BF16, 0, None, 0, None) == _lib.BE_EINVAL
