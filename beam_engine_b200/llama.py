@@ -4,10 +4,10 @@ Llama, ``src/beam_engine/models/modeling_llama.py``), B200 layout.
 Per layer: fused residual-add + RMSNorm -> one QKV GEMM -> fused RoPE + K/V
 append into the pages -> paged attention (cascade / prefill / tree plan) ->
 O GEMM -> fused add + RMSNorm -> one gate|up GEMM -> SiLU*up -> down GEMM.
-GEMMs with at most 128 rows (the decode step) run on ``be_gemm_tn``, the
-library's weight-streaming tcgen05 GEMM (BE_GEMM=0 selects cuBLAS through
-torch.mm); larger ones (prefill) on cuBLAS.  Every other op is a kernel of
-``libbeam_b200.so``.  Tensor parallelism (``tp``) shards q/k/v heads, the
+GEMMs run on cuBLAS (torch.mm on pre-fused weights); BE_GEMM=1 routes the
+ones with at most 128 rows (the decode step) to ``be_gemm_tn``, the library's
+weight-streaming tcgen05 GEMM (correct, not yet faster than cuBLAS on these
+shapes).  Every other op is a kernel of ``libbeam_b200.so``.  Tensor parallelism (``tp``) shards q/k/v heads, the
 O-projection rows, gate/up columns and down rows, with one all-reduce after
 the O and down projections.
 """
@@ -84,7 +84,7 @@ class BeamLlama:
         self.inv_freq = inv_freq_table(D, float(c["rope_theta"]), self.device)
         self.dt = dtype_code(dtype)
         self.qkv_width = (Hq + 2 * Hkv) * D
-        self.use_gemm = (os.environ.get("BE_GEMM", "1") != "0" and dtype == torch.bfloat16
+        self.use_gemm = (os.environ.get("BE_GEMM", "0") == "1" and dtype == torch.bfloat16
                          and self.device.type == "cuda")
         self._gemm_ws = None
         del weights
