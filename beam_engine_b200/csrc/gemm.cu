@@ -12,8 +12,11 @@
 //     to ~2 CTAs per SM; W and X tiles (64 K-elements, 128-byte swizzle) stream
 //     by TMA through a 3-stage ring (two CTAs per SM keep 6 stages in flight);
 //   * one elected lane issues TMA, one elected lane issues the MMAs, then all
-//     four warps drain TMEM (warp w holds features 32w..32w+31) and write Y, or
-//     with split-K an fp32 slice that gemm_reduce_kernel sums into Y.
+//     four warps drain TMEM (warp w holds features 32w..32w+31) and write Y;
+//   * split-K runs as a thread-block cluster along the K splits: each CTA parks
+//     its fp32 partial tile in its own shared memory, and after a cluster
+//     barrier CTA r sums token rows r/S.. of all S partials over distributed
+//     shared memory and writes them -- no partials in HBM, no second kernel.
 // Every wait is bounded (BE_EDEVICE_TIMEOUT, then drain and free the TMEM).
 namespace be {
 
@@ -38,8 +41,8 @@ template <typename OutT>
 __global__ void __launch_bounds__(128) gemm_tn_kernel(const __grid_constant__ CUtensorMap map_w,
                                                       const __grid_constant__ CUtensorMap map_x,
                                                       OutT* __restrict__ y, int64_t ldy,
-                                                      float* __restrict__ ws, int T, int N, int K,
-                                                      int kb_per_split, int x_rows) {
+                                                      int T, int N, int K, int kb_per_split,
+                                                      int x_rows) {
   extern __shared__ char smem_raw[];
   char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~uintptr_t(1023));
@@ -116,25 +119,63 @@ __global__ void __launch_bounds__(128) gemm_tn_kernel(const __grid_constant__ CU
   const bool ok = mbar_wait(done, 0) && !*abort_flag;
   tc_fence_after();
   const int f = m0 + warp * 32 + lane;
-  if (ok) {
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    for (int c0 = 0; c0 < T; c0 += 32) {   // T is uniform: whole warps load together
-      uint32_t v[32];
-      tmem_ld32_nw(trow + c0, v);
-      tmem_wait();
-      if (f < N) {
-        if (ws) {
-          float* dst = ws + ((int64_t)split * T) * N + f;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (c0 + j < T) dst[(int64_t)(c0 + j) * N] = __uint_as_float(v[j]);
-        } else {
+  const int S = gridDim.y;   // CTAs of the cluster = K splits
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  if (S == 1) {
+    if (ok) {
+      for (int c0 = 0; c0 < T; c0 += 32) {   // T is uniform: whole warps load together
+        uint32_t v[32];
+        tmem_ld32_nw(trow + c0, v);
+        tmem_wait();
+        if (f < N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (c0 + j < T) y[(int64_t)(c0 + j) * ldy + f] = from_f<OutT>(__uint_as_float(v[j]));
         }
       }
     }
+  } else {
+    // partial tile -> own shared memory [token][128 features] (the stage ring is idle now)
+    float* part = reinterpret_cast<float*>(smem);
+    for (int c0 = 0; c0 < T; c0 += 32) {
+      uint32_t v[32];
+      if (ok) {
+        tmem_ld32_nw(trow + c0, v);
+        tmem_wait();
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < T) part[(c0 + j) * GM_BM + warp * 32 + lane] = ok ? __uint_as_float(v[j]) : 0.f;
+    }
+    cluster_sync();   // every partial is in place (release / acquire across the cluster)
+    // CTA rank r sums token rows [r*T/S, (r+1)*T/S) of all partials, 4 features per thread
+    const uint32_t rank = cluster_rank();
+    const int t0 = (int)((int64_t)rank * T / S), t1 = (int)((int64_t)(rank + 1) * T / S);
+    const uint32_t base = smem_u32(part);
+    for (int e = tid; e < (t1 - t0) * (GM_BM / 4); e += blockDim.x) {
+      const int t = t0 + e / (GM_BM / 4), f4 = (e % (GM_BM / 4)) * 4;
+      const uint32_t off = base + (uint32_t)((t * GM_BM + f4) * 4);
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (int q = 0; q < S; ++q) {
+        const uint32_t pa = map_peer(off, (uint32_t)q);
+        float b0, b1, b2, b3;
+        asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+                     : "=f"(b0), "=f"(b1), "=f"(b2), "=f"(b3)
+                     : "r"(pa)
+                     : "memory");
+        a0 += b0;
+        a1 += b1;
+        a2 += b2;
+        a3 += b3;
+      }
+      const int fg = m0 + f4;
+      OutT* dst = y + (int64_t)t * ldy + fg;
+      if (fg + 0 < N) dst[0] = from_f<OutT>(a0);
+      if (fg + 1 < N) dst[1] = from_f<OutT>(a1);
+      if (fg + 2 < N) dst[2] = from_f<OutT>(a2);
+      if (fg + 3 < N) dst[3] = from_f<OutT>(a3);
+    }
+    cluster_sync();   // no CTA leaves while a peer may still read its partials
   }
   // ---- teardown: on abort, loads still in flight land before the CTA exits ----
   if (tid == 0 && *abort_flag) {
@@ -146,20 +187,6 @@ __global__ void __launch_bounds__(128) gemm_tn_kernel(const __grid_constant__ CU
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(GM_BN)
                  : "memory");
-  }
-}
-
-// Y[t][n] = sum over splits of ws[s][t][n]
-template <typename OutT>
-__global__ void gemm_reduce_kernel(const float* __restrict__ ws, OutT* __restrict__ y, int64_t ldy,
-                                   int T, int N, int splits) {
-  const int64_t total = (int64_t)T * N;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < splits; ++s) acc += ws[(int64_t)s * total + e];
-    const int64_t t = e / N, n = e - t * N;
-    y[t * ldy + n] = from_f<OutT>(acc);
   }
 }
 
@@ -222,9 +249,8 @@ static int get_map2(const void* p, int64_t rows, int64_t cols, int64_t ld, int b
 }
 
 template <typename OutT>
-static int launch_gemm(const CUtensorMap& mw, const CUtensorMap& mx, void* y, int64_t ldy,
-                       float* ws, int T, int N, int K, int splits, int kb_per_split, int x_rows,
-                       cudaStream_t st) {
+static int launch_gemm(const CUtensorMap& mw, const CUtensorMap& mx, void* y, int64_t ldy, int T,
+                       int N, int K, int splits, int kb_per_split, int x_rows, cudaStream_t st) {
   static bool set = false;
   if (!set) {
     BE_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_kernel<OutT>,
@@ -232,18 +258,20 @@ static int launch_gemm(const CUtensorMap& mw, const CUtensorMap& mx, void* y, in
                                        (int)gm_smem_bytes()));
     set = true;
   }
-  const dim3 grid((N + GM_BM - 1) / GM_BM, splits);
-  gemm_tn_kernel<OutT><<<grid, 128, gm_smem_bytes(), st>>>(
-      mw, mx, reinterpret_cast<OutT*>(y), ldy, splits > 1 ? ws : nullptr, T, N, K, kb_per_split,
-      x_rows);
-  BE_LAUNCH_CHECK();
-  if (splits > 1) {
-    const int64_t total = (int64_t)T * N;
-    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
-    gemm_reduce_kernel<OutT><<<blocks, 256, 0, st>>>(ws, reinterpret_cast<OutT*>(y), ldy, T, N,
-                                                     splits);
-    BE_LAUNCH_CHECK();
-  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((N + GM_BM - 1) / GM_BM, splits, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = gm_smem_bytes();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = splits;   // the K splits of one tile form a cluster
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  BE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_kernel<OutT>, mw, mx, reinterpret_cast<OutT*>(y),
+                                   ldy, T, N, K, kb_per_split, x_rows));
   return BE_OK;
 }
 
@@ -264,21 +292,25 @@ extern "C" int be_gemm_tn(const void* x, int64_t ldx, const void* w, int64_t ldw
   }
   const int tiles = (N + GM_BM - 1) / GM_BM;
   const int kb = K / GM_BK;
+  // split-K = cluster size: a power of two <= 8 with about two CTAs per SM in
+  // total and at least 4 K blocks per split
   int splits = split_k;
-  if (splits <= 0) {   // auto: about two CTAs per SM, at least 4 K blocks per split
+  if (splits <= 0) {
     const int sms = num_sms_cached();
-    splits = std::max(1, std::min(kb / 4, (2 * sms) / tiles));
-    splits = std::min(splits, 16);
+    splits = 1;
+    while (splits < 8 && tiles * splits * 2 <= 2 * sms && kb / (splits * 2) >= 4) splits *= 2;
   }
-  int per = (kb + splits - 1) / splits;
-  splits = (kb + per - 1) / per;   // no empty split
-  if (splits > 1 && (!workspace || (int64_t)splits * T * N > workspace_floats)) {
-    // not enough workspace for that split: the largest split that fits
-    const int64_t fit = workspace ? workspace_floats / ((int64_t)T * N) : 1;
-    splits = (int)std::max<int64_t>(1, std::min<int64_t>(splits, fit));
-    per = (kb + splits - 1) / splits;
-    splits = (kb + per - 1) / per;
+  if (splits != 1 && splits != 2 && splits != 4 && splits != 8) {
+    set_error("be_gemm_tn: split_k %d must be 1, 2, 4 or 8", splits);
+    return BE_EINVAL;
   }
+  const int per = (kb + splits - 1) / splits;
+  if ((int64_t)per * (splits - 1) >= kb) {
+    set_error("be_gemm_tn: split_k %d leaves an empty K range (K %d)", splits, K);
+    return BE_EINVAL;
+  }
+  (void)workspace;
+  (void)workspace_floats;
   // X rows per tile: T rounded up to 8 (rows past T in the box read as zeros;
   // MMA columns past the box only feed output columns that are never stored)
   const int x_rows = std::min(GM_BN, (T + 7) / 8 * 8);
@@ -289,6 +321,6 @@ extern "C" int be_gemm_tn(const void* x, int64_t ldx, const void* w, int64_t ldw
   if (rc != BE_OK) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   return out_dtype == BE_BF16
-             ? launch_gemm<__nv_bfloat16>(mw, mx, y, ldy, workspace, T, N, K, splits, per, x_rows, st)
-             : launch_gemm<float>(mw, mx, y, ldy, workspace, T, N, K, splits, per, x_rows, st);
+             ? launch_gemm<__nv_bfloat16>(mw, mx, y, ldy, T, N, K, splits, per, x_rows, st)
+             : launch_gemm<float>(mw, mx, y, ldy, T, N, K, splits, per, x_rows, st);
 }
