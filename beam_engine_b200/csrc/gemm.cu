@@ -152,28 +152,47 @@ __global__ void __launch_bounds__(128) gemm_tn_kernel(const __grid_constant__ CU
     const uint32_t rank = cluster_rank();
     const int t0 = (int)((int64_t)rank * T / S), t1 = (int)((int64_t)(rank + 1) * T / S);
     const uint32_t base = smem_u32(part);
-    for (int e = tid; e < (t1 - t0) * (GM_BM / 4); e += blockDim.x) {
-      const int t = t0 + e / (GM_BM / 4), f4 = (e % (GM_BM / 4)) * 4;
-      const uint32_t off = base + (uint32_t)((t * GM_BM + f4) * 4);
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    const int n_e = (t1 - t0) * (GM_BM / 4);
+    // four float4 groups per thread per round, every peer's load issued before
+    // any sum, so the distributed-shared-memory latency is paid once per round
+    for (int e0 = tid; e0 < n_e; e0 += 4 * 128) {
+      float4 acc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int q = 0; q < S; ++q) {
-        const uint32_t pa = map_peer(off, (uint32_t)q);
-        float b0, b1, b2, b3;
-        asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
-                     : "=f"(b0), "=f"(b1), "=f"(b2), "=f"(b3)
-                     : "r"(pa)
-                     : "memory");
-        a0 += b0;
-        a1 += b1;
-        a2 += b2;
-        a3 += b3;
+        float4 b[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = e0 + u * 128;
+          b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (e < n_e) {
+            const int t = t0 + e / (GM_BM / 4), f4 = (e % (GM_BM / 4)) * 4;
+            const uint32_t pa = map_peer(base + (uint32_t)((t * GM_BM + f4) * 4), (uint32_t)q);
+            asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+                         : "=f"(b[u].x), "=f"(b[u].y), "=f"(b[u].z), "=f"(b[u].w)
+                         : "r"(pa)
+                         : "memory");
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          acc[u].x += b[u].x;
+          acc[u].y += b[u].y;
+          acc[u].z += b[u].z;
+          acc[u].w += b[u].w;
+        }
       }
-      const int fg = m0 + f4;
-      OutT* dst = y + (int64_t)t * ldy + fg;
-      if (fg + 0 < N) dst[0] = from_f<OutT>(a0);
-      if (fg + 1 < N) dst[1] = from_f<OutT>(a1);
-      if (fg + 2 < N) dst[2] = from_f<OutT>(a2);
-      if (fg + 3 < N) dst[3] = from_f<OutT>(a3);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int e = e0 + u * 128;
+        if (e >= n_e) continue;
+        const int t = t0 + e / (GM_BM / 4), fg = m0 + (e % (GM_BM / 4)) * 4;
+        OutT* dst = y + (int64_t)t * ldy + fg;
+        if (fg + 0 < N) dst[0] = from_f<OutT>(acc[u].x);
+        if (fg + 1 < N) dst[1] = from_f<OutT>(acc[u].y);
+        if (fg + 2 < N) dst[2] = from_f<OutT>(acc[u].z);
+        if (fg + 3 < N) dst[3] = from_f<OutT>(acc[u].w);
+      }
     }
     cluster_sync();   // no CTA leaves while a peer may still read its partials
   }
