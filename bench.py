@@ -44,6 +44,27 @@ TRAFFIC_RATIO = 8.57 / 8.388608
 TRAFFIC_SOURCE = ("scaled: ncu dram__bytes_read+write of attn_umma_kernel on the cfg2 op case "
                   "(profiles/attn_umma_cfg2.md) x this launch's algorithmic bytes")
 PROMPTS, PROMPT_LEN, BEAM, NEW_TOKENS, PAGE = 8, 1024, 16, 128, 16
+MODEL_NAME, KERNEL = "LLAMA3_8B", "cascade"
+WORKLOAD = ("cfg3: Llama-3-8B shape, 8 prompts x 1024 tokens, beam width 16, 128 new tokens, "
+            "page size 16, cascade attention")
+# the BASELINE configs the decode bench can run (--config); cfg3 is the default
+CONFIGS = {
+    "cfg3": dict(PROMPTS=8, PROMPT_LEN=1024, BEAM=16, NEW_TOKENS=128, MODEL_NAME="LLAMA3_8B",
+                 KERNEL="cascade", WORKLOAD=WORKLOAD),
+    "cfg4": dict(PROMPTS=1, PROMPT_LEN=4096, BEAM=32, NEW_TOKENS=256, MODEL_NAME="LLAMA3_8B",
+                 KERNEL="auto",
+                 WORKLOAD="cfg4: Llama-3-8B shape, 1 prompt x 4096 tokens, beam width 32, 256 new "
+                          "tokens, page size 16, tree-vs-cascade picker (kernel_type auto); "
+                          "random-init logits reparent most beams every step (churn reported)"),
+    "cfg5": dict(PROMPTS=4, PROMPT_LEN=2048, BEAM=16, NEW_TOKENS=128, MODEL_NAME="LLAMA3_70B",
+                 KERNEL="cascade",
+                 WORKLOAD="cfg5: Llama-3-70B shape, 4 prompts x 2048 tokens, beam width 16, 128 "
+                          "new tokens, page size 16, cascade attention"),
+}
+
+
+def use_config(name):
+    globals().update(CONFIGS[name])
 
 
 def peaks():
@@ -110,12 +131,13 @@ def run_b200(args, rank, world, local_rank):
 
     from beam_engine_b200.beam import BeamSearchGenerator
     from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy
-    from beam_engine_b200.configs import LLAMA3_8B, param_count
+    from beam_engine_b200 import configs as model_configs
+    from beam_engine_b200.configs import param_count
     from beam_engine_b200.llama import BeamLlama
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    cfg = dict(LLAMA3_8B)
+    cfg = dict(getattr(model_configs, MODEL_NAME))
     tp_mode = world > 1 and args.parallel == "tp"
     tp = None
     if tp_mode:
@@ -126,7 +148,7 @@ def run_b200(args, rank, world, local_rank):
     seed = 1234 if tp_mode else 1234 + rank
     model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=dev, seed=seed, tp=tp)
     gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=PAGE,
-                              max_num_pages=args.pages)
+                              max_num_pages=args.pages, kernel_type=KERNEL)
     g = torch.Generator().manual_seed(0 if tp_mode else rank)
     prompts = [torch.randint(0, cfg["vocab_size"], (PROMPT_LEN,), generator=g).tolist()
                for _ in range(PROMPTS)]
@@ -156,8 +178,15 @@ def run_b200(args, rank, world, local_rank):
     gen.plan_hook = plan_hook
     orig_apply = gen._apply
 
+    churn = []
+
     def apply_hook(state, *a):
         orig_apply(state, *a)
+        if timing["on"]:   # share of new beams whose parent is shared with a sibling or gone
+            cp = np.asarray(a[0])
+            kids = int(cp[-1])
+            if kids:
+                churn.append(1.0 - int((np.diff(cp) > 0).sum()) / kids)
         if timing["on"] and len(state.last_copies[0]):
             launches["n"] += 1
 
@@ -202,7 +231,9 @@ def run_b200(args, rank, world, local_rank):
     achieved = bytes_total / (attn_total_ms / 1e3) / 1e9 if attn_total_ms else 0.0
     step_bytes = (param_count(cfg) - cfg["vocab_size"] * cfg["hidden_size"]) * 2
     if args.no_e2e:
-        return dict(value=value, ms_per_step=ms_max / K, attn_us=attn_total_ms / max(len(attn_ms), 1) * 1e3,
+        return dict(value=value, ms_per_step=ms_max / K, churn=float(np.mean(churn)) if churn else None,
+                    picks=({k: gen.picks.count(k) for k in set(gen.picks)} if gen.picks else None),
+                    attn_us=attn_total_ms / max(len(attn_ms), 1) * 1e3,
                     achieved=achieved, plan_avg=[float(np.mean([p[i] for p in plan_stats])) for i in range(5)])
     # -- end-to-end: the public API call from host token ids to host beams ----
     torch.cuda.synchronize()
@@ -246,13 +277,13 @@ def run_b200(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded uniform token ids, random-init N(0,0.02) weights)",
-        "config": {"workload": "cfg3: Llama-3-8B shape, 8 prompts x 1024 tokens, beam width 16, "
-                               "128 new tokens, page size 16, cascade attention",
-                   "model": "Llama-3-8B-shape (random init)", "global_batch": PROMPTS * BEAM * replicas,
+        "config": {"workload": WORKLOAD,
+                   "model": f"{MODEL_NAME} shape (random init)", "global_batch": PROMPTS * BEAM * replicas,
                    "seq_len": PROMPT_LEN,
                    "parallelism": f"tp{world}" if tp_mode else (f"replicas x{world}" if world > 1
                                                                 else "tp1"),
-                   "l2": "no flush needed: each step reads 15 GB of weights (> 126 MB L2)"},
+                   "l2": f"no flush needed: each step reads {step_bytes / 1e9:.1f} GB of weights "
+                         "(> 126 MB L2)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4),
                      "traffic": round(TRAFFIC_RATIO * bytes_total / max(len(attn_ms), 1)),
@@ -276,6 +307,8 @@ def run_b200(args, rank, world, local_rank):
                 "includes": "prefill of 8 x 1024 prompt tokens + 127 decode steps, host ids in, "
                             "host beams out", "wall_ms": round(wall_ms, 1)},
         "gpu_launches": launches["n"],
+        "churn": round(float(np.mean(churn)), 3) if churn else None,
+        "kernel_picks": ({k: gen.picks.count(k) for k in set(gen.picks)} if gen.picks else None),
         "clocks": ev.get("clocks"),
     }
     return res
@@ -517,6 +550,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--pages", type=int, default=4096)
+    ap.add_argument("--config", default="cfg3", choices=sorted(CONFIGS),
+                    help="decode workload (BASELINE configs); the driver's line is cfg3")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
                     help="N > 1: tensor parallel over the N GPUs (default) or N independent replicas")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -529,6 +564,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end pass and print a short line (for profiling)")
     args = ap.parse_args()
+    use_config(args.config)
     wd = float(os.environ.get("BENCH_WATCHDOG_S", "0") or 0)
     if wd > 0:
         import faulthandler
@@ -556,7 +592,7 @@ def main():
                                 timeout=datetime.timedelta(seconds=180))
     res = run_b200(args, rank, world, local_rank)
     if rank == 0:
-        if not args.no_cpu_baseline and not args.no_e2e and world == 1:
+        if not args.no_cpu_baseline and not args.no_e2e and world == 1 and args.config == "cfg3":
             res["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(res), flush=True)
     if world > 1:
