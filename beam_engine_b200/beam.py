@@ -321,7 +321,7 @@ class BeamSearchGenerator:
 
     def _tree_vnodes(self, state: BeamState, n: int):
         from .fasttree import plan_vnodes
-        par, seql, kids, rptr, rl, r2t = state.tree_arrays(per_node=True)
+        par, seql, kids, rptr, rl, r2t = state.tree_arrays(per_node=True, compress=True)
         v = plan_vnodes(par, seql, kids, rptr, np.ascontiguousarray(rl) if len(rl) else
                         np.zeros(1, np.int32), r2t.shape[1], n, self.model.Hq_total,
                         self.model.Hkv_total)

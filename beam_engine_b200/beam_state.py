@@ -301,11 +301,15 @@ class BeamState:
                 self._cached_write_kv_indptr)
 
     # -- beam_state.py:414-633 ----------------------------------------------
-    def tree_arrays(self, per_node: bool = False):
+    def tree_arrays(self, per_node: bool = False, compress: bool = False):
+        """Tree nodes (BFS), their parents / lengths / child counts, request
+        lists and req_to_token.  ``compress`` merges chains of single-child trie
+        nodes into one tree node (per-node lengths), which the engine's tree
+        plans use; the reference's layout is one node per trie node."""
         n = len(self._leaves)
         nn, ml = C.c_int32(), C.c_int32()
         z = np.zeros(1, np.int32)
-        args = [self._t, n, _lib.ptr32(self._leaves), 1 if per_node else 0,
+        args = [self._t, n, _lib.ptr32(self._leaves), (1 if per_node else 0) | (2 if compress else 0),
                 self.page_table.page_size]
         check(lib().be_tree_build(*args, 0, C.byref(nn), *[_lib.ptr32(z)] * 5, 0, C.byref(ml),
                                   None, 0), "tree build")

@@ -461,6 +461,10 @@ int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node,
                   int32_t* node_children, int32_t* req_ptr, int32_t* req_list,
                   int64_t cap_req_list, int32_t* max_len, int32_t* req_to_token,
                   int64_t cap_req_to_token) {
+  // per_node bit 1: one tree node per chain of trie nodes with a single live
+  // child (a 1024-token prefix is one node, not 64); needs per-node lengths
+  const bool compress = (per_node & 2) != 0;
+  const bool own_len = (per_node & 1) != 0 || compress;
   std::vector<int32_t> roots;
   std::vector<std::vector<int32_t>> paths(ncand);
   int64_t ml = 0;
@@ -474,16 +478,45 @@ int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node,
       roots.push_back(paths[c][0]);
     ml = std::max(ml, t->seq_len(cand_leaf[c]));
   }
-  std::unordered_map<int32_t, int32_t> tid;
-  std::vector<int32_t> order;
+  // live children (on some candidate's path) of every live trie node
+  std::unordered_map<int32_t, std::vector<int32_t>> live_kids;
+  if (compress) {
+    for (int c = 0; c < ncand; ++c)
+      for (size_t i = 0; i + 1 < paths[c].size(); ++i) {
+        auto& v = live_kids[paths[c][i]];
+        if (std::find(v.begin(), v.end(), paths[c][i + 1]) == v.end()) v.push_back(paths[c][i + 1]);
+      }
+  }
+  auto chain_end = [&](int32_t n) {   // last trie node of the chain starting at n
+    if (!compress) return n;
+    for (;;) {
+      auto it = live_kids.find(n);
+      if (it == live_kids.end() || it->second.size() != 1) return n;
+      n = it->second[0];
+    }
+  };
+  auto kids_of = [&](int32_t last) -> std::vector<int32_t> {
+    if (!compress) return t->nodes[last].children;
+    auto it = live_kids.find(last);
+    return it == live_kids.end() ? std::vector<int32_t>{} : it->second;
+  };
+  // tree nodes in BFS order; a node is a chain head (one trie node unless compressed)
+  std::unordered_map<int32_t, int32_t> tid;   // trie node -> tree node (every chain member)
+  std::vector<int32_t> order, order_last;
   std::deque<int32_t> q(roots.begin(), roots.end());
   while (!q.empty()) {
     const int32_t n = q.front();
     q.pop_front();
     if (tid.count(n)) continue;
-    tid[n] = (int32_t)order.size();
+    const int32_t id = (int32_t)order.size();
+    const int32_t last = chain_end(n);
+    for (int32_t m = last;; m = t->nodes[m].parent) {
+      tid[m] = id;
+      if (m == n) break;
+    }
     order.push_back(n);
-    for (int32_t ch : t->nodes[n].children)
+    order_last.push_back(last);
+    for (int32_t ch : kids_of(last))
       if (!tid.count(ch)) q.push_back(ch);
   }
   *num_nodes = (int32_t)order.size();
@@ -496,13 +529,22 @@ int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node,
   // requests per node (candidate order)
   std::vector<std::vector<int32_t>> reqs(order.size());
   for (int c = 0; c < ncand; ++c)
-    for (int32_t n : paths[c]) reqs[tid[n]].push_back(c);
+    for (int32_t n : paths[c]) {
+      auto& r = reqs[tid[n]];
+      if (r.empty() || r.back() != c) r.push_back(c);
+    }
   int64_t rp = 0;
   for (size_t i = 0; i < order.size(); ++i) {
-    const auto& nd = t->nodes[order[i]];
-    node_parent[i] = nd.parent < 0 ? -1 : (tid.count(nd.parent) ? tid[nd.parent] : -1);
-    node_seqlen[i] = per_node ? (int32_t)nd.tokens.size() : (int32_t)t->seq_len(order[i]);
-    node_children[i] = (int32_t)nd.children.size();
+    const auto& head = t->nodes[order[i]];
+    const int32_t last = order_last[i];
+    node_parent[i] = head.parent < 0 ? -1 : (tid.count(head.parent) ? tid[head.parent] : -1);
+    int64_t len = 0;
+    for (int32_t m = last;; m = t->nodes[m].parent) {
+      len += (int64_t)t->nodes[m].tokens.size();
+      if (m == order[i]) break;
+    }
+    node_seqlen[i] = own_len ? (int32_t)len : (int32_t)t->seq_len(last);
+    node_children[i] = (int32_t)kids_of(last).size();
     req_ptr[i] = (int32_t)rp;
     for (int32_t r : reqs[i]) {
       if (rp >= cap_req_list) {

@@ -337,8 +337,10 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
                      int32_t* kv_indices, int32_t* last_page_len);
 /* BeamState._build_kv_tree_structure + _build_req_to_token
  * (beam_state.py:414-564): BFS nodes, request lists, req_to_token slot table
- * [ncand][max_len].  per_node != 0 stores each node's own length as seqlen
- * (the reference stores the cumulative length).  req_to_token == NULL: sizes only. */
+ * [ncand][max_len].  per_node bit 0 stores each node's own length as seqlen
+ * (the reference stores the cumulative length); bit 1 makes one tree node of
+ * every chain of trie nodes with a single live child (own lengths implied), a
+ * layout of this library's tree plans.  req_to_token == NULL: sizes only.   */
 int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node, int page_size,
                   int cap_nodes, int32_t* num_nodes, int32_t* node_parent, int32_t* node_seqlen,
                   int32_t* node_children, int32_t* req_ptr, int32_t* req_list,

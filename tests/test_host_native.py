@@ -215,3 +215,39 @@ def test_picker_exactness_and_cost(cascade_trees):
     assert m.cascade_us(shared, 8, 32, 128) < m.tree_us(tree_dup, 8, 32, 128)
     assert choose(cascade_trees["uneven"]["expect"]["levels"], shared, tree_dup, 8, 32, 128) == \
         "fasttree"
+
+
+@pytest.mark.parametrize("case", ["ps16_w8", "ps8_w6_churn", "ps16_w16"])
+def test_compressed_tree_plans_attend_the_same_tokens(trajectories, case):
+    """Chains of single-child trie nodes merged into one tree node give vnode
+    plans with fewer nodes and the same attention (oracle two-stage FastTree
+    attention, float64) as one node per trie node."""
+    from oracle.attention import fasttree_attention
+    rec = trajectories[case]
+    cs = rec["case"]
+    pt = cpu_table(cs["ps"], cs["pages"])
+    bs = BeamState(cs["W"], pt)
+    bs.add_root_sequence(rec["prompt"])
+    toks, sc = rec["root_children"]
+    bs.update_native(bs.leaves, np.array([0, len(toks)]), np.array(toks), np.array(sc))
+    rng = np.random.default_rng(4)
+    hq, hkv, d = 8, 2, 16
+    pool_k = rng.standard_normal((cs["pages"] * cs["ps"], hkv, d))
+    pool_v = rng.standard_normal((cs["pages"] * cs["ps"], hkv, d))
+    for si, step in enumerate(rec["steps"][:12]):
+        B = len(bs.leaves)
+        outs, sizes = [], []
+        for comp in (False, True):
+            par, seql, kids, rptr, rl, r2t = bs.tree_arrays(per_node=True, compress=comp)
+            v = plan_vnodes(par, seql, kids, rptr, np.ascontiguousarray(rl) if len(rl) else
+                            np.zeros(1, np.int32), r2t.shape[1], B, hq, hkv)
+            v = {k: ([int(x) for x in a] if isinstance(a, np.ndarray) else a) for k, a in v.items()}
+            q = np.random.default_rng(si).standard_normal((B, hq, d))
+            outs.append(fasttree_attention(q, pool_k, pool_v, v, r2t.reshape(-1), d ** -0.5))
+            sizes.append(len(par))
+        assert sizes[1] <= sizes[0]
+        np.testing.assert_allclose(outs[1], outs[0], atol=1e-12, rtol=0)
+        kid_t = np.array([c[0] for c in step["children"]], np.int32)
+        kid_l = np.array([c[1] for c in step["children"]], np.float64)
+        ptr, ct, csc = vanilla_select_arrays(bs.scores, kid_t, kid_l, cs["W"])
+        bs.update_native(bs.leaves, ptr, ct, csc)
