@@ -9,8 +9,9 @@
 //     W tile (M = 128, K-major) x X^T (N = T, K-major), accumulated in TMEM
 //     (128 lanes x T fp32 columns), one tcgen05.mma per 16-wide K step;
 //   * a CTA owns one 128-feature tile and a K range (split-K): the grid is sized
-//     to ~2 CTAs per SM; W and X tiles (64 K-elements, 128-byte swizzle) stream
-//     by TMA through a 3-stage ring (two CTAs per SM keep 6 stages in flight);
+//     to one wave of one CTA per SM; W and X tiles (64 K-elements, 128-byte
+//     swizzle) stream by TMA through a 6-stage ring (192 KB in flight per SM:
+//     a CTA's bandwidth is bytes in flight / latency);
 //   * one elected lane issues TMA, one elected lane issues the MMAs, then all
 //     four warps drain TMEM (warp w holds features 32w..32w+31) and write Y;
 //   * split-K runs as a thread-block cluster along the K splits: each CTA parks
@@ -23,7 +24,7 @@ namespace be {
 constexpr int GM_BM = 128;                 // output features per tile (MMA M)
 constexpr int GM_BN = 128;                 // tokens (MMA N), T <= 128
 constexpr int GM_BK = 64;                  // K elements per stage (one 128-byte swizzle row)
-constexpr int GM_ST = 3;                   // pipeline stages
+constexpr int GM_ST = 6;                   // pipeline stages (192 KB: one CTA per SM)
 constexpr int GM_A = GM_BM * GM_BK * 2;    // 16 KB
 constexpr int GM_B = GM_BN * GM_BK * 2;    // 16 KB
 constexpr size_t gm_smem_bytes() { return 1024 + GM_ST * (GM_A + GM_B) + (2 * GM_ST + 2) * 8 + 16; }
@@ -311,13 +312,13 @@ extern "C" int be_gemm_tn(const void* x, int64_t ldx, const void* w, int64_t ldw
   }
   const int tiles = (N + GM_BM - 1) / GM_BM;
   const int kb = K / GM_BK;
-  // split-K = cluster size: a power of two <= 8 with about two CTAs per SM in
-  // total and at least 4 K blocks per split
+  // split-K = cluster size: the largest power of two <= 8 that keeps the grid
+  // within one wave (one CTA per SM) with at least 4 K blocks per split
   int splits = split_k;
   if (splits <= 0) {
     const int sms = num_sms_cached();
     splits = 1;
-    while (splits < 8 && tiles * splits * 2 <= 2 * sms && kb / (splits * 2) >= 4) splits *= 2;
+    while (splits < 8 && tiles * splits * 2 <= sms && kb / (splits * 2) >= 4) splits *= 2;
   }
   if (splits != 1 && splits != 2 && splits != 4 && splits != 8) {
     set_error("be_gemm_tn: split_k %d must be 1, 2, 4 or 8", splits);
