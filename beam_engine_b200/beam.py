@@ -17,6 +17,7 @@ from __future__ import annotations
 import ctypes as C
 import logging
 import os
+import time
 from typing import List, Optional, Sequence
 
 import numpy as np
@@ -184,18 +185,22 @@ class StepGraph:
         n = self.n
         self.dev_buf[:used].copy_(self.host_buf[:used], non_blocking=True)
         if self.graph is None:
-            cur = torch.cuda.current_stream(self.gen.device)
-            side = torch.cuda.Stream(self.gen.device)
-            side.wait_stream(cur)
-            with torch.cuda.stream(side):
-                self._body()            # warm-up (writes the same K/V the replay will)
-            cur.wait_stream(side)
+            t0 = time.perf_counter()
+            if not self.gen._graph_warm:   # first capture of the generator: warm libraries up
+                cur = torch.cuda.current_stream(self.gen.device)
+                side = torch.cuda.Stream(self.gen.device)
+                side.wait_stream(cur)
+                with torch.cuda.stream(side):
+                    self._body()            # warm-up (writes the same K/V the replay will)
+                cur.wait_stream(side)
+                self.gen._graph_warm = True
             g = torch.cuda.CUDAGraph()
             # thread-local capture: other threads (NCCL's watchdog polling its
             # events) may keep making CUDA calls while this one records
             with torch.cuda.graph(g, capture_error_mode="thread_local"):
                 self._body()
             self.graph = g
+            self.gen.graph_captures.append(time.perf_counter() - t0)
         self.graph.replay()
         torch.cuda.current_stream(self.gen.device).synchronize()
         if self.timing and self.gen.attn_times is not None:
@@ -238,6 +243,8 @@ class BeamSearchGenerator:
         self.attn_times = None        # list to collect them into (ms per launch) when set
         self.plan_hook = None         # called with (queries, plan info) per graph step
         self.picks = []               # kernel_type "auto": the choice of every decode step
+        self.graph_captures = []      # seconds spent recording each step graph
+        self._graph_warm = False
 
     # ------------------------------------------------------------------
     def generate(self, input_text: str, beam_size: int = 4, max_length: int = 50,
@@ -399,8 +406,9 @@ class BeamSearchGenerator:
                         merge=max(n, 1), parts=2 * info.n_parts + 256,
                         ints=2 * info.total_ints + 4096)
             if sg is not None and sg.n == n and sg.k == k and sg.temp == temperature:
+                # outgrown: the plan keeps growing with the suffixes, leave more room
                 for key in caps:
-                    caps[key] = max(caps[key], sg.caps[key])
+                    caps[key] = max(caps[key], sg.caps[key] * 3 // 2)
             self.step_graph = sg = StepGraph(self, n, k, temperature, caps)
             if not fill(sg.host_buf.data_ptr(), sg.total, sg.plan_off):
                 raise RuntimeError("decode step graph sized too small for its own plan")

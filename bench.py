@@ -232,6 +232,7 @@ def run_b200(args, rank, world, local_rank):
     step_bytes = (param_count(cfg) - cfg["vocab_size"] * cfg["hidden_size"]) * 2
     if args.no_e2e:
         return dict(value=value, ms_per_step=ms_max / K, churn=float(np.mean(churn)) if churn else None,
+                    captures_ms=[round(x * 1e3, 1) for x in gen.graph_captures],
                     picks=({k: gen.picks.count(k) for k in set(gen.picks)} if gen.picks else None),
                     attn_us=attn_total_ms / max(len(attn_ms), 1) * 1e3,
                     achieved=achieved, plan_avg=[float(np.mean([p[i] for p in plan_stats])) for i in range(5)])
@@ -307,6 +308,7 @@ def run_b200(args, rank, world, local_rank):
                 "includes": "prefill of 8 x 1024 prompt tokens + 127 decode steps, host ids in, "
                             "host beams out", "wall_ms": round(wall_ms, 1)},
         "gpu_launches": launches["n"],
+        "graph_captures": [round(x * 1e3, 1) for x in gen.graph_captures],   # ms, whole run
         "churn": round(float(np.mean(churn)), 3) if churn else None,
         "kernel_picks": ({k: gen.picks.count(k) for k in set(gen.picks)} if gen.picks else None),
         "clocks": ev.get("clocks"),
