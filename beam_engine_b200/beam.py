@@ -402,9 +402,12 @@ class BeamSearchGenerator:
                 size *= 4
             if info.max_wide_tokens > UMMA_MAX_TOKENS:   # outside the fixed kernels' range
                 return self._topk(self.decode_step(state, "cascade"), k, temperature)
-            caps = dict(work=2 * info.n_work + 64, wide=2 * info.n_work_wide + 16,
-                        merge=max(n, 1), parts=2 * info.n_parts + 256,
-                        ints=2 * info.total_ints + 4096)
+            # headroom: the suffix items (and their partial rows) keep growing with the
+            # beams' suffixes; the shared-prefix items hardly do.  Surplus suffix CTAs exit
+            # at once on the side stream, a re-record costs tens of ms (more under TP)
+            caps = dict(work=3 * info.n_work + 64, wide=2 * info.n_work_wide + 16,
+                        merge=max(n, 1), parts=3 * info.n_parts + 256,
+                        ints=3 * info.total_ints + 4096)
             if sg is not None and sg.n == n and sg.k == k and sg.temp == temperature:
                 # outgrown: the plan keeps growing with the suffixes, leave more room
                 for key in caps:
