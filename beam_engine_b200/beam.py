@@ -244,6 +244,7 @@ class BeamSearchGenerator:
         self.plan_hook = None         # called with (queries, plan info) per graph step
         self.picks = []               # kernel_type "auto": the choice of every decode step
         self.graph_captures = []      # seconds spent recording each step graph
+        self.graph_regrowth = []      # why a step graph was recorded again
         self._graph_warm = False
 
     # ------------------------------------------------------------------
@@ -405,13 +406,20 @@ class BeamSearchGenerator:
             # headroom: the suffix items (and their partial rows) keep growing with the
             # beams' suffixes; the shared-prefix items hardly do.  Surplus suffix CTAs exit
             # at once on the side stream, a re-record costs tens of ms (more under TP)
-            caps = dict(work=3 * info.n_work + 64, wide=2 * info.n_work_wide + 16,
-                        merge=max(n, 1), parts=3 * info.n_parts + 256,
-                        ints=3 * info.total_ints + 4096)
+            # (the first decode step has no suffix items yet: allow ~2 per beam)
+            caps = dict(work=3 * info.n_work + 2 * n + 64, wide=2 * info.n_work_wide + 16,
+                        merge=max(n, 1), parts=3 * info.n_parts + 4 * n + 256,
+                        ints=3 * info.total_ints + 64 * n + 4096)
             if sg is not None and sg.n == n and sg.k == k and sg.temp == temperature:
                 # outgrown: the plan keeps growing with the suffixes, leave more room
+                got = dict(work=info.n_work, wide=info.n_work_wide, merge=info.n_merge,
+                           parts=info.n_parts, ints=info.total_ints)
+                self.graph_regrowth.append({key: (got[key], sg.caps[key]) for key in got
+                                            if got[key] > sg.caps[key]})
                 for key in caps:
                     caps[key] = max(caps[key], sg.caps[key] * 3 // 2)
+            elif sg is not None:
+                self.graph_regrowth.append({"shape": (sg.n, n, sg.k, k)})
             self.step_graph = sg = StepGraph(self, n, k, temperature, caps)
             if not fill(sg.host_buf.data_ptr(), sg.total, sg.plan_off):
                 raise RuntimeError("decode step graph sized too small for its own plan")

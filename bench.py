@@ -233,6 +233,7 @@ def run_b200(args, rank, world, local_rank):
     if args.no_e2e:
         return dict(value=value, ms_per_step=ms_max / K, churn=float(np.mean(churn)) if churn else None,
                     captures_ms=[round(x * 1e3, 1) for x in gen.graph_captures],
+                    regrowth=gen.graph_regrowth,
                     picks=({k: gen.picks.count(k) for k in set(gen.picks)} if gen.picks else None),
                     attn_us=attn_total_ms / max(len(attn_ms), 1) * 1e3,
                     achieved=achieved, plan_avg=[float(np.mean([p[i] for p in plan_stats])) for i in range(5)])
