@@ -19,6 +19,7 @@ PP32 = C.POINTER(P32)
 (BE_OK, BE_EINVAL, BE_ENOMEM, BE_ECUDA, BE_ENOT_ALLOCATED, BE_ECAPACITY, BE_EDEVICE_RANGE,
  BE_EDEVICE_TIMEOUT) = range(8)
 BE_F32, BE_F16, BE_BF16 = 0, 1, 2
+BE_CAPS_SLOTS = 1
 
 
 class AttnPlanInfo(C.Structure):
@@ -29,7 +30,7 @@ class AttnPlanInfo(C.Structure):
 
 
 class AttnCaps(C.Structure):
-    _fields_ = [(n, C.c_int32) for n in ("max_work", "max_wide", "max_merge", "cluster")]
+    _fields_ = [(n, C.c_int32) for n in ("max_work", "max_wide", "max_merge", "cluster", "flags")]
 
 
 _SIGS = {

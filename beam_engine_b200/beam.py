@@ -102,18 +102,23 @@ class StepGraph:
     of the top-k) recorded once as a CUDA graph and replayed every step.
 
     Everything that changes per step lives in one static device buffer
-    [query ids | positions | append pages | append slots | attention plan]
-    filled by one H2D copy before the replay; attention runs through
-    ``be_attn_run_fixed``, whose launch shape depends only on the capacities
-    (the kernels read the plan's counts from its device-side header)."""
+    [query ids | positions | append pages | append slots | attention plan
+    | slot list (tree plans)] filled by one H2D copy before the replay;
+    attention runs through ``be_attn_run_fixed_2s``, whose launch shape depends
+    only on the capacities (the kernels read the plan's counts from its
+    device-side header).  ``kind`` is "cascade" (page-list plans, tensor-core
+    prefix and suffix kernels) or "fasttree" (slot-list plans, general kernel)."""
 
-    def __init__(self, gen, n, k, temperature, caps):
+    def __init__(self, gen, n, k, temperature, caps, kind="cascade"):
         self.gen, self.n, self.k, self.temp = gen, n, k, temperature
+        self.kind = kind
         m = gen.model
         self.caps = dict(caps)
+        self.caps.setdefault("slots", 0)
         dev = gen.device
         self.plan_off = -(-4 * n // 32) * 32
-        self.total = self.plan_off + self.caps["ints"]
+        self.slots_off = self.plan_off + -(-self.caps["ints"] // 32) * 32
+        self.total = self.slots_off + self.caps["slots"]
         self.dev_buf = torch.zeros(self.total, dtype=torch.int32, device=dev)
         self.host_buf = torch.empty(self.total, dtype=torch.int32).pin_memory()
         self.mid_o = torch.empty(max(1, self.caps["parts"]) * m.Hq * m.D, dtype=torch.float32,
@@ -122,7 +127,8 @@ class StepGraph:
                                    device=dev)
         self.vals_h = torch.empty(n * k, dtype=torch.float32).pin_memory()
         self.idx_h = torch.empty(n * k, dtype=torch.int64).pin_memory()
-        self.ccaps = _lib.AttnCaps(self.caps["work"], self.caps["wide"], self.caps["merge"], 1)
+        self.ccaps = _lib.AttnCaps(self.caps["work"], self.caps["wide"], self.caps["merge"], 1,
+                                   _lib.BE_CAPS_SLOTS if kind == "fasttree" else 0)
         # suffix tiles on a second stream, overlapping the shared-prefix tiles
         self.side = (torch.cuda.Stream(dev) if os.environ.get("BE_ATTN_TWO_STREAMS", "1") != "0"
                      else None)
@@ -138,12 +144,13 @@ class StepGraph:
                 err, ev = rt.cudaEventCreate()
                 self.events.append(ev)
 
-    def fits(self, n, k, temperature, info):
+    def fits(self, n, k, temperature, info, n_slots=0):
         c = self.caps
         return (n == self.n and k == self.k and temperature == self.temp
                 and info.n_work <= c["work"] and info.n_work_wide <= c["wide"]
                 and info.n_merge <= c["merge"] and info.n_parts <= c["parts"]
-                and info.total_ints <= c["ints"] and info.max_wide_tokens <= UMMA_MAX_TOKENS)
+                and info.total_ints <= c["ints"] and n_slots <= c["slots"]
+                and (self.kind != "cascade" or info.max_wide_tokens <= UMMA_MAX_TOKENS))
 
     def _mark(self, idx, qkv):
         if self.timing and torch.cuda.is_current_stream_capturing():
@@ -166,7 +173,9 @@ class StepGraph:
             self.dev_buf.data_ptr() + 4 * self.plan_off, C.byref(self.ccaps), pt.page_size,
             qkv.data_ptr(), qkv.stride(0), pt.kv_cache[layer].data_ptr(), pt.max_num_pages, m.Hq,
             m.Hkv, m.D, m.dt, m.D ** -0.5, out.data_ptr(), out.stride(0), None,
-            self.mid_o.data_ptr(), self.mid_lse.data_ptr(), None, stream_ptr(qkv.device),
+            self.mid_o.data_ptr(), self.mid_lse.data_ptr(),
+            (self.dev_buf.data_ptr() + 4 * self.slots_off) if self.kind == "fasttree" else None,
+            stream_ptr(qkv.device),
             C.c_void_p(self.side.cuda_stream) if self.side is not None else None)
         check(rc, "be_attn_run_fixed_2s")
         self._mark(2 * layer + 1, qkv)
@@ -238,7 +247,12 @@ class BeamSearchGenerator:
         # cascade decode steps replay one CUDA graph (bf16/fp16 pools, page size 16)
         self.use_graph = (use_graph and kernel_type in ("cascade", "auto") and page_size == 16
                           and self.page_table.store_dtype != torch.float32)
+        # tree steps replay their own graph (slot-list plans, any page size, 2-byte pools)
+        self.use_graph_tree = (use_graph and kernel_type in ("fasttree", "auto")
+                               and self.page_table.store_dtype != torch.float32)
         self.step_graph = None
+        self.step_graph_tree = None
+        self._tree_stash = None       # the picker's tree plan, reused by the same step
         self.time_attention = False   # record per-layer attention events in the step graph
         self.attn_times = None        # list to collect them into (ms per launch) when set
         self.plan_hook = None         # called with (queries, plan info) per graph step
@@ -345,12 +359,42 @@ class BeamSearchGenerator:
         levels = state.cascade_levels()
         cinfo, _ = cascade_plan_host(levels, n, ps, m.Hq, m.Hkv, causal=True,
                                      num_sms=self.attn.plan.num_sms)
-        v, _ = self._tree_vnodes(state, n)
-        tinfo, _ = build_tree_plan(v, n, ps, m.Hq, m.Hkv)
+        v, r2t = self._tree_vnodes(state, n)
+        tinfo, tplan = build_tree_plan(v, n, ps, m.Hq, m.Hkv)
         elt = 4 if self.page_table.store_dtype == torch.float32 else 2
         kind = choose(levels, cinfo, tinfo, m.Hkv, m.Hq, m.D, elt=elt)
         self.picks.append(kind)
+        self._tree_stash = (v, r2t, tinfo, tplan) if kind == "fasttree" else None
         return kind
+
+    def _tree_graph_step(self, state: BeamState, k: int, temperature: float):
+        """A tree-attention decode step replayed from its own CUDA graph."""
+        from .fasttree import build_tree_plan
+        m = self.model
+        n = len(state.leaves)
+        q, wp, wpos, pos = state.step_inputs()
+        if self._tree_stash is not None:
+            v, r2t, info, plan = self._tree_stash
+            self._tree_stash = None
+        else:
+            v, r2t = self._tree_vnodes(state, n)
+            info, plan = build_tree_plan(v, n, self.page_table.page_size, m.Hq, m.Hkv)
+        slots = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)])
+        sg = self.step_graph_tree
+        if not (sg is not None and sg.fits(n, k, temperature, info, len(slots))):
+            caps = dict(work=3 * info.n_work + 2 * n + 64, wide=2 * info.n_work_wide + 16,
+                        merge=max(n, 1), parts=3 * info.n_parts + 4 * n + 256,
+                        ints=3 * info.total_ints + 64 * n + 4096,
+                        slots=2 * len(slots) + 64 * n + 4096)
+            if sg is not None and sg.n == n and sg.k == k and sg.temp == temperature:
+                for key in caps:
+                    caps[key] = max(caps[key], sg.caps[key] * 3 // 2)
+            self.step_graph_tree = sg = StepGraph(self, n, k, temperature, caps, kind="fasttree")
+        h = sg.host_buf.numpy()
+        h[0:n], h[n:2 * n], h[2 * n:3 * n], h[3 * n:4 * n] = q, pos, wp, wpos
+        h[sg.plan_off:sg.plan_off + info.total_ints] = plan[:info.total_ints]
+        h[sg.slots_off:sg.slots_off + len(slots)] = slots
+        return sg.step_filled(sg.slots_off + len(slots))
 
     def decode_step(self, state: BeamState, kind: Optional[str] = None):
         """One beam step's forward: returns logits [beams, vocab]."""
@@ -374,6 +418,9 @@ class BeamSearchGenerator:
     def decode_topk(self, state: BeamState, k: int, temperature: float):
         """One decode step through to the host: (log-prob top-k [beams, k], ids)."""
         kind = self.pick_kernel(state) if self.kernel_type == "auto" else self.kernel_type
+        if kind == "fasttree" and self.use_graph_tree:
+            return self._tree_graph_step(state, k, temperature)
+        self._tree_stash = None
         if not self.use_graph or kind != "cascade":
             return self._topk(self.decode_step(state, kind), k, temperature)
         m = self.model

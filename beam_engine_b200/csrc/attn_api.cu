@@ -10,6 +10,7 @@ struct Caps {                // grid sizes; fixed = true: counts come from the p
   int work, wide, merge, cluster;
   bool fixed;
   cudaStream_t side = nullptr;   // narrow tiles on this stream (fork / join by events)
+  bool slots = false;            // fixed grids for plans with slot lists (tree plans)
 };
 
 // Fork / join events for the two-stream launch, one pair per device, created
@@ -39,7 +40,7 @@ int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t
   if (c.work > 0) {
     int rc = BE_OK;
     if constexpr (sizeof(T) == 2) {
-      const bool tma_ok = (c.fixed || (!info->any_slots && info->page_size == 16)) &&
+      const bool tma_ok = (c.fixed ? !c.slots : (!info->any_slots && info->page_size == 16)) &&
                           p.page_size == 16 && (D == 128 || D == 64) && !force_cp_async();
       if (tma_ok) {
         CUtensorMap map;
@@ -236,7 +237,8 @@ extern "C" int be_attn_run_fixed(const int32_t* plan_dev, const be_attn_caps* ca
   p.kvlist = kv_list_override;  // null: the plan's own list
   p.n_work = caps->max_work;
   p.n_wide = caps->max_wide;
-  const Caps c{caps->max_work, caps->max_wide, caps->max_merge, caps->cluster, true};
+  Caps c{caps->max_work, caps->max_wide, caps->max_merge, caps->cluster, true};
+  c.slots = (caps->flags & BE_CAPS_SLOTS) != 0;
   return dispatch(dtype, p, nullptr, plan_dev, head_dim, c, (cudaStream_t)stream);
 }
 
@@ -273,5 +275,6 @@ extern "C" int be_attn_run_fixed_2s(const int32_t* plan_dev, const be_attn_caps*
   p.n_wide = caps->max_wide;
   Caps c{caps->max_work, caps->max_wide, caps->max_merge, caps->cluster, true};
   c.side = (cudaStream_t)side_stream;
+  c.slots = (caps->flags & BE_CAPS_SLOTS) != 0;
   return dispatch(dtype, p, nullptr, plan_dev, head_dim, c, (cudaStream_t)stream);
 }

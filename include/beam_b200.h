@@ -196,7 +196,9 @@ typedef struct {
   int32_t max_wide;   /* >= n_work_wide                                         */
   int32_t max_merge;  /* >= n_merge                                             */
   int32_t cluster;    /* CTAs per work item for narrow tiles (1..8)             */
+  int32_t flags;      /* BE_CAPS_SLOTS: the plans hold slot lists (tree plans)   */
 } be_attn_caps;
+#define BE_CAPS_SLOTS 1
 
 /* be_attn_run with a launch shape fixed by `caps` instead of a host-side plan
  * description: the plan at plan_dev (header included) may change between

@@ -132,3 +132,27 @@ def test_auto_picker_runs_and_agrees_when_it_picks_cascade():
         assert [s for s, _ in out] == [s for s, _ in runs["cascade"][0]]
     if set(picks) == {"fasttree"}:
         assert [s for s, _ in out] == [s for s, _ in runs["fasttree"][0]]
+
+
+def test_tree_graph_step_matches_eager_bf16():
+    """Tree-attention decode steps replayed from a CUDA graph (slot-list plans
+    through the fixed-grid kernel) select the same beams as eager tree steps."""
+    from beam_engine_b200.beam import BeamSearchGenerator
+    from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy
+    from beam_engine_b200.configs import TINY
+    from beam_engine_b200.llama import BeamLlama
+    cfg = dict(TINY, head_dim=128, num_attention_heads=4, num_key_value_heads=2, hidden_size=512)
+    model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=dev(), seed=4)
+    g = torch.Generator().manual_seed(10)
+    prompts = [torch.randint(0, 1024, (50,), generator=g).tolist() for _ in range(2)]
+    outs = []
+    for graph in (False, True):
+        gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=16,
+                                  kernel_type="fasttree", max_num_pages=512, use_graph=graph)
+        outs.append(gen.generate_ids(prompts, 8, max_new_tokens=24, num_return_sequences=8))
+        assert gen.use_graph_tree == graph
+        if graph:
+            assert gen.step_graph_tree is not None and gen.step_graph_tree.graph is not None
+    for a, b in zip(*outs):
+        assert [s for s, _ in a] == [s for s, _ in b]
+        np.testing.assert_allclose([x for _, x in a], [x for _, x in b], rtol=1e-6)
