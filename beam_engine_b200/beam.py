@@ -71,10 +71,10 @@ class PlannedAttention:
         p = self.plan
         p.info = info
         host = torch.from_numpy(buf)
+        if p.copied is not None:          # previous H2D still reading the staging buffer
+            p.copied.synchronize()
         if p.host.numel() < host.numel():
             p.host = torch.empty(host.numel(), dtype=torch.int32).pin_memory()
-        if p.copied is not None:
-            p.copied.synchronize()
         p.host[:host.numel()].copy_(host)
         p.place(self.m.Hq, self.m.D)
         self.kv_list = kv_entries_dev
@@ -275,10 +275,12 @@ class BeamSearchGenerator:
     def _to_device(self, arrays: Sequence[np.ndarray]):
         """One pinned staging buffer, one H2D copy -> list of int32 device views."""
         n = sum(len(a) for a in arrays)
-        if self.meta_host.numel() < n:
-            self.meta_host = torch.empty(max(n, 1024) * 2, dtype=torch.int32).pin_memory()
+        # the previous copy out of the staging buffer must finish before the
+        # buffer is reused -- or dropped for a larger one
         if getattr(self, "_meta_ev", None) is not None:
             self._meta_ev.synchronize()
+        if self.meta_host.numel() < n:
+            self.meta_host = torch.empty(max(n, 1024) * 2, dtype=torch.int32).pin_memory()
         hv = self.meta_host.numpy()
         off = 0
         for a in arrays:

@@ -603,7 +603,11 @@ int be_fasttree_prepare(int num_nodes, const int32_t* node_parent, const int32_t
   std::vector<int64_t> L(node_seqlen, node_seqlen + n);
   std::vector<int> merged(n, 0);
   if (n > 0) {
-    std::deque<int> fifo{0};
+    // BFS from every root: the reference decodes one prompt (one root, node 0);
+    // several prompts decoded together make a forest
+    std::deque<int> fifo;
+    for (int i = 0; i < n; ++i)
+      if (node_parent[i] == -1) fifo.push_back(i);
     while (!fifo.empty()) {
       const int v = fifo.front();
       fifo.pop_front();
@@ -635,14 +639,17 @@ int be_fasttree_prepare(int num_nodes, const int32_t* node_parent, const int32_t
     const int v = fifo.front();
     fifo.pop_front();
     const int par = node_parent[v];
-    if (merged[v] == 0 && v != 0)  // par == -1 would index the last entry, as in Python
-      node_reqs[par >= 0 ? par : n - 1].insert(node_reqs[par >= 0 ? par : n - 1].end(),
-                                                req_list + req_ptr[v], req_list + req_ptr[v + 1]);
-    vkids[par >= 0 ? par : n - 1] -= 1;
-    if (par >= 0 && vkids[par] == 0) fifo.push_back(par);
+    if (par < 0) continue;   // a root: its requests stay with it (node 0 in the reference)
+    if (merged[v] == 0)
+      node_reqs[par].insert(node_reqs[par].end(), req_list + req_ptr[v], req_list + req_ptr[v + 1]);
+    vkids[par] -= 1;
+    if (vkids[par] == 0) fifo.push_back(par);
   }
   std::vector<int64_t> tok_off(n, 0);
-  for (int i = 1; i < n; ++i) tok_off[i] = tok_off[node_parent[i]] + node_seqlen[node_parent[i]];
+  // token offset of each node within its requests' rows (roots start at 0); nodes
+  // are in BFS order, so a parent's offset is known before its children's
+  for (int i = 0; i < n; ++i)
+    tok_off[i] = node_parent[i] < 0 ? 0 : tok_off[node_parent[i]] + node_seqlen[node_parent[i]];
   std::vector<int32_t> qe, qo, ql, ko, kl;
   for (int i = 0; i < n; ++i) {
     const auto& reqs = node_reqs[i];

@@ -142,14 +142,14 @@ def test_tree_graph_step_matches_eager_bf16():
     from beam_engine_b200.configs import TINY
     from beam_engine_b200.llama import BeamLlama
     cfg = dict(TINY, head_dim=128, num_attention_heads=4, num_key_value_heads=2, hidden_size=512)
-    model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=dev(), seed=4)
-    g = torch.Generator().manual_seed(10)
-    prompts = [torch.randint(0, 1024, (50,), generator=g).tolist() for _ in range(2)]
+    model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=dev(), seed=3)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, 1024, (70,), generator=g).tolist() for _ in range(3)]
     outs = []
     for graph in (False, True):
         gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=16,
                                   kernel_type="fasttree", max_num_pages=512, use_graph=graph)
-        outs.append(gen.generate_ids(prompts, 8, max_new_tokens=24, num_return_sequences=8))
+        outs.append(gen.generate_ids(prompts, 8, max_new_tokens=12, num_return_sequences=8))
         assert gen.use_graph_tree == graph
         if graph:
             assert gen.step_graph_tree is not None and gen.step_graph_tree.graph is not None

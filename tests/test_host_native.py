@@ -251,3 +251,47 @@ def test_compressed_tree_plans_attend_the_same_tokens(trajectories, case):
         kid_l = np.array([c[1] for c in step["children"]], np.float64)
         ptr, ct, csc = vanilla_select_arrays(bs.scores, kid_t, kid_l, cs["W"])
         bs.update_native(bs.leaves, ptr, ct, csc)
+
+
+def test_tree_plans_of_several_prompts_attend_each_request_exactly():
+    """Several prompts decoded together make a forest: every request's vnodes
+    must cover exactly its own tokens (oracle two-stage attention against dense
+    attention over the request's token slots, float64)."""
+    from oracle.attention import fasttree_attention
+    rng = np.random.default_rng(5)
+    W, ps, hq, hkv, d = 6, 16, 8, 2, 16
+    pt = cpu_table(ps, 1024)
+    bs = BeamState(W, pt)
+    for p in range(3):
+        bs.add_root_sequence(rng.integers(0, 1000, 40 + 9 * p).tolist())
+    bs.update_native(bs.leaves, np.arange(4, dtype=np.int32) * W,
+                     rng.integers(0, 1000, 3 * W).astype(np.int32), -rng.random(3 * W))
+    kpool = rng.standard_normal((1024 * ps, hkv, d))
+    vpool = rng.standard_normal((1024 * ps, hkv, d))
+    for step in range(8):
+        n = len(bs.leaves)
+        lens = [len(bs.sequence(int(l))) for l in bs.leaves]
+        for comp in (False, True):
+            par, seql, kids, rptr, rl, r2t = bs.tree_arrays(per_node=True, compress=comp)
+            v = plan_vnodes(par, seql, kids, rptr, np.ascontiguousarray(rl) if len(rl) else
+                            np.zeros(1, np.int32), r2t.shape[1], n, hq, hkv)
+            v = {k: ([int(x) for x in a] if isinstance(a, np.ndarray) else a) for k, a in v.items()}
+            q = np.random.default_rng(step).standard_normal((n, hq, d))
+            got = fasttree_attention(q, kpool, vpool, v, [int(x) for x in r2t.reshape(-1)], d ** -0.5)
+            for c in range(n):
+                sl = r2t[c, :lens[c]].astype(np.int64)
+                K = np.repeat(kpool[sl], hq // hkv, axis=1)
+                V = np.repeat(vpool[sl], hq // hkv, axis=1)
+                s = np.einsum("hd,thd->ht", q[c], K) * d ** -0.5
+                pr = np.exp(s - s.max(-1, keepdims=True))
+                pr /= pr.sum(-1, keepdims=True)
+                np.testing.assert_allclose(got[c], np.einsum("ht,thd->hd", pr, V), atol=1e-10)
+        cnt = np.zeros(n, np.int32)
+        for p in range(3):
+            c = np.zeros(W, np.int32)
+            c[: W // 2] = 2
+            rng.shuffle(c)
+            cnt[p * W:(p + 1) * W] = c
+        ptr = np.concatenate([[0], np.cumsum(cnt)]).astype(np.int32)
+        bs.update_native(bs.leaves, ptr, rng.integers(0, 1000, int(ptr[-1])).astype(np.int32),
+                         -rng.random(int(ptr[-1])))
