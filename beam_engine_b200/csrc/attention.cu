@@ -487,6 +487,7 @@ __global__ void __launch_bounds__(128) merge_kernel(const int32_t* __restrict__ 
                                                     const float* __restrict__ mid_lse, int hq, int D,
                                                     char* out, int64_t out_row_stride, float* lse,
                                                     const int32_t* __restrict__ hdr) {
+  pdl_wait();
   const int item = blockIdx.x * 4 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (hdr) {

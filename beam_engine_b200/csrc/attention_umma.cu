@@ -119,6 +119,7 @@ __global__ void __launch_bounds__(160) attn_umma_kernel(const __grid_constant__ 
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 5);
 
+  pdl_wait();   // q and the plan come from earlier kernels / copies on this stream
   resolve_plan(p);
   if ((int)blockIdx.x >= plan_n_wide(p)) return;  // before any barrier or TMEM use
   const Work w = p.work[blockIdx.x];
@@ -370,8 +371,7 @@ int launch_umma(const AttnParams& p, const CUtensorMap& map, int n_items, cudaSt
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     set = true;
   }
-  attn_umma_kernel<T, D><<<dim3(n_items, p.hkv), 160, smem, st>>>(map, p);
-  BE_LAUNCH_CHECK();
+  BE_CUDA_CHECK(launch_pdl(attn_umma_kernel<T, D>, dim3(n_items, p.hkv), 160, smem, st, map, p));
   return BE_OK;
 }
 

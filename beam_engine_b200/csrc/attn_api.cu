@@ -113,11 +113,12 @@ int launch_all(const AttnParams& p, const be_attn_plan_info* info, const int32_t
   if (c.merge > 0) {
     const int items = c.merge * p.hq;
     const bool dev = c.fixed;
-    merge_kernel<T><<<(items + 3) / 4, 128, 0, st>>>(
+    BE_CUDA_CHECK(launch_pdl(
+        merge_kernel<T>, (items + 3) / 4, 128, 0, st,
         dev ? nullptr : plan + info->off_merge_q, dev ? nullptr : plan + info->off_merge_ptr,
-        dev ? nullptr : plan + info->off_merge_parts, c.merge, p.mid_o, p.mid_lse, p.hq, D, p.out,
-        p.out_row_stride, p.lse, dev ? plan : nullptr);
-    BE_LAUNCH_CHECK();
+        dev ? nullptr : plan + info->off_merge_parts, c.merge, (const float*)p.mid_o,
+        (const float*)p.mid_lse, p.hq, D, p.out, p.out_row_stride, p.lse,
+        dev ? plan : (const int32_t*)nullptr));
   }
   return BE_OK;
 }

@@ -6,6 +6,8 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <utility>
 
 #include "beam_b200.h"
 
@@ -32,6 +34,37 @@ template <> __device__ __forceinline__ __half from_f<__half>(float x) { return _
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
 inline int dtype_size(int dt) { return dt == BE_F32 ? 4 : 2; }
+
+// Programmatic dependent launch: a kernel launched with launch_pdl may be
+// scheduled while the previous kernel on its stream is still finishing (the
+// launch latency overlaps that tail); it must call pdl_wait() before it reads
+// anything the previous kernel writes.  BE_PDL=0 turns the attribute off.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("BE_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Host-side thread-local last-error text (read through be_last_error()).
 void set_error(const char* fmt, ...);

@@ -48,6 +48,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(T* __restrict__ residu
                                                           const T* __restrict__ delta,
                                                           const T* __restrict__ w,
                                                           T* __restrict__ out, int H, float eps) {
+  pdl_wait();   // inputs come from the previous kernel (launched with launch_pdl)
   constexpr int V = 16 / sizeof(T);
   const int row = blockIdx.x;
   T* x = residual + (int64_t)row * H;
@@ -105,6 +106,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
     const int32_t* __restrict__ positions, const float* __restrict__ inv_freq,
     T* __restrict__ pool, int num_pages, int page_size, const int32_t* __restrict__ write_page,
     const int32_t* __restrict__ write_pos, int write_rope_k_in_place) {
+  pdl_wait();
   const int warps_per_row = hq + 2 * hkv;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -154,6 +156,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
 template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu,
                                                        T* __restrict__ out, int n, int F) {
+  pdl_wait();
   constexpr int V = 16 / sizeof(T);
   const int64_t per_row = F / V;
   const int64_t total = (int64_t)n * per_row;
@@ -188,19 +191,18 @@ extern "C" int be_add_rmsnorm(void* residual, const void* delta, const void* wei
   const int threads = 256;
   switch (dtype) {
     case BE_BF16:
-      add_rmsnorm_kernel<__nv_bfloat16><<<rows, threads, 0, st>>>(
-          (__nv_bfloat16*)residual, (const __nv_bfloat16*)delta, (const __nv_bfloat16*)weight,
-          (__nv_bfloat16*)out, hidden, eps);
+      BE_CUDA_CHECK(launch_pdl(add_rmsnorm_kernel<__nv_bfloat16>, rows, threads, 0, st,
+                               (__nv_bfloat16*)residual, (const __nv_bfloat16*)delta,
+                               (const __nv_bfloat16*)weight, (__nv_bfloat16*)out, hidden, eps));
       break;
     case BE_F16:
-      add_rmsnorm_kernel<__half><<<rows, threads, 0, st>>>((__half*)residual, (const __half*)delta,
-                                                           (const __half*)weight, (__half*)out,
-                                                           hidden, eps);
+      BE_CUDA_CHECK(launch_pdl(add_rmsnorm_kernel<__half>, rows, threads, 0, st, (__half*)residual,
+                               (const __half*)delta, (const __half*)weight, (__half*)out, hidden,
+                               eps));
       break;
     default:
-      add_rmsnorm_kernel<float><<<rows, threads, 0, st>>>((float*)residual, (const float*)delta,
-                                                          (const float*)weight, (float*)out, hidden,
-                                                          eps);
+      BE_CUDA_CHECK(launch_pdl(add_rmsnorm_kernel<float>, rows, threads, 0, st, (float*)residual,
+                               (const float*)delta, (const float*)weight, (float*)out, hidden, eps));
   }
   BE_LAUNCH_CHECK();
   return BE_OK;
@@ -221,11 +223,11 @@ extern "C" int be_rope_qkv_append(void* qkv, int64_t row_stride, int n, int num_
   const int threads = 256;
   const int blocks = (int)((warps * 32 + threads - 1) / threads);
   cudaStream_t st = (cudaStream_t)stream;
-#define BE_ROPE(T)                                                                              \
-  rope_append_kernel<T><<<blocks, threads, 0, st>>>((T*)qkv, row_stride, n, num_qo_heads,       \
-                                                    num_kv_heads, head_dim, positions, inv_freq, \
-                                                    (T*)paged_kv_cache, num_pages, page_size,    \
-                                                    write_page, write_pos, rope_k_in_place)
+#define BE_ROPE(T)                                                                           \
+  BE_CUDA_CHECK(launch_pdl(rope_append_kernel<T>, blocks, threads, 0, st, (T*)qkv, row_stride, n, \
+                           num_qo_heads, num_kv_heads, head_dim, positions, inv_freq,            \
+                           (T*)paged_kv_cache, num_pages, page_size, write_page, write_pos,      \
+                           rope_k_in_place))
   switch (dtype) {
     case BE_BF16: BE_ROPE(__nv_bfloat16); break;
     case BE_F16: BE_ROPE(__half); break;
@@ -250,15 +252,16 @@ extern "C" int be_silu_mul(const void* gate_up, void* out, int n, int ffn, int d
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
     case BE_BF16:
-      silu_mul_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(
-          (const __nv_bfloat16*)gate_up, (__nv_bfloat16*)out, n, ffn);
+      BE_CUDA_CHECK(launch_pdl(silu_mul_kernel<__nv_bfloat16>, blocks, threads, 0, st,
+                               (const __nv_bfloat16*)gate_up, (__nv_bfloat16*)out, n, ffn));
       break;
     case BE_F16:
-      silu_mul_kernel<__half><<<blocks, threads, 0, st>>>((const __half*)gate_up, (__half*)out, n,
-                                                          ffn);
+      BE_CUDA_CHECK(launch_pdl(silu_mul_kernel<__half>, blocks, threads, 0, st,
+                               (const __half*)gate_up, (__half*)out, n, ffn));
       break;
     default:
-      silu_mul_kernel<float><<<blocks, threads, 0, st>>>((const float*)gate_up, (float*)out, n, ffn);
+      BE_CUDA_CHECK(launch_pdl(silu_mul_kernel<float>, blocks, threads, 0, st,
+                               (const float*)gate_up, (float*)out, n, ffn));
   }
   BE_LAUNCH_CHECK();
   return BE_OK;

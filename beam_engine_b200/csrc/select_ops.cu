@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(TK_THREADS) logsoftmax_topk_kernel(
   __shared__ float s_v[TK_WARPS][TK_KMAX];
   __shared__ int s_i[TK_WARPS][TK_KMAX];
   __shared__ float s_m[TK_WARPS], s_s[TK_WARPS];
+  pdl_wait();
   const int row = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float* x = logits + (int64_t)row * ld;
@@ -222,9 +223,9 @@ extern "C" int be_logsoftmax_topk(const float* logits, int64_t ld, int rows, int
     return BE_EINVAL;
   }
   if (rows == 0) return BE_OK;
-  logsoftmax_topk_kernel<<<rows, TK_THREADS, 0, (cudaStream_t)stream>>>(
-      logits, ld, v, temperature, k, vocab_offset, full_vocab, out_val, out_idx, row_max,
-      row_sumexp);
+  BE_CUDA_CHECK(launch_pdl(logsoftmax_topk_kernel, rows, TK_THREADS, 0, (cudaStream_t)stream,
+                           logits, ld, v, temperature, k, vocab_offset, full_vocab, out_val, out_idx,
+                           row_max, row_sumexp));
   BE_LAUNCH_CHECK();
   return BE_OK;
 }
