@@ -53,6 +53,8 @@ _SIGS = {
     "be_rope_qkv_append": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp,
                                      C.c_int, C.c_int, vp, vp, C.c_int, C.c_int, vp]),
     "be_silu_mul": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
+    "be_gemm_lt": (C.c_int, [vp, i64, vp, i64, vp, i64, C.c_int, C.c_int, C.c_int, C.c_int, vp,
+                             i64, vp]),
     "be_gemm_tn": (C.c_int, [vp, i64, vp, i64, vp, i64, C.c_int, C.c_int, C.c_int, C.c_int,
                              C.c_int, vp, i64, vp]),
     "be_logsoftmax_topk": (C.c_int, [vp, i64, C.c_int, C.c_int, f32, C.c_int, i64, C.c_int, vp, vp,

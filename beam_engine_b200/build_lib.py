@@ -59,7 +59,7 @@ def build(force=False, verbose=False, extra=()):
             print(" ".join(cmd))
         subprocess.run(cmd, check=True)
         objs.append(obj)
-    cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-lcuda"]
+    cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-lcuda", "-lcublasLt"]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)

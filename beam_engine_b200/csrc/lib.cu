@@ -12,3 +12,4 @@
 #include "model_ops.cu"
 #include "select_ops.cu"
 #include "gemm.cu"
+#include "gemm_lt.cu"

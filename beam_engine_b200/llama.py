@@ -84,9 +84,12 @@ class BeamLlama:
         self.inv_freq = inv_freq_table(D, float(c["rope_theta"]), self.device)
         self.dt = dtype_code(dtype)
         self.qkv_width = (Hq + 2 * Hkv) * D
-        self.use_gemm = (os.environ.get("BE_GEMM", "0") == "1" and dtype == torch.bfloat16
-                         and self.device.type == "cuda")
+        mode = os.environ.get("BE_GEMM", "0")
+        cuda_bf16 = dtype == torch.bfloat16 and self.device.type == "cuda"
+        self.use_gemm = mode == "1" and cuda_bf16          # tcgen05 weight-streaming GEMM
+        self.use_lt = mode == "lt" and cuda_bf16           # cuBLASLt, per-shape tuned
         self._gemm_ws = None
+        self._lt_ws = None
         del weights
 
     def _mm(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor):
@@ -103,6 +106,16 @@ class BeamLlama:
                                    _lib.BE_BF16 if out.dtype == torch.bfloat16 else _lib.BE_F32,
                                    0, self._gemm_ws.data_ptr(), self._gemm_ws.numel(),
                                    stream_ptr(self.device)), "be_gemm_tn")
+            return out
+        if (self.use_lt and a.stride(1) == 1 and w.is_contiguous() and out.stride(1) == 1
+                and out.dtype in (torch.bfloat16, torch.float32)):
+            if self._lt_ws is None:   # split-K scratch for cuBLASLt
+                self._lt_ws = torch.empty(32 << 20, dtype=torch.uint8, device=self.device)
+            check(lib().be_gemm_lt(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0),
+                                   out.data_ptr(), out.stride(0), T, N, K,
+                                   _lib.BE_BF16 if out.dtype == torch.bfloat16 else _lib.BE_F32,
+                                   self._lt_ws.data_ptr(), self._lt_ws.numel(),
+                                   stream_ptr(self.device)), "be_gemm_lt")
             return out
         if out.dtype == a.dtype:
             return torch.mm(a, w.t(), out=out)

@@ -276,6 +276,14 @@ int be_gemm_tn(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, 
                int T, int N, int K, int out_dtype, int split_k, float* workspace,
                int64_t workspace_floats, void* stream);
 
+/* The same GEMM through cuBLASLt: the first call of a shape outside stream
+ * capture times cuBLASLt's top heuristic candidates on `stream` and keeps the
+ * fastest (later calls and captured calls reuse it).  workspace: device
+ * scratch of workspace_bytes for split-K algorithms.                        */
+int be_gemm_lt(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+               int T, int N, int K, int out_dtype, void* workspace, int64_t workspace_bytes,
+               void* stream);
+
 /* ------------------------------------------------------------------------
  * Host page manager (no CUDA): FIFO page allocator + beam trie.  One
  * be_trie backs one PageTable and the BeamState objects over it.

@@ -417,3 +417,28 @@ def test_gemm_tn_rejects_unsupported_shapes():
     y = torch.zeros((200, 128), dtype=torch.bfloat16, device=d)
     assert _lib.lib().be_gemm_tn(x.data_ptr(), 128, w.data_ptr(), 128, y.data_ptr(), 128, 200, 128,
                                  128, _lib.BE_BF16, 0, None, 0, None) == _lib.BE_EINVAL
+
+
+@pytest.mark.parametrize("T,N,K,out", [(128, 4096, 4096, "bf16"), (128, 12800, 4096, "f32"),
+                                       (77, 384, 256, "bf16")])
+def test_gemm_lt_matches_torch(T, N, K, out):
+    """be_gemm_lt (cuBLASLt, per-shape tuned) against an fp32 matmul of the same
+    bf16 operands: within bf16 output rounding, on the first (tuning) call and
+    on a reused plan."""
+    from beam_engine_b200 import _lib
+    d = dev()
+    g = torch.Generator(device=d).manual_seed(T + N)
+    x = (torch.randn((T, K), generator=g, device=d) * 0.5).to(torch.bfloat16)
+    w = (torch.randn((N, K), generator=g, device=d) * 0.02).to(torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    ot = torch.bfloat16 if out == "bf16" else torch.float32
+    ws = torch.empty(32 << 20, dtype=torch.uint8, device=d)
+    for _ in range(2):
+        y = torch.full((T, N), float("nan"), dtype=ot, device=d)
+        _lib.check(_lib.lib().be_gemm_lt(x.data_ptr(), K, w.data_ptr(), K, y.data_ptr(), N, T, N, K,
+                                         _lib.BE_BF16 if out == "bf16" else _lib.BE_F32,
+                                         ws.data_ptr(), ws.numel(), None))
+        torch.cuda.synchronize()
+        err = (y.float() - ref).abs()
+        tol = (1e-2 if out == "bf16" else 1e-4) * ref.abs() + 1e-3
+        assert bool((err <= tol).all()), float(err.max())
