@@ -4,10 +4,11 @@ Llama, ``src/beam_engine/models/modeling_llama.py``), B200 layout.
 Per layer: fused residual-add + RMSNorm -> one QKV GEMM -> fused RoPE + K/V
 append into the pages -> paged attention (cascade / prefill / tree plan) ->
 O GEMM -> fused add + RMSNorm -> one gate|up GEMM -> SiLU*up -> down GEMM.
-GEMMs run on cuBLAS (torch.mm on pre-fused weights); BE_GEMM=1 routes the
-ones with at most 128 rows (the decode step) to ``be_gemm_tn``, the library's
-weight-streaming tcgen05 GEMM (correct, not yet faster than cuBLAS on these
-shapes).  Every other op is a kernel of ``libbeam_b200.so``.  Tensor parallelism (``tp``) shards q/k/v heads, the
+GEMMs run on cuBLASLt through ``be_gemm_lt`` (pre-fused weights, the fastest
+of cuBLASLt's candidates timed once per shape; BE_GEMM=0 selects torch.mm);
+BE_GEMM=1 routes the ones with at most 128 rows to ``be_gemm_tn``, the
+library's weight-streaming tcgen05 GEMM (correct, not yet faster than cuBLAS
+on these shapes).  Every other op is a kernel of ``libbeam_b200.so``.  Tensor parallelism (``tp``) shards q/k/v heads, the
 O-projection rows, gate/up columns and down rows, with one all-reduce after
 the O and down projections.
 """
@@ -84,7 +85,7 @@ class BeamLlama:
         self.inv_freq = inv_freq_table(D, float(c["rope_theta"]), self.device)
         self.dt = dtype_code(dtype)
         self.qkv_width = (Hq + 2 * Hkv) * D
-        mode = os.environ.get("BE_GEMM", "0")
+        mode = os.environ.get("BE_GEMM", "lt")
         cuda_bf16 = dtype == torch.bfloat16 and self.device.type == "cuda"
         self.use_gemm = mode == "1" and cuda_bf16          # tcgen05 weight-streaming GEMM
         self.use_lt = mode == "lt" and cuda_bf16           # cuBLASLt, per-shape tuned
