@@ -96,6 +96,10 @@ _SIGS = {
                                              C.POINTER(C.c_double), P32]),
     "be_beam_decode_inputs": (C.c_int, [vp, C.c_int, P32, C.c_int, C.c_int, C.c_int, vp, i64,
                                         C.c_int, C.POINTER(AttnPlanInfo)]),
+    "be_leaf_sequences": (i64, [vp, C.c_int, P32, P32, P32, i64]),
+    "be_diverse_select": (C.c_int, [C.c_int, P32, C.c_int, C.POINTER(C.c_double), P32,
+                                    C.POINTER(C.c_double), P32, P32, C.c_int, C.c_int, C.c_double,
+                                    C.c_int, C.c_double, P32, P32, C.POINTER(C.c_double), P32]),
     "be_vanilla_select": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_double), P32,
                                     C.POINTER(C.c_double), C.c_int, P32, P32,
                                     C.POINTER(C.c_double)]),

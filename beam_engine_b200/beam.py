@@ -512,7 +512,11 @@ class BeamSearchGenerator:
                     on_step(step)
                 k = min(2 * W, V) if W != 1 else 1
                 vals, idx = self.decode_topk(state, k, temperature)
-                if hasattr(self.strategy, "select_segments"):
+                if getattr(self.strategy, "needs_state", False):
+                    cp, ct, cs, new_seg = self.strategy.select_segments(seg, state.scores, idx, vals, W,
+                                                                        state=state)
+                    self._apply(state, cp, ct, cs)
+                elif hasattr(self.strategy, "select_segments"):
                     cp, ct, cs, new_seg = self.strategy.select_segments(seg, state.scores, idx, vals, W)
                     self._apply(state, cp, ct, cs)
                 else:

@@ -348,6 +348,26 @@ class BeamState:
         lib().be_node_sequence(self._t, int(leaf), _lib.ptr32(buf), n)
         return buf[:n].tolist()
 
+    def leaf_sequences(self, leaves=None):
+        """Token sequences of ``leaves`` (default: the candidates) as CSR
+        ``(seq_ptr [n+1], seq_tokens)``, walking up to the first node without
+        tokens (beam_strategy.py:96-103)."""
+        leaves = np.ascontiguousarray(self._leaves if leaves is None else leaves, np.int32)
+        n = len(leaves)
+        ptr = np.zeros(n + 1, np.int32)
+        cap = int(getattr(self, "_seq_cap", 0))
+        buf = np.zeros(max(cap, 1), np.int32)
+        total = lib().be_leaf_sequences(self._t, n, _lib.ptr32(leaves), _lib.ptr32(ptr),
+                                        _lib.ptr32(buf), cap)
+        if total < 0:
+            check(_lib.BE_EINVAL, "leaf_sequences")
+        if total > cap:
+            self._seq_cap = cap = int(total * 1.25) + 64
+            buf = np.zeros(cap, np.int32)
+            lib().be_leaf_sequences(self._t, n, _lib.ptr32(leaves), _lib.ptr32(ptr),
+                                    _lib.ptr32(buf), cap)
+        return ptr, buf[:total]
+
     def get_final_sequences(self, num_return: int, length_penalty: float = 1.0
                             ) -> List[Tuple[List[int], float]]:
         res = []

@@ -18,7 +18,7 @@ LIB = os.path.join(OUT_DIR, "libbeam_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_SOURCES = ["lib.cu"]
-HOST_SOURCES = ["host/planner.cpp", "host/trie.cpp"]
+HOST_SOURCES = ["host/planner.cpp", "host/trie.cpp", "host/diverse.cpp"]
 
 
 def _sources():

@@ -214,6 +214,34 @@ int64_t be_node_sequence(be_trie* t, int32_t leaf, int32_t* out, int64_t cap) {
   return k;
 }
 
+// Token sequences of many leaves as CSR (DiverseBeamSearchStrategy.
+// _get_sequence_from_node, beam_strategy.py:96-103): tokens of the leaf's
+// ancestors front to back, stopping at the first node (walking up) that holds
+// no tokens.  seq_ptr [n + 1]; seq_tokens is written while it has room (cap);
+// returns the total, -1 for an unknown leaf.
+int64_t be_leaf_sequences(be_trie* t, int n, const int32_t* leaves, int32_t* seq_ptr,
+                          int32_t* seq_tokens, int64_t cap) {
+  int64_t k = 0;
+  seq_ptr[0] = 0;
+  std::vector<int32_t> chain;
+  for (int i = 0; i < n; ++i) {
+    if (!t->valid(leaves[i])) {
+      set_error("be_leaf_sequences: unknown node %d", leaves[i]);
+      return -1;
+    }
+    chain.clear();
+    for (int32_t c = leaves[i]; c >= 0 && !t->nodes[c].tokens.empty(); c = t->nodes[c].parent)
+      chain.push_back(c);
+    for (auto it = chain.rbegin(); it != chain.rend(); ++it)
+      for (int32_t tok : t->nodes[*it].tokens) {
+        if (seq_tokens && k < cap) seq_tokens[k] = tok;
+        ++k;
+      }
+    seq_ptr[i + 1] = (int32_t)k;
+  }
+  return k;
+}
+
 // BeamState.add_root_sequence (beam_state.py:76-98).
 int be_beam_add_root(be_trie* t, const int32_t* tokens, int n, int32_t* leaf_out,
                      int32_t* pages_out) {

@@ -319,6 +319,12 @@ int be_node_append_token(be_trie* t, int32_t node, int32_t token);
 /* Root-to-leaf token sequence (beam_state.py:667-671); returns its length.  */
 int64_t be_node_sequence(be_trie* t, int32_t leaf, int32_t* out, int64_t cap);
 
+/* Token sequences of n leaves as CSR (DiverseBeamSearchStrategy._get_sequence_from_node,
+ * src/beam_engine/beam_strategy.py:96-103: the walk up stops at a node with no
+ * tokens).  seq_ptr [n + 1]; seq_tokens written up to cap; returns the total
+ * length (-1 for an unknown leaf).                                           */
+int64_t be_leaf_sequences(be_trie* t, int n, const int32_t* leaves, int32_t* seq_ptr,
+                          int32_t* seq_tokens, int64_t cap);
 /* BeamState.add_root_sequence (beam_state.py:76-98).                        */
 int be_beam_add_root(be_trie* t, const int32_t* tokens, int n, int32_t* leaf_out,
                      int32_t* pages_out);
@@ -383,6 +389,20 @@ int be_vanilla_select_segments(int nseg, const int32_t* seg_ptr, int k,
                                const double* logps, int beam_size, int32_t* child_ptr,
                                int32_t* child_tokens, double* child_scores,
                                int32_t* new_seg_ptr);
+/* DiverseBeamSearchStrategy.select_candidates (src/beam_engine/beam_strategy.py:173-317)
+ * for several prompts at once (candidates seg_ptr[s]..seg_ptr[s+1] form prompt s).
+ * tokens/logps [ncand][k] in top-k order; seq_ptr [ncand + 1] / seq_tokens are the
+ * parents' token sequences (be_leaf_sequences; seq_tokens may be NULL for hamming).
+ * diversity_type 0 = "hamming", 1 = "cumulative" (any other reference string).
+ * Outputs child_ptr [ncand + 1], child_tokens / child_scores [<= nseg * beam_size]
+ * (children per parent in pick order), new_seg_ptr [nseg + 1].              */
+int be_diverse_select(int nseg, const int32_t* seg_ptr, int k, const double* parent_scores,
+                      const int32_t* tokens, const double* logps, const int32_t* seq_ptr,
+                      const int32_t* seq_tokens, int beam_size, int num_groups,
+                      double diversity_penalty, int diversity_type, double length_penalty,
+                      int32_t* child_ptr, int32_t* child_tokens, double* child_scores,
+                      int32_t* new_seg_ptr);
+
 /* One call for a cascade decode step's host inputs (beam.py:168-221 decode
  * inputs + BeamState.get_cascade_input beam_state.py:211-412 + the attention
  * plan): out[0..n) query tokens, [n..2n) RoPE positions, [2n..3n) append

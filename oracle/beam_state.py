@@ -265,3 +265,65 @@ def vanilla_select(parent_scores, child_tokens, child_logps, beam_size):
     for i, tok, sc in flat[:beam_size]:
         out[i].append((tok, sc))
     return out
+
+
+def diverse_select(parent_scores, parent_seqs, child_tokens, child_logps, beam_size, num_groups=4,
+                   diversity_penalty=0.5, diversity_type="hamming", length_penalty=1.0):
+    """DiverseBeamSearchStrategy.select_candidates (beam_strategy.py:173-317).
+
+    Choices (parent, token, logp) in parent-major, top-k order, stable-sorted
+    by logp descending once (:215).  Each of ``num_groups`` groups re-scores
+    every choice not yet picked (same parent and token, :225-227) as
+    ``(logp - penalty) / len ** length_penalty`` with len = parent sequence + 1
+    (:229-247; no division when length_penalty == 0, :157-170), stable-sorts
+    descending and picks ``max(1, beam_size // num_groups)`` (:250-262).
+    Penalty: hamming = diversity_penalty if the token was picked before this
+    group (:105-125); otherwise cumulative = mean over earlier picks of
+    position-wise agreements of the two sequences (zip) * diversity_penalty,
+    summed in pick order (:127-155).  Picks are regrouped per parent in pick
+    order with score parent_score + logp (:264-300); if more than beam_size
+    were picked, children drop from the end, last parent first (:303-315).
+    Returns per-parent lists of (token, score).
+    """
+    bpg = max(1, beam_size // num_groups)
+    choices = []
+    for i in range(len(parent_scores)):
+        for tok, lp in zip(child_tokens[i], child_logps[i]):
+            choices.append((i, int(tok), float(lp)))
+    choices.sort(key=lambda x: x[2], reverse=True)
+    picked, picked_tokens, picked_seqs = [], set(), []
+    for _ in range(num_groups):
+        adj = []
+        for i, tok, lp in choices:
+            if any(pi == i and pt == tok for pi, pt, _ in picked):
+                continue
+            seq = list(parent_seqs[i]) + [tok]
+            if diversity_type == "hamming":
+                pen = diversity_penalty if tok in picked_tokens else 0.0
+            elif not picked_seqs:
+                pen = 0.0
+            else:
+                tot = 0.0
+                for s in picked_seqs:
+                    tot += sum(1 for a, b in zip(seq, s) if a == b) * diversity_penalty
+                pen = tot / len(picked_seqs)
+            sc = lp - pen
+            if length_penalty != 0:
+                sc = sc / (len(seq) ** length_penalty)
+            adj.append((i, tok, lp, sc))
+        adj.sort(key=lambda x: x[3], reverse=True)
+        for i, tok, lp, _ in adj[:bpg]:
+            picked.append((i, tok, lp))
+            picked_tokens.add(tok)
+            picked_seqs.append(list(parent_seqs[i]) + [tok])
+    out = [[] for _ in parent_scores]
+    for i, tok, lp in picked:
+        out[i].append((tok, parent_scores[i] + lp))
+    extra = sum(len(o) for o in out) - beam_size
+    for o in reversed(out):
+        while extra > 0 and o:
+            o.pop()
+            extra -= 1
+        if extra <= 0:
+            break
+    return out

@@ -19,6 +19,13 @@ Writes ``tests/golden/*.json`` / ``*.npz``.  What each fixture pins:
 * ``fasttree_kernel.npz`` -- outputs of the reference Triton FastTree kernel
   (``attention/fasttree/kernel.py``) run by the Triton interpreter on a
   trajectory state with per-node metadata.
+* ``diverse_trajectories.json`` -- seeded trajectories driven by the reference
+  ``DiverseBeamSearchStrategy`` (hamming / cumulative / an unknown type string,
+  1-5 groups, length penalty 0 / 0.7 / 1 / 2, tied log-probabilities, more
+  groups than beams): parents' sequences, offered children, the selection,
+  copies, free list and trie after each step, final ranking and groups.
+* ``e2e_cfg1_diverse.json`` -- as ``e2e_cfg1.json`` with the diverse strategy
+  (2 groups, hamming, penalty 0.5).
 * ``e2e_cfg1.json`` -- the reference ``BeamSearchGenerator`` (cascade, vanilla
   strategy, fp32, CPU) on the tiny config: selected tokens per step and the
   final ranked sequences.  FlashInfer calls go through the CPU restatement in
@@ -43,7 +50,7 @@ import torch  # noqa: E402
 from beam_engine.page_table import PageTable  # noqa: E402
 from beam_engine.beam_state import (BeamState, BeamCandidate, TrieNode,  # noqa: E402
                                     BeamGenerateInput, BeamTokenCandidate)
-from beam_engine.beam_strategy import VanillaBeamSearchStrategy  # noqa: E402
+from beam_engine.beam_strategy import VanillaBeamSearchStrategy, DiverseBeamSearchStrategy  # noqa: E402
 from beam_engine.attention.fasttree.preparation import prepare_fasttree_metadata_for_paged_cache  # noqa: E402
 import logging  # noqa: E402
 
@@ -276,6 +283,92 @@ CFG1 = dict(hidden_size=256, intermediate_size=688, num_hidden_layers=2, num_att
             num_key_value_heads=2, head_dim=64, vocab_size=1024, rope_theta=10000.0, rms_norm_eps=1e-6)
 
 
+E2E_DIVERSE = dict(num_groups=2, diversity_penalty=0.5, diversity_type="hamming", length_penalty=1.0)
+
+DIVERSE_CASES = [
+    dict(name="ham_w4_g2", seed=11, ps=4, pages=160, W=4, prompt=10, steps=14, vocab=12, quant=0.0,
+         strat=dict(num_groups=2, diversity_penalty=0.5, diversity_type="hamming", length_penalty=1.0)),
+    dict(name="ham_w8_g4_ties_nolp", seed=12, ps=8, pages=200, W=8, prompt=21, steps=12, vocab=20,
+         quant=0.5, strat=dict(num_groups=4, diversity_penalty=1.5, diversity_type="hamming",
+                               length_penalty=0.0)),
+    dict(name="cum_w4_g4", seed=13, ps=4, pages=160, W=4, prompt=10, steps=14, vocab=10, quant=0.0,
+         strat=dict(num_groups=4, diversity_penalty=0.3, diversity_type="cumulative",
+                    length_penalty=1.0)),
+    dict(name="cum_w6_g4_lp07_ties", seed=14, ps=16, pages=120, W=6, prompt=40, steps=12, vocab=14,
+         quant=0.25, strat=dict(num_groups=4, diversity_penalty=0.8, diversity_type="cumulative",
+                                length_penalty=0.7)),
+    dict(name="ham_w3_g5_trunc", seed=15, ps=4, pages=120, W=3, prompt=7, steps=12, vocab=8, quant=0.0,
+         strat=dict(num_groups=5, diversity_penalty=0.5, diversity_type="hamming", length_penalty=1.0)),
+    dict(name="cum_w4_g1", seed=16, ps=8, pages=120, W=4, prompt=12, steps=10, vocab=10, quant=0.0,
+         strat=dict(num_groups=1, diversity_penalty=0.5, diversity_type="cumulative",
+                    length_penalty=1.0)),
+    dict(name="other_type_w4_g2", seed=17, ps=4, pages=160, W=4, prompt=9, steps=10, vocab=10,
+         quant=0.5, strat=dict(num_groups=2, diversity_penalty=0.4, diversity_type="overlap",
+                               length_penalty=2.0)),
+]
+
+
+def make_diverse():
+    """Seeded trajectories through the reference PageTable + BeamState +
+    DiverseBeamSearchStrategy: per step the parents' sequences, the offered
+    children, the selection and the allocator state after the fork."""
+    from beam_engine.beam_state import BeamGenerateResult, BeamToken
+    out = {}
+    for cs in DIVERSE_CASES:
+        g = torch.Generator().manual_seed(cs["seed"])
+        pt = PageTable(layer_num=1, page_size=cs["ps"], max_num_pages=cs["pages"], head_num=1,
+                       head_dim=4, device=torch.device("cpu"), store_dtype=torch.float32)
+        copies = []
+        orig_copy = pt.copy_block
+
+        def rec_copy(p, n, _orig=orig_copy, _c=copies):
+            d = _orig(p, n)
+            _c.append([p, d, n])
+            return d
+
+        pt.copy_block = rec_copy
+        bs = BeamState(cs["W"], pt)
+        strat = DiverseBeamSearchStrategy(**cs["strat"])
+        prompt = torch.randint(0, cs["vocab"], (cs["prompt"],), generator=g).tolist()
+        bs.add_root_sequence(prompt)
+        W = cs["W"]
+        toks = torch.randperm(cs["vocab"], generator=g)[:W].tolist()
+        sc = sorted((-torch.rand(W, generator=g) * 3).tolist(), reverse=True)
+        bs.add_filtered_results([BeamGenerateResult(candidate=bs.candidates[0],
+                                                    children=[BeamToken(t, s) for t, s in zip(toks, sc)])])
+        steps = []
+        for step in range(cs["steps"]):
+            if not bs.candidates:
+                break
+            rec = dict(scores=[c.score for c in bs.candidates],
+                       seqs=[strat._get_sequence_from_node(c.trie_node) for c in bs.candidates])
+            inputs, kids = [], []
+            k = min(2 * W, cs["vocab"])
+            for c in bs.candidates:
+                t = torch.randperm(cs["vocab"], generator=g)[:k].tolist()
+                lp = torch.log_softmax(torch.randn(k, generator=g) * 2.0, 0)
+                if cs["quant"]:
+                    lp = torch.round(lp / cs["quant"]) * cs["quant"]
+                lp = sorted(lp.tolist(), reverse=True)
+                kids.append([t, lp])
+                inputs.append(BeamGenerateInput(candidate=c, children=[BeamTokenCandidate(a, b)
+                                                                        for a, b in zip(t, lp)]))
+            rec["children"] = kids
+            res = strat.select_candidates(bs, inputs, step)
+            rec["selected"] = [[[x.token_id, x.accumulated_score] for x in r.children] for r in res]
+            ncopy = len(copies)
+            bs.add_filtered_results(res)
+            rec["copies"] = copies[ncopy:]
+            rec["free_after"] = list(pt.free_pages)
+            rec["spec_after"] = tree_spec(bs)
+            steps.append(rec)
+        groups = [[c.score for c in grp] for grp in strat.get_diverse_groups(bs)]
+        out[cs["name"]] = dict(case=cs, prompt=prompt, root_children=[toks, sc], steps=steps,
+                               final=[[s, float(x)] for s, x in strat.get_final_sequences(bs)],
+                               groups=groups)
+    dump("diverse_trajectories.json", out)
+
+
 def cfg1_weights(seed=0):
     """Seeded N(0, 0.02) weights (norms = 1) in a fixed generation order."""
     sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
@@ -283,7 +376,7 @@ def cfg1_weights(seed=0):
     return random_llama_weights(CFG1, seed=seed, dtype=torch.float32, device="cpu")
 
 
-def make_e2e():
+def make_e2e(strategy="vanilla"):
     from beam_engine.models.configuration_llama import LlamaConfig
     import beam_engine.models.modeling_llama as ml
     from beam_engine.beam import BeamSearchGenerator
@@ -332,7 +425,9 @@ def make_e2e():
             return " ".join(str(int(i)) for i in ids)
 
     prompt = torch.randint(0, 1024, (64,), generator=torch.Generator().manual_seed(0)).tolist()
-    strat = VanillaBeamSearchStrategy(length_penalty=1.0)
+    strat = (VanillaBeamSearchStrategy(length_penalty=1.0) if strategy == "vanilla" else
+             DiverseBeamSearchStrategy(**E2E_DIVERSE))
+    cls = type(strat)
     gen = BeamSearchGenerator(model, Tok(prompt), strat, page_size=16, kernel_type="cascade")
     gen.page_table = PageTable(layer_num=2, page_size=16, max_num_pages=256, head_num=2, head_dim=64,
                                device=torch.device("cpu"), store_dtype=torch.float32)
@@ -345,23 +440,26 @@ def make_e2e():
 
     BeamState.add_filtered_results = traced
     captured = {}
-    orig_final = VanillaBeamSearchStrategy.get_final_sequences
+    orig_final = cls.get_final_sequences
 
     def fin(self, bs, num_return=None):
         r = orig_final(self, bs, num_return)
         captured["final"] = [[s, float(x)] for s, x in bs.get_final_sequences(len(bs.candidates), 1.0)]
         return r
 
-    VanillaBeamSearchStrategy.get_final_sequences = fin
+    cls.get_final_sequences = fin
     with torch.no_grad():
         texts = gen.generate("x", beam_size=4, max_length=64 + 32, num_return_sequences=4)
     BeamState.add_filtered_results = orig
-    dump("e2e_cfg1.json", dict(config=CFG1, prompt=prompt, beam_size=4, max_length=96, page_size=16,
-                               selections=trace, final=captured["final"], texts=texts))
+    cls.get_final_sequences = orig_final
+    name = "e2e_cfg1.json" if strategy == "vanilla" else "e2e_cfg1_diverse.json"
+    extra = {} if strategy == "vanilla" else dict(strategy=E2E_DIVERSE)
+    dump(name, dict(config=CFG1, prompt=prompt, beam_size=4, max_length=96, page_size=16,
+                    selections=trace, final=captured["final"], texts=texts, **extra))
 
 
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["trees", "traj", "ftk", "e2e"]
+    which = sys.argv[1:] or ["trees", "traj", "ftk", "e2e", "diverse", "e2e_diverse"]
     if "trees" in which:
         make_cascade_trees()
     if "traj" in which:
@@ -370,3 +468,7 @@ if __name__ == "__main__":
         make_fasttree_kernel()
     if "e2e" in which:
         make_e2e()
+    if "diverse" in which:
+        make_diverse()
+    if "e2e_diverse" in which:
+        make_e2e("diverse")
