@@ -6,6 +6,7 @@
 // query list, the KV list and the per-query merge lists.
 #include <algorithm>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <numeric>
@@ -33,6 +34,16 @@ struct W {
   int64_t cost;
   bool wide;
 };
+
+// Tokens per decode-time wide (tensor-core) chunk when > 0 (BE_PLAN_WIDE_CHUNK,
+// rounded to pages and capped at the resident tile); 0 = balance the split.
+inline int wide_chunk_override() {
+  static const int v = [] {
+    const char* e = getenv("BE_PLAN_WIDE_CHUNK");
+    return e ? std::max(0, atoi(e)) : 0;
+  }();
+  return v;
+}
 
 // Wide tiles hold up to 64 rows, narrow tiles 16 (rows = queries x group size).
 inline int tile_queries(int qlen, int g) {
@@ -215,7 +226,11 @@ extern "C" int be_cascade_plan(int num_levels, const int32_t* const* qo_indptr,
       const int min_chunk = round_pages((int64_t)std::min(gr.qlen, tq) * g * 8);
       chunk = std::max(min_chunk, balanced);
       // decode-time wide tiles run as one resident tensor-core tile
-      if (wide && !causal) chunk = std::min(chunk, BE_UMMA_MAX_TOKENS);
+      if (wide && !causal) {
+        chunk = std::min(chunk, BE_UMMA_MAX_TOKENS);
+        if (wide_chunk_override() > 0)
+          chunk = std::min(round_pages(wide_chunk_override()), BE_UMMA_MAX_TOKENS);
+      }
       const int nsplit = (gr.kv_len + chunk - 1) / chunk;
       chunk = round_pages((gr.kv_len + nsplit - 1) / nsplit);
     }
