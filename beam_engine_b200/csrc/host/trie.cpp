@@ -29,6 +29,7 @@ struct be_trie {
   struct Node {
     int32_t parent = -1;
     int32_t page = -1;
+    int64_t prefix = 0;   // tokens of the strict ancestors (kept by add_node / append_tok)
     std::vector<int32_t> tokens;
     std::vector<int32_t> children;
   };
@@ -38,6 +39,7 @@ struct be_trie {
   std::vector<char> allocated;
   std::vector<Node> nodes;
   std::vector<int32_t> level_memo;  // per call scratch
+  std::vector<int32_t> head_memo;   // first node of the node's level segment (same gen)
   std::vector<int32_t> memo_gen;
   int32_t gen = 0;
   std::vector<int32_t> level_stack;  // scratch of level()
@@ -70,6 +72,7 @@ struct be_trie {
     nd.parent = parent;
     nd.page = page;
     nd.tokens.assign(tok, tok + n);
+    if (parent >= 0) nd.prefix = nodes[parent].prefix + (int64_t)nodes[parent].tokens.size();
     nodes.push_back(std::move(nd));
     const int32_t id = (int32_t)nodes.size() - 1;
     if (parent >= 0) nodes[parent].children.push_back(id);
@@ -82,9 +85,21 @@ struct be_trie {
     std::reverse(out.begin(), out.end());
   }
   int64_t seq_len(int32_t leaf) const {
-    int64_t s = 0;
-    for (int32_t n = leaf; n >= 0; n = nodes[n].parent) s += nodes[n].tokens.size();
-    return s;
+    return nodes[leaf].prefix + (int64_t)nodes[leaf].tokens.size();
+  }
+  // append one token; descendants (only a node built through the object API can
+  // have any) get their ancestor lengths refreshed
+  void append_tok(int32_t n, int32_t tok) {
+    nodes[n].tokens.push_back(tok);
+    if (nodes[n].children.empty()) return;
+    std::vector<int32_t> st(nodes[n].children.begin(), nodes[n].children.end());
+    while (!st.empty()) {
+      const int32_t c = st.back();
+      st.pop_back();
+      const Node& par = nodes[nodes[c].parent];
+      nodes[c].prefix = par.prefix + (int64_t)par.tokens.size();
+      st.insert(st.end(), nodes[c].children.begin(), nodes[c].children.end());
+    }
   }
   int32_t level(int32_t n) {
     // level(root) = 0; level(n) = level(parent) + (parent has > 1 children)
@@ -98,8 +113,10 @@ struct be_trie {
     int32_t lv = cur >= 0 ? level_memo[cur] : 0;
     for (auto it = stack.rbegin(); it != stack.rend(); ++it) {
       const int32_t p = nodes[*it].parent;
-      lv = p < 0 ? 0 : lv + (nodes[p].children.size() > 1 ? 1 : 0);
+      const bool split = p >= 0 && nodes[p].children.size() > 1;
+      lv = p < 0 ? 0 : lv + (split ? 1 : 0);
       level_memo[*it] = lv;
+      head_memo[*it] = (p >= 0 && !split) ? head_memo[p] : *it;
       memo_gen[*it] = gen;
     }
     return level_memo[n];
@@ -108,6 +125,7 @@ struct be_trie {
     ++gen;
     if (level_memo.size() < nodes.size()) {
       level_memo.resize(nodes.size(), 0);
+      head_memo.resize(nodes.size(), 0);
       memo_gen.resize(nodes.size(), 0);
     }
   }
@@ -196,7 +214,7 @@ int be_node_append_token(be_trie* t, int32_t node, int32_t token) {
     set_error("be_node_append_token: bad node %d", node);
     return BE_EINVAL;
   }
-  t->nodes[node].tokens.push_back(token);
+  t->append_tok(node, token);
   return BE_OK;
 }
 
@@ -299,7 +317,7 @@ int be_beam_update(be_trie* t, int ncand, const int32_t* cand_leaf, const int32_
     const int32_t nid = cand_leaf[i];
     if (c1 - c0 == 1) {
       if ((int)t->nodes[nid].tokens.size() < ps) {
-        t->nodes[nid].tokens.push_back(child_tokens[c0]);
+        t->append_tok(nid, child_tokens[c0]);
         new_leaf[k] = nid;
       } else {
         int32_t page;
@@ -334,7 +352,7 @@ int be_beam_update(be_trie* t, int ncand, const int32_t* cand_leaf, const int32_
         new_leaf[k] = t->add_node(t->nodes[nid].parent, page, tk.data(), (int)tk.size());
         new_child[k++] = j;
       }
-      t->nodes[nid].tokens.push_back(child_tokens[c0]);
+      t->append_tok(nid, child_tokens[c0]);
       new_leaf[k] = nid;
       new_child[k++] = c0;
     }
@@ -375,31 +393,45 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
                      int32_t* level_page_ptr, int32_t* qo_indptr, int32_t* kv_indptr,
                      int32_t* kv_indices, int32_t* last_page_len) {
   t->new_generation();
+  // A candidate's root path splits into one segment per level 0..level(leaf):
+  // segment lv runs from head (first node of the level) to the node before the
+  // next level's head.  level() memoises each node's level and head for this
+  // generation, so walking a path hops once per level instead of once per node.
   struct Seg {
-    int32_t first, last;  // indices into the candidate's path
+    int32_t first, last;  // node ids, first is an ancestor of (or equal to) last
   };
-  static thread_local std::vector<std::vector<int32_t>> paths;
-  static thread_local std::vector<std::vector<Seg>> segs;  // by level
-  if ((int)paths.size() < ncand) {
-    paths.resize(ncand);
-    segs.resize(ncand);
-  }
-  for (int c = 0; c < ncand; ++c) segs[c].clear();
+  struct G {
+    int cand0, count;
+    Seg seg;
+  };
+  struct Scratch {
+    std::vector<std::vector<Seg>> segs;  // by candidate, by level
+    std::vector<int32_t> chain;
+    std::vector<G> groups;
+  };
+  static thread_local Scratch tls;   // looked up once (TLS access is a call in a shared library)
+  Scratch& S = tls;
+  auto& segs = S.segs;
+  auto& chain = S.chain;
+  auto& groups = S.groups;
+  if ((int)segs.size() < ncand) segs.resize(ncand);
   int top = 0;
   for (int c = 0; c < ncand; ++c) {
     if (!t->valid(cand_leaf[c])) {
       set_error("be_cascade_build: bad leaf %d", cand_leaf[c]);
       return -BE_EINVAL;
     }
-    t->path(cand_leaf[c], paths[c]);
     auto& sg = segs[c];
-    for (int i = 0; i < (int)paths[c].size(); ++i) {
-      const int lv = t->level(paths[c][i]);
-      while ((int)sg.size() <= lv) sg.push_back({-1, -1});
-      if (sg[lv].first < 0) sg[lv].first = i;
-      sg[lv].last = i;
-      top = std::max(top, lv);
+    const int32_t leaf = cand_leaf[c];
+    const int lv_leaf = t->level(leaf);
+    sg.resize(lv_leaf + 1);
+    int32_t x = leaf;
+    for (int lv = lv_leaf; lv >= 0; --lv) {
+      const int32_t h = t->head_memo[x];
+      sg[lv] = {h, x};
+      x = t->nodes[h].parent;
     }
+    top = std::max(top, lv_leaf);
   }
   const int nlev = ncand > 0 ? top + 1 : 0;
   if (nlev > cap_levels) {
@@ -407,11 +439,6 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
     return -BE_ECAPACITY;
   }
   int gbase = 0, pbase = 0;
-  struct G {
-    int cand0, count;
-    Seg seg;
-  };
-  static thread_local std::vector<G> groups;
   for (int lv = 0; lv < nlev; ++lv) {
     level_group_ptr[lv] = gbase;
     level_page_ptr[lv] = pbase;
@@ -420,12 +447,9 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
     groups.clear();
     for (int c = 0; c < ncand; ++c) {
       const auto& sg = segs[c];
-      Seg s = (lv < (int)sg.size() && sg[lv].first >= 0) ? sg[lv] : sg.back();
-      if (s.first < 0) {  // deepest level always exists; keep the compiler honest
-        for (int k = (int)sg.size() - 1; k >= 0; --k)
-          if (sg[k].first >= 0) { s = sg[k]; break; }
-      }
-      const int32_t key = paths[c][s.last];
+      // a candidate with no segment this deep reuses its deepest one
+      const Seg s = lv < (int)sg.size() ? sg[lv] : sg.back();
+      const int32_t key = s.last;
       if (t->node_mark[key] != kst) {
         t->node_mark[key] = kst;
         t->node_val[key] = (int32_t)groups.size();
@@ -447,10 +471,14 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
     int npages = 0;
     for (size_t gi = 0; gi < groups.size(); ++gi) {
       const auto& g = groups[gi];
-      const auto& p = paths[g.cand0];
+      chain.clear();   // the segment's nodes, last to first
+      for (int32_t x = g.seg.last;; x = t->nodes[x].parent) {
+        chain.push_back(x);
+        if (x == g.seg.first) break;
+      }
       const int32_t pst = t->next_stamp();   // pages already listed for this group
-      for (int i = g.seg.first; i <= g.seg.last; ++i) {
-        const int32_t pg = t->nodes[p[i]].page;
+      for (auto it = chain.rbegin(); it != chain.rend(); ++it) {
+        const int32_t pg = t->nodes[*it].page;
         if (pg >= 0 && pg < t->max_pages) {
           if (t->page_mark[pg] == pst) continue;
           t->page_mark[pg] = pst;
@@ -461,7 +489,7 @@ int be_cascade_build(be_trie* t, int ncand, const int32_t* cand_leaf, int cap_le
         }
         kv_indices[pbase + npages++] = pg;
       }
-      const int32_t tail = p[g.seg.last];
+      const int32_t tail = g.seg.last;
       const int ln = (int)t->nodes[tail].tokens.size();
       last_page_len[gbase + gi] = (tail == cand_leaf[g.cand0]) ? std::max(0, ln - 1) : ln;
       kvp[gi + 1] = npages;
@@ -755,27 +783,78 @@ int be_vanilla_select(int n, int k, const double* parent_scores, const int32_t* 
   // Only the first beam_size of that order matter, so a partial sort with the
   // index as the tie-break gives the same result as the full stable sort.
   const int64_t total = (int64_t)n * k;
-  static thread_local std::vector<int64_t> idx;
-  static thread_local std::vector<double> sc;
-  static thread_local std::vector<int32_t> cnt;
+  // per-thread scratch, looked up once per call (a thread_local in a shared
+  // library costs a TLS call per access otherwise)
+  struct Scratch {
+    std::vector<int64_t> idx;
+    std::vector<double> sc;
+    std::vector<int32_t> cnt, head, off;
+  };
+  static thread_local Scratch tls;
+  Scratch& S = tls;
+  auto& idx = S.idx;
+  auto& sc = S.sc;
   idx.resize(total);
   sc.resize(total);
-  for (int64_t e = 0; e < total; ++e) {
-    idx[e] = e;
-    sc[e] = parent_scores[e / k] + logps[e];
+  for (int i = 0; i < n; ++i) {   // nested loops: no 64-bit division per element
+    const double ps = parent_scores[i];
+    const int64_t b = (int64_t)i * k;
+    for (int j = 0; j < k; ++j) {
+      idx[b + j] = b + j;
+      sc[b + j] = ps + logps[b + j];
+    }
   }
   const int64_t keep = std::min<int64_t>(beam_size, total);
-  std::partial_sort(idx.begin(), idx.begin() + keep, idx.end(), [&](int64_t a, int64_t b) {
+  auto before = [&](int64_t a, int64_t b) {   // the stable sort's order
     return sc[a] > sc[b] || (!(sc[b] > sc[a]) && a < b);
-  });
+  };
+  // Rows straight from a top-k are already in that order (parent + logp is
+  // non-increasing along a row, ties keep the row order): merge the row heads
+  // instead of sorting.  Otherwise (or with NaNs) a partial sort.
+  bool rows_sorted = n <= 64;
+  for (int i = 0; rows_sorted && i < n; ++i) {
+    const double* r = sc.data() + (int64_t)i * k;
+    for (int j = 0; j < k; ++j)
+      if (std::isnan(r[j]) || (j + 1 < k && r[j + 1] > r[j])) {
+        rows_sorted = false;
+        break;
+      }
+  }
+  auto& row = S.cnt;   // parent row of each kept entry
+  row.resize(std::max<int64_t>(keep, n + 1));
+  if (rows_sorted) {
+    // equal scores: the lower row comes first (its flat index is smaller), so a
+    // strict '>' scan over the rows in order picks exactly the stable order
+    auto& head = S.head;
+    head.assign(n, 0);
+    for (int64_t r = 0; r < keep; ++r) {
+      int bi = -1;
+      double bs = 0.0;
+      for (int i = 0; i < n; ++i) {
+        if (head[i] >= k) continue;
+        const double v = sc[(int64_t)i * k + head[i]];
+        if (bi < 0 || v > bs) {
+          bi = i;
+          bs = v;
+        }
+      }
+      idx[r] = (int64_t)bi * k + head[bi];
+      row[r] = bi;
+      head[bi]++;
+    }
+  } else {
+    std::partial_sort(idx.begin(), idx.begin() + keep, idx.end(), before);
+    for (int64_t r = 0; r < keep; ++r) row[r] = (int)(idx[r] / k);
+  }
   // group the kept candidates by parent, each parent's in score order
-  cnt.assign(n + 1, 0);
-  for (int64_t r = 0; r < keep; ++r) cnt[idx[r] / k + 1]++;
-  for (int i = 0; i < n; ++i) cnt[i + 1] += cnt[i];
-  for (int i = 0; i <= n; ++i) child_ptr[i] = cnt[i];
+  auto& off = S.off;
+  off.assign(n + 1, 0);
+  for (int64_t r = 0; r < keep; ++r) off[row[r] + 1]++;
+  for (int i = 0; i < n; ++i) off[i + 1] += off[i];
+  for (int i = 0; i <= n; ++i) child_ptr[i] = off[i];
   for (int64_t r = 0; r < keep; ++r) {
     const int64_t e = idx[r];
-    const int o = cnt[e / k]++;
+    const int o = off[row[r]]++;
     child_tokens[o] = tokens[e];
     child_scores[o] = sc[e];
   }

@@ -295,3 +295,23 @@ def test_tree_plans_of_several_prompts_attend_each_request_exactly():
         ptr = np.concatenate([[0], np.cumsum(cnt)]).astype(np.int32)
         bs.update_native(bs.leaves, ptr, rng.integers(0, 1000, int(ptr[-1])).astype(np.int32),
                          -rng.random(int(ptr[-1])))
+
+
+@pytest.mark.parametrize("seed", range(30))
+def test_vanilla_select_matches_oracle_with_ties(seed):
+    """be_vanilla_select against the oracle's stable sort on rows with many ties:
+    rows in top-k order (the row-merge path) and rows in arbitrary order (the
+    partial-sort path)."""
+    from oracle.beam_state import vanilla_select
+    rng = np.random.default_rng(seed)
+    n, k = int(rng.integers(1, 20)), int(rng.integers(1, 40))
+    W = int(rng.integers(1, 2 * n * k + 2))
+    ps = np.round(rng.uniform(-3, 0, n) * 2) / 2
+    lp = np.round(rng.uniform(-3, 0, (n, k)) * 4) / 4
+    if seed % 2 == 0:
+        lp = -np.sort(-lp, axis=1)
+    toks = rng.integers(0, 1000, (n, k)).astype(np.int32)
+    ptr, ct, cs = vanilla_select_arrays(ps, toks, lp, W)
+    want = vanilla_select(ps.tolist(), toks.tolist(), lp.tolist(), W)
+    got = [[(int(ct[j]), float(cs[j])) for j in range(ptr[i], ptr[i + 1])] for i in range(n)]
+    assert got == want
