@@ -82,8 +82,8 @@ _SIGS = {
     "be_node_append_token": (C.c_int, [vp, i32, i32]),
     "be_node_sequence": (i64, [vp, i32, P32, i64]),
     "be_beam_add_root": (C.c_int, [vp, P32, C.c_int, P32, P32]),
-    "be_beam_update": (C.c_int, [vp, C.c_int, P32, P32, P32, P32, P32, P32, P32, P32, P32, P32]),
-    "be_beam_step_inputs": (C.c_int, [vp, C.c_int, P32, P32, P32, P32, P32]),
+    "be_beam_update": (C.c_int, [vp, C.c_int, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "be_beam_step_inputs": (C.c_int, [vp, C.c_int, vp, vp, vp, vp, vp]),
     "be_cascade_build": (C.c_int, [vp, C.c_int, P32, C.c_int, C.c_int, C.c_int, P32, P32, P32, P32,
                                    P32, P32]),
     "be_tree_build": (C.c_int, [vp, C.c_int, P32, C.c_int, C.c_int, C.c_int, P32, P32, P32, P32, P32, P32,
@@ -91,18 +91,18 @@ _SIGS = {
     "be_fasttree_prepare": (C.c_int, [C.c_int, P32, P32, P32, P32, P32, i64, C.c_int, C.c_int,
                                       C.c_int, C.c_int, C.c_int, P32, P32, P32, P32, P32, P32, P32,
                                       P32, P32]),
-    "be_vanilla_select_segments": (C.c_int, [C.c_int, P32, C.c_int, C.POINTER(C.c_double), P32,
-                                             C.POINTER(C.c_double), C.c_int, P32, P32,
-                                             C.POINTER(C.c_double), P32]),
-    "be_beam_decode_inputs": (C.c_int, [vp, C.c_int, P32, C.c_int, C.c_int, C.c_int, vp, i64,
+    "be_vanilla_select_segments": (C.c_int, [C.c_int, vp, C.c_int, vp, vp,
+                                             vp, C.c_int, vp, vp,
+                                             vp, vp]),
+    "be_beam_decode_inputs": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp, i64,
                                         C.c_int, C.POINTER(AttnPlanInfo)]),
-    "be_leaf_sequences": (i64, [vp, C.c_int, P32, P32, P32, i64]),
-    "be_diverse_select": (C.c_int, [C.c_int, P32, C.c_int, C.POINTER(C.c_double), P32,
-                                    C.POINTER(C.c_double), P32, P32, C.c_int, C.c_int, C.c_double,
-                                    C.c_int, C.c_double, P32, P32, C.POINTER(C.c_double), P32]),
-    "be_vanilla_select": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_double), P32,
-                                    C.POINTER(C.c_double), C.c_int, P32, P32,
-                                    C.POINTER(C.c_double)]),
+    "be_leaf_sequences": (i64, [vp, C.c_int, vp, vp, vp, i64]),
+    "be_diverse_select": (C.c_int, [C.c_int, vp, C.c_int, vp, vp,
+                                    vp, vp, vp, C.c_int, C.c_int, C.c_double,
+                                    C.c_int, C.c_double, vp, vp, vp, vp]),
+    "be_vanilla_select": (C.c_int, [C.c_int, C.c_int, vp, vp,
+                                    vp, C.c_int, vp, vp,
+                                    vp]),
 }
 
 
@@ -140,6 +140,12 @@ def check(rc, what=""):
     if rc == BE_ENOMEM:
         raise MemoryError(text)
     raise BeamEngineError(f"[status {rc}] {text}")
+
+
+def addr(arr):
+    """Address of a contiguous numpy array, for arguments bound as void* (half
+    the cost of ptr32 on the per-step host path)."""
+    return arr.ctypes.data
 
 
 def ptr32(arr):

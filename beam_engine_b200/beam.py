@@ -432,7 +432,7 @@ class BeamSearchGenerator:
         sg = self.step_graph
 
         def fill(buf_ptr, cap, plan_off):
-            rc = lib().be_beam_decode_inputs(self.page_table._trie, n, _lib.ptr32(leaves), m.Hq,
+            rc = lib().be_beam_decode_inputs(self.page_table._trie, n, _lib.addr(leaves), m.Hq,
                                              m.Hkv, self.attn.plan.num_sms, C.c_void_p(buf_ptr),
                                              cap, plan_off, C.byref(info))
             if rc not in (_lib.BE_OK, _lib.BE_ECAPACITY):

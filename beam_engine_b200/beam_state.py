@@ -228,10 +228,10 @@ class BeamState:
         leaves = np.ascontiguousarray(leaves, np.int32)
         child_ptr = np.ascontiguousarray(child_ptr, np.int32)
         child_tokens = np.ascontiguousarray(child_tokens, np.int32)
-        rc = lib().be_beam_update(self._t, len(leaves), _lib.ptr32(leaves), _lib.ptr32(child_ptr),
-                                  _lib.ptr32(child_tokens), _lib.ptr32(new_leaf),
-                                  _lib.ptr32(new_child), C.byref(n_new), _lib.ptr32(cs),
-                                  _lib.ptr32(cd), _lib.ptr32(cl), C.byref(n_cp))
+        rc = lib().be_beam_update(self._t, len(leaves), _lib.addr(leaves), _lib.addr(child_ptr),
+                                  _lib.addr(child_tokens), _lib.addr(new_leaf),
+                                  _lib.addr(new_child), C.byref(n_new), _lib.addr(cs),
+                                  _lib.addr(cd), _lib.addr(cl), C.byref(n_cp))
         if rc == _lib.BE_ENOMEM:
             raise MemoryError("No free pages available")
         check(rc, "add_filtered_results")
@@ -248,8 +248,8 @@ class BeamState:
         """(query tokens, write pages, write positions, RoPE positions), int32 arrays."""
         n = len(self._leaves)
         out = [np.zeros(max(n, 1), np.int32) for _ in range(4)]
-        check(lib().be_beam_step_inputs(self._t, n, _lib.ptr32(self._leaves),
-                                        *[_lib.ptr32(o) for o in out]), "step inputs")
+        check(lib().be_beam_step_inputs(self._t, n, _lib.addr(self._leaves),
+                                        *[_lib.addr(o) for o in out]), "step inputs")
         return [o[:n] for o in out]
 
     def cascade_levels(self):
@@ -357,15 +357,15 @@ class BeamState:
         ptr = np.zeros(n + 1, np.int32)
         cap = int(getattr(self, "_seq_cap", 0))
         buf = np.zeros(max(cap, 1), np.int32)
-        total = lib().be_leaf_sequences(self._t, n, _lib.ptr32(leaves), _lib.ptr32(ptr),
-                                        _lib.ptr32(buf), cap)
+        total = lib().be_leaf_sequences(self._t, n, _lib.addr(leaves), _lib.addr(ptr),
+                                        _lib.addr(buf), cap)
         if total < 0:
             check(_lib.BE_EINVAL, "leaf_sequences")
         if total > cap:
             self._seq_cap = cap = int(total * 1.25) + 64
             buf = np.zeros(cap, np.int32)
-            lib().be_leaf_sequences(self._t, n, _lib.ptr32(leaves), _lib.ptr32(ptr),
-                                    _lib.ptr32(buf), cap)
+            lib().be_leaf_sequences(self._t, n, _lib.addr(leaves), _lib.addr(ptr),
+                                    _lib.addr(buf), cap)
         return ptr, buf[:total]
 
     def get_final_sequences(self, num_return: int, length_penalty: float = 1.0

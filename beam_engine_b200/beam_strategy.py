@@ -67,12 +67,12 @@ def diverse_select_segments(seg, parent_scores, tokens, logps, seq_ptr, seq_toke
     cs = np.zeros(cap, np.float64)
     ns = np.zeros(len(seg), np.int32)
     D = C.POINTER(C.c_double)
-    check(lib().be_diverse_select(len(seg) - 1, _lib.ptr32(seg), k, ps.ctypes.data_as(D),
-                                  _lib.ptr32(tokens), logps.ctypes.data_as(D), _lib.ptr32(seq_ptr),
-                                  _lib.ptr32(seq_tokens), int(beam_size), int(num_groups),
+    check(lib().be_diverse_select(len(seg) - 1, _lib.addr(seg), k, ps.ctypes.data,
+                                  _lib.addr(tokens), logps.ctypes.data, _lib.addr(seq_ptr),
+                                  _lib.addr(seq_tokens), int(beam_size), int(num_groups),
                                   float(diversity_penalty), dtype, float(length_penalty),
-                                  _lib.ptr32(ptr), _lib.ptr32(ct), cs.ctypes.data_as(D),
-                                  _lib.ptr32(ns)), "diverse select")
+                                  _lib.addr(ptr), _lib.addr(ct), cs.ctypes.data,
+                                  _lib.addr(ns)), "diverse select")
     m = int(ptr[-1])
     return ptr, ct[:m], cs[:m], ns
 
@@ -87,10 +87,10 @@ def vanilla_select_arrays(parent_scores, tokens, logps, beam_size):
     ptr = np.zeros(n + 1, np.int32)
     ct = np.zeros(max(beam_size, 1), np.int32)
     cs = np.zeros(max(beam_size, 1), np.float64)
-    check(lib().be_vanilla_select(n, k, parent_scores.ctypes.data_as(C.POINTER(C.c_double)),
-                                  _lib.ptr32(tokens), logps.ctypes.data_as(C.POINTER(C.c_double)),
-                                  beam_size, _lib.ptr32(ptr), _lib.ptr32(ct),
-                                  cs.ctypes.data_as(C.POINTER(C.c_double))), "vanilla select")
+    check(lib().be_vanilla_select(n, k, parent_scores.ctypes.data,
+                                  _lib.addr(tokens), logps.ctypes.data,
+                                  beam_size, _lib.addr(ptr), _lib.addr(ct),
+                                  cs.ctypes.data), "vanilla select")
     m = int(ptr[-1])
     return ptr, ct[:m], cs[:m]
 
@@ -138,10 +138,10 @@ class VanillaBeamSearchStrategy(BeamStrategy):
         cs = np.zeros(cap, np.float64)
         ns = np.zeros(len(seg), np.int32)
         D = C.POINTER(C.c_double)
-        check(lib().be_vanilla_select_segments(len(seg) - 1, _lib.ptr32(seg), k, ps.ctypes.data_as(D),
-                                               _lib.ptr32(tokens), logps.ctypes.data_as(D),
-                                               beam_size, _lib.ptr32(ptr), _lib.ptr32(ct),
-                                               cs.ctypes.data_as(D), _lib.ptr32(ns)),
+        check(lib().be_vanilla_select_segments(len(seg) - 1, _lib.addr(seg), k, ps.ctypes.data,
+                                               _lib.addr(tokens), logps.ctypes.data,
+                                               beam_size, _lib.addr(ptr), _lib.addr(ct),
+                                               cs.ctypes.data, _lib.addr(ns)),
               "select_segments")
         m = int(ptr[-1])
         return ptr, ct[:m], cs[:m], ns
