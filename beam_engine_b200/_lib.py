@@ -96,6 +96,8 @@ _SIGS = {
                                              vp, vp]),
     "be_beam_decode_inputs": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp, i64,
                                         C.c_int, C.POINTER(AttnPlanInfo)]),
+    "be_fork_tail_copy_list": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                         C.c_int, vp, C.c_int, C.c_int, vp]),
     "be_leaf_sequences": (i64, [vp, C.c_int, vp, vp, vp, i64]),
     "be_diverse_select": (C.c_int, [C.c_int, vp, C.c_int, vp, vp,
                                     vp, vp, vp, C.c_int, C.c_int, C.c_double,

@@ -97,13 +97,25 @@ class PlannedAttention:
             t.append((s, e))
 
 
+def step_plan_offset(n):
+    """Offset (int32 units) of the attention plan in a step buffer of n beams."""
+    return -(-(7 * n + 1) // 32) * 32
+
+
+def _pool_dtype(pt):
+    return (_lib.BE_F32 if pt.store_dtype == torch.float32 else
+            (_lib.BE_BF16 if pt.store_dtype == torch.bfloat16 else _lib.BE_F16))
+
+
 class StepGraph:
     """One beam decode step (forward over all layers, log-softmax, top-k, D2H
     of the top-k) recorded once as a CUDA graph and replayed every step.
 
     Everything that changes per step lives in one static device buffer
-    [query ids | positions | append pages | append slots | attention plan
-    | slot list (tree plans)] filled by one H2D copy before the replay;
+    [query ids | positions | append pages | append slots | fork copy list
+    | attention plan | slot list (tree plans)] filled by one H2D copy before
+    the replay; the step's first launch performs the copy-on-write tail copies
+    of the previous selection (``be_fork_tail_copy_list``);
     attention runs through ``be_attn_run_fixed_2s``, whose launch shape depends
     only on the capacities (the kernels read the plan's counts from its
     device-side header).  ``kind`` is "cascade" (page-list plans, tensor-core
@@ -116,7 +128,9 @@ class StepGraph:
         self.caps = dict(caps)
         self.caps.setdefault("slots", 0)
         dev = gen.device
-        self.plan_off = -(-4 * n // 32) * 32
+        # [q | pos | pages | slots] then the fork list [count | src[n] | dst[n] | len[n]]
+        self.fork_off = 4 * n
+        self.plan_off = step_plan_offset(n)
         self.slots_off = self.plan_off + -(-self.caps["ints"] // 32) * 32
         self.total = self.slots_off + self.caps["slots"]
         self.dev_buf = torch.zeros(self.total, dtype=torch.int32, device=dev)
@@ -180,9 +194,29 @@ class StepGraph:
         check(rc, "be_attn_run_fixed_2s")
         self._mark(2 * layer + 1, qkv)
 
+    def set_fork(self, copies):
+        """Write the pending copy-on-write list (src, dst, len arrays; None = none)."""
+        h = self.host_buf.numpy()
+        n, o = self.n, self.fork_off
+        if copies is None or len(copies[0]) == 0:
+            h[o] = 0
+            return
+        c = len(copies[0])
+        h[o] = c
+        h[o + 1:o + 1 + c] = copies[0]
+        h[o + 1 + n:o + 1 + n + c] = copies[1]
+        h[o + 1 + 2 * n:o + 1 + 2 * n + c] = copies[2]
+
     def _body(self):
         n = self.n
         d = self.dev_buf
+        pt = self.gen.page_table
+        check(lib().be_fork_tail_copy_list(pt.kv_cache.data_ptr(), pt.kv_cache.stride(0),
+                                           pt.layer_num, pt.max_num_pages, pt.page_size,
+                                           pt.head_num, pt.head_dim, _pool_dtype(pt),
+                                           d.data_ptr() + 4 * self.fork_off, n,
+                                           self.gen.attn.plan.num_sms,
+                                           stream_ptr(self.gen.device)), "fork list")
         logits = self.gen.model.forward(d[0:n], d[n:2 * n], self.gen.page_table, d[2 * n:3 * n],
                                         d[3 * n:4 * n], self)
         v, i = self.gen._logprob_topk(logits, self.k, self.temp)
@@ -190,9 +224,10 @@ class StepGraph:
         self.idx_h.copy_(i.reshape(-1), non_blocking=True)
 
     def step_filled(self, used):
-        """Replay with host_buf[:used] already holding [q | pos | pages | slots | plan]."""
+        """Replay with host_buf[:used] already holding [q | pos | pages | slots | fork | plan]."""
         n = self.n
         self.dev_buf[:used].copy_(self.host_buf[:used], non_blocking=True)
+        self.gen.h2d_bytes += 4 * used
         if self.graph is None:
             t0 = time.perf_counter()
             if not self.gen._graph_warm:   # first capture of the generator: warm libraries up
@@ -260,6 +295,8 @@ class BeamSearchGenerator:
         self.graph_captures = []      # seconds spent recording each step graph
         self.graph_regrowth = []      # why a step graph was recorded again
         self._graph_warm = False
+        self._pending_fork = None     # copies of the last selection, run by the next graph step
+        self.h2d_bytes = 0            # host -> device bytes copied by the engine (inputs, plans)
 
     # ------------------------------------------------------------------
     def generate(self, input_text: str, beam_size: int = 4, max_length: int = 50,
@@ -288,6 +325,7 @@ class BeamSearchGenerator:
             off += len(a)
         dev = torch.empty(n, dtype=torch.int32, device=self.device)
         dev.copy_(self.meta_host[:n], non_blocking=True)
+        self.h2d_bytes += 4 * n
         self._meta_ev = torch.cuda.Event()
         self._meta_ev.record()
         out, off = [], 0
@@ -394,6 +432,7 @@ class BeamSearchGenerator:
             self.step_graph_tree = sg = StepGraph(self, n, k, temperature, caps, kind="fasttree")
         h = sg.host_buf.numpy()
         h[0:n], h[n:2 * n], h[2 * n:3 * n], h[3 * n:4 * n] = q, pos, wp, wpos
+        self._take_fork(sg)
         h[sg.plan_off:sg.plan_off + info.total_ints] = plan[:info.total_ints]
         h[sg.slots_off:sg.slots_off + len(slots)] = slots
         return sg.step_filled(sg.slots_off + len(slots))
@@ -402,6 +441,7 @@ class BeamSearchGenerator:
         """One beam step's forward: returns logits [beams, vocab]."""
         if kind is None:
             kind = self.pick_kernel(state) if self.kernel_type == "auto" else self.kernel_type
+        self._flush_fork()
         q, wp, wpos, pos = state.step_inputs()
         if kind == "cascade":
             levels = state.cascade_levels()
@@ -443,7 +483,7 @@ class BeamSearchGenerator:
                 and fill(sg.host_buf.data_ptr(), sg.total, sg.plan_off)
                 and sg.fits(n, k, temperature, info)):
             # size a new graph from this step's plan (grow the probe buffer until it fits)
-            off = -(-4 * n // 32) * 32
+            off = step_plan_offset(n)
             size = off + 65536
             while True:
                 probe = np.empty(size, np.int32)
@@ -474,6 +514,7 @@ class BeamSearchGenerator:
                 raise RuntimeError("decode step graph sized too small for its own plan")
         if self.plan_hook is not None:
             self.plan_hook(n, info)
+        self._take_fork(sg)
         return sg.step_filled(sg.plan_off + info.total_ints)
 
     def generate_ids(self, prompts: List[List[int]], beam_size: int = 4,
@@ -533,6 +574,7 @@ class BeamSearchGenerator:
                     self._apply(state, np.asarray(ptr_all, np.int32), np.asarray(tok_all, np.int32),
                                 np.asarray(sc_all, np.float64))
                 seg = np.asarray(new_seg)
+            self._flush_fork()
             if on_step is not None:
                 on_step(n_steps)
         out = []
@@ -545,14 +587,34 @@ class BeamSearchGenerator:
 
     def _apply(self, state, child_ptr, child_tokens, child_scores):
         state.update_native(state.leaves, child_ptr, child_tokens, child_scores)
+        self._flush_fork()
         cs, cd, cl = state.last_copies
         if len(cs):
-            d = self._to_device([cs, cd, cl])
-            pt = self.page_table
-            check(lib().be_fork_tail_copy(pt.kv_cache.data_ptr(), pt.kv_cache.stride(0),
-                                          pt.layer_num, pt.max_num_pages, pt.page_size,
-                                          pt.head_num, pt.head_dim,
-                                          _lib.BE_F32 if pt.store_dtype == torch.float32 else
-                                          (_lib.BE_BF16 if pt.store_dtype == torch.bfloat16 else _lib.BE_F16),
-                                          d[0].data_ptr(), d[1].data_ptr(), d[2].data_ptr(), len(cs),
-                                          stream_ptr(self.device)), "fork")
+            if self.use_graph or self.use_graph_tree:
+                self._pending_fork = (cs, cd, cl)   # the next step graph's first launch
+            else:
+                self._fork_now((cs, cd, cl))
+
+    def _fork_now(self, copies):
+        cs, cd, cl = copies
+        d = self._to_device([cs, cd, cl])
+        pt = self.page_table
+        check(lib().be_fork_tail_copy(pt.kv_cache.data_ptr(), pt.kv_cache.stride(0),
+                                      pt.layer_num, pt.max_num_pages, pt.page_size,
+                                      pt.head_num, pt.head_dim, _pool_dtype(pt),
+                                      d[0].data_ptr(), d[1].data_ptr(), d[2].data_ptr(), len(cs),
+                                      stream_ptr(self.device)), "fork")
+
+    def _flush_fork(self):
+        """Run pending copy-on-write copies now (a path without a step graph)."""
+        if self._pending_fork is not None:
+            copies, self._pending_fork = self._pending_fork, None
+            self._fork_now(copies)
+
+    def _take_fork(self, sg):
+        """Hand the pending copies to the step graph about to replay."""
+        copies, self._pending_fork = self._pending_fork, None
+        if copies is not None and len(copies[0]) > sg.n:   # more than the list holds
+            self._fork_now(copies)
+            copies = None
+        sg.set_fork(copies)

@@ -188,3 +188,66 @@ extern "C" int be_device_status_clear(void* stream) {
                                         cudaMemcpyHostToDevice, (cudaStream_t)stream));
   return BE_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Fork with the copy list in device memory (for a captured decode step):
+// list = [count | src[cap] | dst[cap] | len[cap]].  A fixed grid strides over
+// the count * layers * 2 (copy, layer, plane) segments, so one launch shape
+// serves every step; a step without copies costs one wave of empty CTAs.
+// ---------------------------------------------------------------------------
+namespace be {
+
+__global__ void __launch_bounds__(256) fork_list_kernel(
+    char* __restrict__ pool, int64_t pool_layer_stride_b, int num_layers, int num_pages,
+    int page_size, int64_t tok_bytes, const int32_t* __restrict__ list, int cap) {
+  const int count = min(max(list[0], 0), cap);
+  const int32_t* src_pages = list + 1;
+  const int32_t* dst_pages = list + 1 + cap;
+  const int32_t* lens = list + 1 + 2 * cap;
+  const int64_t plane_bytes = page_size * tok_bytes;
+  const int64_t nseg = (int64_t)count * num_layers * 2;
+  for (int64_t seg = blockIdx.x; seg < nseg; seg += gridDim.x) {
+    const int plane = (int)(seg & 1);
+    const int64_t jl = seg >> 1;
+    const int layer = (int)(jl % num_layers);
+    const int j = (int)(jl / num_layers);
+    const int s = src_pages[j], d = dst_pages[j], len = lens[j];
+    if (s < 0 || s >= num_pages || d < 0 || d >= num_pages || len < 0 || len > page_size) {
+      if (threadIdx.x == 0) flag_range_error();
+      continue;
+    }
+    const int4* s4 = reinterpret_cast<const int4*>(
+        pool + layer * pool_layer_stride_b + ((int64_t)s * 2 + plane) * plane_bytes);
+    int4* d4 = reinterpret_cast<int4*>(pool + layer * pool_layer_stride_b +
+                                       ((int64_t)d * 2 + plane) * plane_bytes);
+    const int n16 = (int)((len * tok_bytes) >> 4);
+    for (int c = threadIdx.x; c < n16; c += blockDim.x) d4[c] = __ldg(s4 + c);
+  }
+}
+
+}  // namespace be
+
+extern "C" int be_fork_tail_copy_list(void* paged_kv_cache, int64_t pool_layer_stride,
+                                      int num_layers, int num_pages, int page_size,
+                                      int num_kv_heads, int head_dim, int dtype,
+                                      const int32_t* copy_list, int cap, int num_sms,
+                                      void* stream) {
+  using namespace be;
+  if (!paged_kv_cache || !copy_list || cap < 0 || num_layers < 1 || page_size < 1 ||
+      num_kv_heads < 1 || head_dim < 1 || dtype < BE_F32 || dtype > BE_BF16) {
+    set_error("be_fork_tail_copy_list: invalid arguments");
+    return BE_EINVAL;
+  }
+  const int elt = dtype_size(dtype);
+  const int64_t tok_bytes = (int64_t)num_kv_heads * head_dim * elt;
+  if (tok_bytes % 16 || ((uintptr_t)paged_kv_cache % 16) || (pool_layer_stride * elt) % 16) {
+    set_error("be_fork_tail_copy_list: pool rows must be 16-byte aligned");
+    return BE_EINVAL;
+  }
+  const int grid = 4 * (num_sms > 0 ? num_sms : 148);
+  fork_list_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      (char*)paged_kv_cache, pool_layer_stride * elt, num_layers, num_pages, page_size, tok_bytes,
+      copy_list, cap);
+  BE_LAUNCH_CHECK();
+  return BE_OK;
+}

@@ -172,8 +172,9 @@ def run_b200(args, rank, world, local_rank):
                               + 2 * nq * model.Hq * model.D * 2)
             plan_stats.append((nq, inf.n_work, inf.n_work_wide, inf.n_parts, inf.n_merge))
             # per layer: 2 add_rmsnorm, rope_append, silu_mul + attention (tcgen05 wide,
-            # all-heads narrow, LSE merge); final norm; fused log-softmax / top-k
-            launches["n"] += cfg["num_hidden_layers"] * (4 + 3) + 1 + 1
+            # all-heads narrow, LSE merge); final norm; fused log-softmax / top-k; the
+            # copy-on-write fork list at the head of the step
+            launches["n"] += cfg["num_hidden_layers"] * (4 + 3) + 1 + 1 + 1
 
     gen.plan_hook = plan_hook
     orig_apply = gen._apply
@@ -187,8 +188,6 @@ def run_b200(args, rank, world, local_rank):
             kids = int(cp[-1])
             if kids:
                 churn.append(1.0 - int((np.diff(cp) > 0).sum()) / kids)
-        if timing["on"] and len(state.last_copies[0]):
-            launches["n"] += 1
 
     gen._apply = apply_hook
 
@@ -243,14 +242,7 @@ def run_b200(args, rank, world, local_rank):
         dist.barrier()
     gen2_t0 = torch.cuda.Event(enable_timing=True)
     gen2_t1 = torch.cuda.Event(enable_timing=True)
-    h2d = {"b": 0}
-    orig_to_dev = gen._to_device
-
-    def count_h2d(arrays):
-        h2d["b"] += sum(len(a) for a in arrays) * 4
-        return orig_to_dev(arrays)
-
-    gen._to_device = count_h2d
+    h2d0 = gen.h2d_bytes
     gen2_t0.record()
     t0 = time.perf_counter()
     out = gen.generate_ids(prompts, BEAM, max_new_tokens=NEW_TOKENS)
@@ -304,7 +296,7 @@ def run_b200(args, rank, world, local_rank):
                           round(step_bytes / (ms_max / K / 1e3) / 1e9, 1),
                           "frac": round(step_bytes / (ms_max / K / 1e3) / 1e9 / hbm, 4)},
         "e2e": {"value": round(e2e_tokens / (e2e_ms / 1e3), 2), "unit": "beam tokens/s",
-                "h2d_bytes_per_step": int(h2d["b"] / steps_e2e),
+                "h2d_bytes_per_step": int((gen.h2d_bytes - h2d0) / steps_e2e),
                 "d2h_bytes_per_step": d2h,
                 "includes": "prefill of 8 x 1024 prompt tokens + 127 decode steps, host ids in, "
                             "host beams out", "wall_ms": round(wall_ms, 1)},

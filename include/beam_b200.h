@@ -77,6 +77,15 @@ int be_fork_tail_copy(void* paged_kv_cache, int64_t pool_layer_stride, int num_l
                       const int32_t* src_pages, const int32_t* dst_pages, const int32_t* lens,
                       int num_copies, void* stream);
 
+/* be_fork_tail_copy with the copy list in device memory, for a decode step
+ * recorded once as a CUDA graph: copy_list = [count | src_pages[cap] |
+ * dst_pages[cap] | lens[cap]] (int32).  The launch shape depends only on
+ * num_sms, so the same recorded launch serves every step's list.            */
+int be_fork_tail_copy_list(void* paged_kv_cache, int64_t pool_layer_stride, int num_layers,
+                           int num_pages, int page_size, int num_kv_heads, int head_dim,
+                           int dtype, const int32_t* copy_list, int cap, int num_sms,
+                           void* stream);
+
 /* ------------------------------------------------------------------------
  * Paged attention plans.  A plan is a flat int32 buffer built on the host by
  * be_cascade_plan / be_tree_plan, copied to the device by the caller, and run
