@@ -1,4 +1,4 @@
-"""Tensor parallelism on CPU ranks (gloo, world size 2): the sharding of
+"""Tensor parallelism on CPU ranks (gloo, world sizes 2 and 4): the sharding of
 :class:`BeamLlama` and the vocab-parallel log-softmax / top-k reproduce the
 unsharded model.  The decoder layer is run here in plain torch (fp32, causal
 dense attention with RoPE) on each rank's weight shards, with the same
@@ -9,9 +9,8 @@ import socket
 
 import torch
 import torch.distributed as dist
+import pytest
 import torch.multiprocessing as mp
-
-WORLD = 2
 
 
 def _free_port():
@@ -68,12 +67,16 @@ def _forward(m, ids, tp):
     return h @ m.lm_head.float().t()
 
 
-def _worker(rank, port, q):
+def _worker(rank, port, q, WORLD):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
     try:
-        from beam_engine_b200.configs import TINY
+        from beam_engine_b200.configs import TINY as T0
+        # 4 ranks: one KV head and two query heads per rank (the 8B shape at TP = 8 has
+        # one KV head per rank too)
+        TINY = T0 if WORLD == 2 else dict(T0, num_attention_heads=8, num_key_value_heads=4,
+                                          head_dim=32)
         from beam_engine_b200.llama import BeamLlama
         from beam_engine_b200.parallel import TensorParallel, vocab_parallel_log_softmax_topk
         torch.manual_seed(0)
@@ -102,11 +105,12 @@ def _worker(rank, port, q):
         dist.destroy_process_group()
 
 
-def test_tensor_parallel_matches_unsharded_gloo():
+@pytest.mark.parametrize("WORLD", [2, 4])
+def test_tensor_parallel_matches_unsharded_gloo(WORLD):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, port, q, WORLD)) for r in range(WORLD)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(WORLD)]
