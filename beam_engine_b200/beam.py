@@ -535,6 +535,7 @@ class BeamSearchGenerator:
         else:
             n_steps = max_new_tokens - 1
         W = beam_size
+        self._pending_fork = None    # copies left by an interrupted earlier call are void
         state = BeamState(W, self.page_table)
         state.defer_copies = True
         V = self.model.vocab
