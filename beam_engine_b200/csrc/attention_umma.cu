@@ -119,7 +119,11 @@ __global__ void __launch_bounds__(160) attn_umma_kernel(const __grid_constant__ 
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 5);
 
-  pdl_wait();   // q and the plan come from earlier kernels / copies on this stream
+  // Fixed-grid launches (p.hdr set) take a plan that is in device memory before
+  // the preceding kernel starts (the step's host copy): it is read before
+  // pdl_wait(), overlapping that kernel.  Otherwise, and for q and the pages
+  // the preceding kernels write, everything waits.
+  if (!p.hdr) pdl_wait();
   resolve_plan(p);
   if ((int)blockIdx.x >= plan_n_wide(p)) return;  // before any barrier or TMEM use
   const Work w = p.work[blockIdx.x];
@@ -155,6 +159,7 @@ __global__ void __launch_bounds__(160) attn_umma_kernel(const __grid_constant__ 
   stamp(p, 1);
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();
 
   if (warp == 4) {
     // ------------- producer: page ids (one coalesced read) -> TMA -------------

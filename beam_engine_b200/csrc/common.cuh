@@ -40,6 +40,11 @@ inline int dtype_size(int dt) { return dt == BE_F32 ? 4 : 2; }
 // launch latency overlaps that tail); it must call pdl_wait() before it reads
 // anything the previous kernel writes.  BE_PDL=0 turns the attribute off.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next PDL kernel on the stream start its preamble now (it still waits
+// in pdl_wait() for this grid's completion before reading what it wrote).
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 inline bool pdl_enabled() {
   static int v = -1;

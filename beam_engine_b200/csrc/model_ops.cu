@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
     T* __restrict__ pool, int num_pages, int page_size, const int32_t* __restrict__ write_page,
     const int32_t* __restrict__ write_pos, int write_rope_k_in_place) {
   pdl_wait();
+  pdl_trigger();   // the attention launch after this one prepares (plan reads, TMEM) meanwhile
   const int warps_per_row = hq + 2 * hkv;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;

@@ -214,8 +214,11 @@ typedef struct {
  * calls without any host involvement.  Page-list plans with page size 16 use
  * the tensor-core kernels; wide items must span <= 256 tokens (the planner's
  * decode chunks do); a plan that breaks the caps is flagged in the device
- * status and its surplus items are skipped.  Same contract as
- * MultiLevelCascadeAttentionWrapper.run (modeling_llama.py:362).            */
+ * status and its surplus items are skipped.  The plan must be in device
+ * memory before the kernel preceding this call on the stream starts (a host
+ * copy, as in a recorded decode step): the kernels read it while that kernel
+ * finishes.  Same contract as MultiLevelCascadeAttentionWrapper.run
+ * (modeling_llama.py:362).                                                   */
 int be_attn_run_fixed(const int32_t* plan_dev, const be_attn_caps* caps, int page_size,
                       const void* q, int64_t q_row_stride, const void* paged_kv_cache,
                       int num_pages, int num_qo_heads, int num_kv_heads, int head_dim, int dtype,
