@@ -32,6 +32,23 @@ from .parallel import vocab_parallel_log_softmax_topk
 
 logger = logging.getLogger(__name__)
 UMMA_MAX_TOKENS = 128   # BE_UMMA_MAX_TOKENS in include/beam_b200.h
+_NVTX = os.environ.get("BE_NVTX", "0") == "1"   # NVTX ranges per generation phase
+
+
+class _Range:
+    """NVTX range (BE_NVTX=1) around a phase of generation, for nsys / ncu timelines."""
+    __slots__ = ("name",)
+
+    def __init__(self, name):
+        self.name = name
+
+    def __enter__(self):
+        if _NVTX:
+            torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *exc):
+        if _NVTX:
+            torch.cuda.nvtx.range_pop()
 
 
 def _i32(a):
@@ -540,7 +557,8 @@ class BeamSearchGenerator:
         state.defer_copies = True
         V = self.model.vocab
         with torch.no_grad():
-            logits = self.prefill(state, prompts)
+            with _Range("prefill"):
+                logits = self.prefill(state, prompts)
             k0 = min(2 * W, V)
             vals, idx = self._topk(logits, k0, temperature)
             kw = min(W, k0)
@@ -553,27 +571,29 @@ class BeamSearchGenerator:
                 if on_step is not None:
                     on_step(step)
                 k = min(2 * W, V) if W != 1 else 1
-                vals, idx = self.decode_topk(state, k, temperature)
-                if getattr(self.strategy, "needs_state", False):
-                    cp, ct, cs, new_seg = self.strategy.select_segments(seg, state.scores, idx, vals, W,
-                                                                        state=state)
-                    self._apply(state, cp, ct, cs)
-                elif hasattr(self.strategy, "select_segments"):
-                    cp, ct, cs, new_seg = self.strategy.select_segments(seg, state.scores, idx, vals, W)
-                    self._apply(state, cp, ct, cs)
-                else:
-                    ptr_all, tok_all, sc_all = [0], [], []
-                    new_seg = [0]
-                    for p in range(len(prompts)):
-                        a, b = seg[p], seg[p + 1]
-                        cp, ct, cs = self.strategy.select_arrays(state.scores[a:b], idx[a:b],
-                                                                 vals[a:b], W)
-                        ptr_all.extend((cp[1:] + len(tok_all)).tolist())
-                        tok_all.extend(ct.tolist())
-                        sc_all.extend(cs.tolist())
-                        new_seg.append(new_seg[-1] + int(cp[-1]))
-                    self._apply(state, np.asarray(ptr_all, np.int32), np.asarray(tok_all, np.int32),
-                                np.asarray(sc_all, np.float64))
+                with _Range("decode_step"):
+                    vals, idx = self.decode_topk(state, k, temperature)
+                with _Range("select"):
+                    if getattr(self.strategy, "needs_state", False):
+                        cp, ct, cs, new_seg = self.strategy.select_segments(seg, state.scores, idx, vals, W,
+                                                                            state=state)
+                        self._apply(state, cp, ct, cs)
+                    elif hasattr(self.strategy, "select_segments"):
+                        cp, ct, cs, new_seg = self.strategy.select_segments(seg, state.scores, idx, vals, W)
+                        self._apply(state, cp, ct, cs)
+                    else:
+                        ptr_all, tok_all, sc_all = [0], [], []
+                        new_seg = [0]
+                        for p in range(len(prompts)):
+                            a, b = seg[p], seg[p + 1]
+                            cp, ct, cs = self.strategy.select_arrays(state.scores[a:b], idx[a:b],
+                                                                     vals[a:b], W)
+                            ptr_all.extend((cp[1:] + len(tok_all)).tolist())
+                            tok_all.extend(ct.tolist())
+                            sc_all.extend(cs.tolist())
+                            new_seg.append(new_seg[-1] + int(cp[-1]))
+                        self._apply(state, np.asarray(ptr_all, np.int32), np.asarray(tok_all, np.int32),
+                                    np.asarray(sc_all, np.float64))
                 seg = np.asarray(new_seg)
             self._flush_fork()
             if on_step is not None:
