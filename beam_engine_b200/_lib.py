@@ -98,6 +98,13 @@ _SIGS = {
                                         C.c_int, C.POINTER(AttnPlanInfo)]),
     "be_fork_tail_copy_list": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                          C.c_int, vp, C.c_int, C.c_int, vp]),
+    "be_comm_create": (C.c_int, [C.c_int, C.c_int, i64, C.c_int, C.c_int, vp, C.POINTER(vp)]),
+    "be_comm_open": (C.c_int, [vp, vp]),
+    "be_comm_slot": (vp, [vp, C.c_int]),
+    "be_comm_close_peers": (C.c_int, [vp]),
+    "be_comm_destroy": (C.c_int, [vp]),
+    "be_comm_allreduce_rmsnorm": (C.c_int, [vp, C.c_int, vp, vp, vp, C.c_int, C.c_int, C.c_float,
+                                            C.c_int, vp]),
     "be_leaf_sequences": (i64, [vp, C.c_int, vp, vp, vp, i64]),
     "be_diverse_select": (C.c_int, [C.c_int, vp, C.c_int, vp, vp,
                                     vp, vp, vp, C.c_int, C.c_int, C.c_double,

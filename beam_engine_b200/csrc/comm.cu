@@ -1,0 +1,336 @@
+// Tensor-parallel all-reduce over peer memory, fused with the residual add and
+// the RMSNorm that follow it in the decoder layer.
+//
+// The row-parallel projections (o_proj, down_proj) end in an all-reduce of a
+// [rows, hidden] partial, and the layer continues with residual += sum;
+// h = rmsnorm(residual) * w.  For decode (128 rows x 4096 = 1 MiB) a ring
+// all-reduce is latency-bound, so each rank instead:
+//   1. has its GEMM write the partial straight into its own slot of a buffer
+//      the other ranks have mapped (CUDA IPC, one process per GPU);
+//   2. per CTA (one CTA per row, grid-stride beyond the flag capacity): signals
+//      every rank with a per-CTA counter (st.release.sys to the peer's flag
+//      array) and waits until every rank has signalled the same count
+//      (ld.acquire.sys, bounded by %globaltimer: on expiry BE_EDEVICE_TIMEOUT is
+//      recorded and the CTA returns);
+//   3. reads the row from every rank's slot (plain 16-byte loads over NVLink,
+//      L2-only, in rank order so every rank computes identical bits), sums in
+//      fp32, rounds to the storage type, adds it to the residual, and writes
+//      the normalised row -- the add_rmsnorm kernel's arithmetic.
+// Consecutive calls alternate between two slots: a rank can only write a slot
+// again after the barrier of the call in between, which every rank reaches
+// after finishing its reads of that slot -- so no closing barrier is needed.
+// No TMA, no multicast: peers' memory is only touched by plain loads/stores.
+#include "common.cuh"
+
+#include <vector>
+
+namespace be {
+
+constexpr int COMM_MAX_RANKS = 8;
+constexpr uint64_t kCommWaitNs = 2000000000ull;   // 2 s
+
+struct CommArgs {
+  uint32_t* flags_out[COMM_MAX_RANKS];  // every rank's incoming-flag array
+  uint32_t* flags_in;                   // this rank's: [cta][src rank]
+  uint32_t* counter;                    // this rank's per-CTA call counter
+  const char* slot[COMM_MAX_RANKS];     // every rank's slot of this call
+  int rank, world, max_ctas;
+};
+
+__device__ __forceinline__ uint64_t comm_gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Barrier of CTA `cta` across ranks; false if it timed out.
+__device__ bool comm_barrier(const CommArgs& a, int cta) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    const uint32_t e = a.counter[cta] + 1;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");   // prior writes before the signal
+    for (int p = 0; p < a.world; ++p)
+      st_release_sys(a.flags_out[p] + (size_t)cta * COMM_MAX_RANKS + a.rank, e);
+    bool good = true;
+    const uint64_t t0 = comm_gtimer();
+    for (int p = 0; p < a.world && good; ++p) {
+      const uint32_t* f = a.flags_in + (size_t)cta * COMM_MAX_RANKS + p;
+      int polls = 0;
+      while ((int32_t)(ld_acquire_sys(f) - e) < 0) {   // monotonic: a peer may be ahead
+        if (++polls == 64) {
+          polls = 0;
+          if (comm_gtimer() - t0 > kCommWaitNs) {
+            atomicCAS(&g_device_status, 0, BE_EDEVICE_TIMEOUT);
+            good = false;
+            break;
+          }
+        }
+      }
+    }
+    a.counter[cta] = e;
+    ok = good ? 1 : 0;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+template <typename T>
+__device__ __forceinline__ void load16_cg(const T* p, float* out) {
+  const int4 raw = __ldcg(reinterpret_cast<const int4*>(p));
+  if constexpr (sizeof(T) == 2) {
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = to_f(e[i]);
+  } else {
+    out[0] = __int_as_float(raw.x);
+    out[1] = __int_as_float(raw.y);
+    out[2] = __int_as_float(raw.z);
+    out[3] = __int_as_float(raw.w);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void load16(const T* p, float* out) {
+  const int4 raw = *reinterpret_cast<const int4*>(p);
+  if constexpr (sizeof(T) == 2) {
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = to_f(e[i]);
+  } else {
+    out[0] = __int_as_float(raw.x);
+    out[1] = __int_as_float(raw.y);
+    out[2] = __int_as_float(raw.z);
+    out[3] = __int_as_float(raw.w);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store16(T* p, const float* v) {
+  int4 raw;
+  if constexpr (sizeof(T) == 2) {
+    T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) e[i] = from_f<T>(v[i]);
+  } else {
+    raw = make_int4(__float_as_int(v[0]), __float_as_int(v[1]), __float_as_int(v[2]),
+                    __float_as_int(v[3]));
+  }
+  *reinterpret_cast<int4*>(p) = raw;
+}
+
+// One CTA per row (grid-stride).  With residual: residual += round_T(sum);
+// out = w * round_T(residual * rsqrt(mean(residual^2) + eps)).  Without it:
+// out = round_T(sum).  H <= 256 threads x 8 vectors x (16 / sizeof(T)).
+template <typename T>
+__global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(CommArgs a, T* __restrict__ residual,
+                                                                const T* __restrict__ w,
+                                                                T* __restrict__ out, int rows,
+                                                                int H, float eps) {
+  constexpr int V = 16 / sizeof(T);
+  const int cta = blockIdx.x;
+  if (!comm_barrier(a, cta)) return;
+  __shared__ float red[32];
+  for (int row = cta; row < rows; row += gridDim.x) {
+    float cache[8][V];
+    float ss = 0.f;
+    int nv = 0;
+    const int64_t base = (int64_t)row * H;
+    for (int c = threadIdx.x * V; c < H; c += blockDim.x * V, ++nv) {
+      float s[V];
+      load16_cg(reinterpret_cast<const T*>(a.slot[0]) + base + c, s);
+      for (int p = 1; p < a.world; ++p) {
+        float t[V];
+        load16_cg(reinterpret_cast<const T*>(a.slot[p]) + base + c, t);
+#pragma unroll
+        for (int i = 0; i < V; ++i) s[i] += t[i];
+      }
+      if (residual) {
+        float x[V];
+        load16(residual + base + c, x);
+#pragma unroll
+        for (int i = 0; i < V; ++i) x[i] = to_f(from_f<T>(x[i] + to_f(from_f<T>(s[i]))));
+        store16(residual + base + c, x);
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          ss += x[i] * x[i];
+          cache[nv][i] = x[i];
+        }
+      } else {
+        store16(out + base + c, s);
+      }
+    }
+    if (!residual) continue;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+      for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] / (float)H + eps);
+    nv = 0;
+    for (int c = threadIdx.x * V; c < H; c += blockDim.x * V, ++nv) {
+      float wv[V], r[V];
+      load16(w + c, wv);
+#pragma unroll
+      for (int i = 0; i < V; ++i) r[i] = wv[i] * to_f(from_f<T>(cache[nv][i] * inv));
+      store16(out + base + c, r);
+    }
+    __syncthreads();   // red[] is reused by the next row
+  }
+}
+
+}  // namespace be
+
+using namespace be;
+
+struct be_comm {
+  int rank = 0, world = 0, num_slots = 0, max_ctas = 0, device = 0;
+  int64_t slot_bytes = 0;
+  size_t flags_bytes = 0;       // flags + counters, rounded up to 256
+  char* base = nullptr;         // this rank's allocation
+  char* peer[COMM_MAX_RANKS] = {};
+  bool opened[COMM_MAX_RANKS] = {};
+};
+
+static size_t comm_flags_bytes(int max_ctas) {
+  const size_t b = (size_t)max_ctas * COMM_MAX_RANKS * 4 + (size_t)max_ctas * 4;
+  return (b + 255) / 256 * 256;
+}
+
+extern "C" int be_comm_create(int world, int rank, int64_t slot_bytes, int num_slots,
+                              int max_ctas, void* handle_out, be_comm** out) {
+  if (!out || !handle_out || world < 1 || world > COMM_MAX_RANKS || rank < 0 || rank >= world ||
+      slot_bytes < 16 || slot_bytes % 16 || num_slots < 1 || max_ctas < 1) {
+    set_error("be_comm_create: invalid arguments (world <= %d, 16-byte slots)", COMM_MAX_RANKS);
+    return BE_EINVAL;
+  }
+  auto* c = new be_comm();
+  c->rank = rank;
+  c->world = world;
+  c->num_slots = num_slots;
+  c->max_ctas = max_ctas;
+  c->slot_bytes = slot_bytes;
+  c->flags_bytes = comm_flags_bytes(max_ctas);
+  cudaGetDevice(&c->device);
+  const size_t total = c->flags_bytes + (size_t)num_slots * slot_bytes;
+  cudaError_t e = cudaMalloc(&c->base, total);
+  if (e == cudaSuccess) e = cudaMemset(c->base, 0, c->flags_bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle((cudaIpcMemHandle_t*)handle_out, c->base);
+  if (e != cudaSuccess) {
+    set_error("be_comm_create: %s", cudaGetErrorString(e));
+    if (c->base) cudaFree(c->base);
+    delete c;
+    return BE_ECUDA;
+  }
+  c->peer[rank] = c->base;
+  *out = c;
+  return BE_OK;
+}
+
+extern "C" int be_comm_open(be_comm* c, const void* handles) {
+  if (!c || !handles) {
+    set_error("be_comm_open: invalid arguments");
+    return BE_EINVAL;
+  }
+  const auto* h = reinterpret_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int p = 0; p < c->world; ++p) {
+    if (p == c->rank || c->opened[p]) continue;
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h[p], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      set_error("be_comm_open: rank %d: %s", p, cudaGetErrorString(e));
+      return BE_ECUDA;
+    }
+    c->peer[p] = reinterpret_cast<char*>(ptr);
+    c->opened[p] = true;
+  }
+  return BE_OK;
+}
+
+extern "C" void* be_comm_slot(be_comm* c, int slot) {
+  if (!c || slot < 0 || slot >= c->num_slots) return nullptr;
+  return c->base + c->flags_bytes + (size_t)slot * c->slot_bytes;
+}
+
+extern "C" int be_comm_close_peers(be_comm* c) {
+  if (!c) return BE_OK;
+  cudaDeviceSynchronize();
+  for (int p = 0; p < c->world; ++p)
+    if (c->opened[p]) {
+      cudaIpcCloseMemHandle(c->peer[p]);
+      c->opened[p] = false;
+      c->peer[p] = nullptr;
+    }
+  return BE_OK;
+}
+
+extern "C" int be_comm_destroy(be_comm* c) {
+  if (!c) return BE_OK;
+  be_comm_close_peers(c);
+  if (c->base) cudaFree(c->base);
+  delete c;
+  return BE_OK;
+}
+
+extern "C" int be_comm_allreduce_rmsnorm(be_comm* c, int slot, void* residual, const void* norm_w,
+                                         void* out, int rows, int hidden, float eps, int dtype,
+                                         void* stream) {
+  if (!c || slot < 0 || slot >= c->num_slots || !out || rows < 0 || hidden < 1 ||
+      dtype < BE_F32 || dtype > BE_BF16 || (residual && !norm_w)) {
+    set_error("be_comm_allreduce_rmsnorm: invalid arguments");
+    return BE_EINVAL;
+  }
+  const int elt = dtype_size(dtype), V = 16 / elt;
+  if ((int64_t)rows * hidden * elt > c->slot_bytes || hidden % V || hidden > 256 * 8 * V ||
+      ((uintptr_t)out | (uintptr_t)residual | (uintptr_t)norm_w) % 16) {
+    set_error("be_comm_allreduce_rmsnorm: %d x %d does not fit a %lld-byte slot / 16-byte rows",
+              rows, hidden, (long long)c->slot_bytes);
+    return BE_EINVAL;
+  }
+  for (int p = 0; p < c->world; ++p)
+    if (!c->peer[p]) {
+      set_error("be_comm_allreduce_rmsnorm: rank %d not opened (be_comm_open)", p);
+      return BE_EINVAL;
+    }
+  if (rows == 0) return BE_OK;
+  CommArgs a = {};
+  for (int p = 0; p < c->world; ++p) {
+    a.flags_out[p] = reinterpret_cast<uint32_t*>(c->peer[p]);
+    a.slot[p] = c->peer[p] + c->flags_bytes + (size_t)slot * c->slot_bytes;
+  }
+  a.flags_in = reinterpret_cast<uint32_t*>(c->base);
+  a.counter = reinterpret_cast<uint32_t*>(c->base + (size_t)c->max_ctas * COMM_MAX_RANKS * 4);
+  a.rank = c->rank;
+  a.world = c->world;
+  a.max_ctas = c->max_ctas;
+  const int grid = std::min(rows, c->max_ctas);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case BE_BF16:
+      allreduce_rmsnorm_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+          a, (__nv_bfloat16*)residual, (const __nv_bfloat16*)norm_w, (__nv_bfloat16*)out, rows,
+          hidden, eps);
+      break;
+    case BE_F16:
+      allreduce_rmsnorm_kernel<__half><<<grid, 256, 0, st>>>(
+          a, (__half*)residual, (const __half*)norm_w, (__half*)out, rows, hidden, eps);
+      break;
+    default:
+      allreduce_rmsnorm_kernel<float><<<grid, 256, 0, st>>>(
+          a, (float*)residual, (const float*)norm_w, (float*)out, rows, hidden, eps);
+  }
+  BE_LAUNCH_CHECK();
+  return BE_OK;
+}

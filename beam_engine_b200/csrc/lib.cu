@@ -13,3 +13,4 @@
 #include "select_ops.cu"
 #include "gemm.cu"
 #include "gemm_lt.cu"
+#include "comm.cu"

@@ -91,7 +91,27 @@ class BeamLlama:
         self.use_lt = mode == "lt" and cuda_bf16           # cuBLASLt, per-shape tuned
         self._gemm_ws = None
         self._lt_ws = None
+        self.comm = None          # PeerAllReduce: fused all-reduce + add + RMSNorm under TP
+        self._slot_views = {}
         del weights
+
+    def enable_peer_allreduce(self, max_rows: int = 512):
+        """Route the row-parallel all-reduces of forwards with <= max_rows rows
+        through ``be_comm_allreduce_rmsnorm`` (peer memory, fused with the
+        residual add and the next RMSNorm) instead of NCCL + add_rmsnorm."""
+        from .parallel import PeerAllReduce
+        if self.tp is None or self.tp.size < 2:
+            return None
+        elt = torch.empty(0, dtype=self.dtype).element_size()
+        self.comm = PeerAllReduce(self.tp, max_rows * self.H * elt, self.device)
+        return self.comm
+
+    def _slots(self, n):
+        v = self._slot_views.get(n)
+        if v is None:
+            v = self._slot_views[n] = [self.comm.slot_view(i, (n, self.H), self.dtype)
+                                       for i in (0, 1)]
+        return v
 
     def _mm(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor):
         """out = a @ w.T (a [T, K], w [N, K] row-major, out [T, N])."""
@@ -147,10 +167,15 @@ class BeamLlama:
         pool = page_table.kv_cache
         P, ps = page_table.max_num_pages, page_table.page_size
         have_delta = False
+        # fused peer all-reduce: the O / down GEMMs write into this rank's slots and
+        # one kernel sums the ranks' slots, adds the residual and applies the next norm
+        fused = self.comm is not None and self.comm.fits(n, self.H, x.element_size())
+        slots = self._slots(n) if fused else None
         for i in range(self.L):
-            check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr() if have_delta else None,
-                                   self.n_in[i].data_ptr(), h.data_ptr(), n, self.H, self.eps,
-                                   self.dt, st), "add_rmsnorm")
+            if not fused or i == 0:
+                check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr() if have_delta else None,
+                                       self.n_in[i].data_ptr(), h.data_ptr(), n, self.H, self.eps,
+                                       self.dt, st), "add_rmsnorm")
             self._mm(h, self.w_qkv[i], qkv)
             check(L.be_rope_qkv_append(qkv.data_ptr(), self.qkv_width, n, self.Hq, self.Hkv, self.D,
                                        positions.data_ptr(), self.inv_freq.data_ptr(),
@@ -159,17 +184,31 @@ class BeamLlama:
             attention.run(i, qkv, att)
             if layer_hook is not None:
                 layer_hook(i)
-            self._mm(att, self.w_o[i], delta)
-            self._all_reduce(delta)
-            check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.n_post[i].data_ptr(),
-                                   h.data_ptr(), n, self.H, self.eps, self.dt, st), "add_rmsnorm")
+            if fused:
+                self._mm(att, self.w_o[i], slots[0])
+                check(L.be_comm_allreduce_rmsnorm(self.comm.ptr, 0, x.data_ptr(),
+                                                  self.n_post[i].data_ptr(), h.data_ptr(), n,
+                                                  self.H, self.eps, self.dt, st), "allreduce o")
+            else:
+                self._mm(att, self.w_o[i], delta)
+                self._all_reduce(delta)
+                check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.n_post[i].data_ptr(),
+                                       h.data_ptr(), n, self.H, self.eps, self.dt, st), "add_rmsnorm")
             self._mm(h, self.w_gu[i], gu)
             check(L.be_silu_mul(gu.data_ptr(), act.data_ptr(), n, self.F, self.dt, st), "silu_mul")
-            self._mm(act, self.w_down[i], delta)
-            self._all_reduce(delta)
+            if fused:
+                nxt = self.n_in[i + 1] if i + 1 < self.L else self.norm
+                self._mm(act, self.w_down[i], slots[1])
+                check(L.be_comm_allreduce_rmsnorm(self.comm.ptr, 1, x.data_ptr(), nxt.data_ptr(),
+                                                  h.data_ptr(), n, self.H, self.eps, self.dt, st),
+                      "allreduce down")
+            else:
+                self._mm(act, self.w_down[i], delta)
+                self._all_reduce(delta)
             have_delta = True
-        check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.norm.data_ptr(), h.data_ptr(),
-                               n, self.H, self.eps, self.dt, st), "final norm")
+        if not fused:
+            check(L.be_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.norm.data_ptr(),
+                                   h.data_ptr(), n, self.H, self.eps, self.dt, st), "final norm")
         hs = h if logits_rows is None else h.index_select(0, logits_rows)
         logits = torch.empty((hs.shape[0], self.lm_head.shape[0]), dtype=torch.float32, device=dev)
         return self._mm(hs, self.lm_head, logits)

@@ -52,6 +52,65 @@ class TensorParallel:
         return torch.cat(out.view((self.size,) + tuple(t.shape)).unbind(0), dim=dim)
 
 
+class PeerAllReduce:
+    """All-reduce of the row-parallel projections over peer memory, fused with
+    the residual add + RMSNorm after it (``be_comm_allreduce_rmsnorm``).
+
+    Each rank's GEMM writes its partial into its own slot of a buffer the other
+    ranks map through CUDA IPC (handles exchanged once with an all-gather);
+    the fused kernel signals / waits per CTA over peer flags and sums every
+    rank's slot with plain loads.  Two slots, alternated call by call.  Only
+    for one process per GPU on one node."""
+
+    def __init__(self, tp: TensorParallel, slot_bytes: int, device, max_ctas: int = 1024):
+        import ctypes as C
+        from ._lib import check, lib
+        self.tp = tp
+        self.device = torch.device(device)
+        self.slot_bytes = int(slot_bytes)
+        h = (C.c_char * 64)()
+        ptr = C.c_void_p()
+        check(lib().be_comm_create(tp.size, tp.rank, self.slot_bytes, 2, max_ctas, h,
+                                   C.byref(ptr)), "be_comm_create")
+        self.ptr = ptr
+        handles = [None] * tp.size
+        dist.all_gather_object(handles, bytes(h), group=tp.group)
+        check(lib().be_comm_open(ptr, b"".join(handles)), "be_comm_open")
+        dist.barrier(group=tp.group)          # every rank mapped before anyone signals
+        self.next_slot = 0
+
+    def slot_view(self, slot: int, shape, dtype) -> torch.Tensor:
+        """This rank's slot as a tensor (non-owning) to be used as a GEMM output."""
+        from ._lib import lib
+        addr = lib().be_comm_slot(self.ptr, slot)
+        n = 1
+        for d in shape:
+            n *= d
+        nbytes = n * torch.empty(0, dtype=dtype).element_size()
+        if nbytes > self.slot_bytes:
+            raise ValueError("partial larger than the all-reduce slot")
+        st = torch._C._construct_storage_from_data_pointer(addr, self.device, nbytes)
+        stride = [1] * len(shape)
+        for i in range(len(shape) - 2, -1, -1):
+            stride[i] = stride[i + 1] * shape[i + 1]
+        return torch.empty(0, dtype=dtype, device=self.device).set_(st, 0, tuple(shape),
+                                                                   tuple(stride))
+
+    def fits(self, rows: int, hidden: int, elt: int) -> bool:
+        return rows * hidden * elt <= self.slot_bytes
+
+    def close(self):
+        """Collective teardown: unmap the peers, wait for every rank, free."""
+        from ._lib import lib
+        if getattr(self, "ptr", None):
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.tp.group)
+            lib().be_comm_close_peers(self.ptr)
+            dist.barrier(group=self.tp.group)
+            lib().be_comm_destroy(self.ptr)
+            self.ptr = None
+
+
 def vocab_parallel_log_softmax_topk(logits: torch.Tensor, k: int, vocab_offset: int,
                                     tp: TensorParallel | None, temperature: float = 1.0):
     """``topk(log_softmax(logits_full / temperature), k)`` from a vocabulary

@@ -415,6 +415,41 @@ int be_diverse_select(int nseg, const int32_t* seg_ptr, int k, const double* par
                       int32_t* child_ptr, int32_t* child_tokens, double* child_scores,
                       int32_t* new_seg_ptr);
 
+/* ---- Tensor-parallel all-reduce over peer memory (one process per GPU) ----
+ * Replaces the NCCL all-reduce after the row-parallel projections
+ * (o_proj, down_proj) plus the residual add + RMSNorm that follow it
+ * (modeling_llama.py:68-173 decoder layer under tensor parallelism).  Each rank
+ * owns `num_slots` data slots in one allocation that the other ranks map
+ * through CUDA IPC; the GEMM writes its partial into this rank's slot, then
+ * be_comm_allreduce_rmsnorm sums every rank's slot (plain peer loads, no
+ * multicast) and applies the residual add and the norm.  Consecutive calls
+ * must alternate between two slots.  A rank that stops answering makes the
+ * others' barrier time out after 2 s (BE_EDEVICE_TIMEOUT in be_device_status). */
+typedef struct be_comm be_comm;
+#define BE_IPC_HANDLE_BYTES 64
+/* Allocate this rank's flags + slots; writes its IPC handle (BE_IPC_HANDLE_BYTES)
+ * to handle_out.  max_ctas bounds the CTAs of one call (rows beyond it are
+ * strided).  world <= 8.                                                     */
+int be_comm_create(int world, int rank, int64_t slot_bytes, int num_slots, int max_ctas,
+                   void* handle_out, be_comm** out);
+/* Map the other ranks' allocations: handles = world x BE_IPC_HANDLE_BYTES in rank
+ * order.  Every rank must have finished be_comm_open before any rank's first
+ * be_comm_allreduce_rmsnorm (a host barrier).                                */
+int be_comm_open(be_comm* comm, const void* handles);
+/* Device address of this rank's slot (where the GEMM writes its partial).    */
+void* be_comm_slot(be_comm* comm, int slot);
+/* Unmap the other ranks' allocations (after the last call on every rank).    */
+int be_comm_close_peers(be_comm* comm);
+/* Free this rank's allocation -- after every other rank closed its mapping of
+ * it (a host barrier after be_comm_close_peers on all ranks).                */
+int be_comm_destroy(be_comm* comm);
+/* sum = sum over ranks of slot[rows][hidden] (fp32, rank order: identical bits
+ * on every rank).  residual != NULL: residual += round(sum), out = norm_w *
+ * rmsnorm(residual) (be_add_rmsnorm's arithmetic); residual == NULL: out = sum. */
+int be_comm_allreduce_rmsnorm(be_comm* comm, int slot, void* residual, const void* norm_w,
+                              void* out, int rows, int hidden, float eps, int dtype,
+                              void* stream);
+
 /* One call for a cascade decode step's host inputs (beam.py:168-221 decode
  * inputs + BeamState.get_cascade_input beam_state.py:211-412 + the attention
  * plan): out[0..n) query tokens, [n..2n) RoPE positions, [2n..3n) append

@@ -1,7 +1,9 @@
 """Tensor parallelism on GPUs (NCCL, 2 ranks as child processes): the cfg1
 model sharded over two GPUs selects the same beams as the unsharded model on
 one GPU, in fp32 (eager step) and in bf16 (CUDA-graph step, NCCL all-reduces
-captured in the graph; scores within 2e-2).  Skipped on boxes with fewer than
+captured in the graph; scores within 2e-2), with the all-reduces on NCCL or
+on the fused peer-memory kernel (be_comm_allreduce_rmsnorm, which is also
+checked on its own against torch on every rank).  Skipped on boxes with fewer than
 two GPUs.  NVLS is switched off: a rank dying while bound to a multicast
 object has faulted peers on this kind of box."""
 import os
@@ -21,7 +23,47 @@ def _port():
         return s.getsockname()[1]
 
 
-def _run(dtype_name, tp_rank, world, port, q):
+def _check_peer_kernel(model, tp, dtype, rank):
+    """be_comm_allreduce_rmsnorm against torch: sum of every rank's partial,
+    residual add, RMSNorm; three calls over both slots."""
+    import torch.distributed as dist
+    from beam_engine_b200 import _lib
+    from beam_engine_b200._lib import check, lib
+    from beam_engine_b200.page_table import stream_ptr
+    comm, dev, H, n = model.comm, model.device, model.H, 7
+    eps = 1e-6
+    worst = 0.0
+    for call, slot in enumerate((0, 1, 0, 1)):
+        g = torch.Generator().manual_seed(100 * call + rank)
+        part = torch.randn(n, H, generator=g).to(dev, dtype)
+        gs = torch.Generator().manual_seed(1000 + call)        # replicated inputs
+        x = torch.randn(n, H, generator=gs).to(dev, dtype)
+        w = torch.randn(H, generator=gs).to(dev, dtype)
+        comm.slot_view(slot, (n, H), dtype).copy_(part)
+        parts = [torch.empty_like(part) for _ in range(tp.size)]
+        dist.all_gather(parts, part)
+        s = parts[0].float()
+        for p in parts[1:]:
+            s = s + p.float()
+        xr = (x.float() + s.to(dtype).float()).to(dtype)
+        hr = w.float() * (xr.float() * torch.rsqrt(xr.float().pow(2).mean(-1, keepdim=True) + eps)
+                          ).to(dtype).float()
+        h = torch.empty_like(x)
+        torch.cuda.synchronize(dev)
+        check(lib().be_comm_allreduce_rmsnorm(comm.ptr, slot, x.data_ptr(), w.data_ptr(),
+                                              h.data_ptr(), n, H, eps, model.dt, stream_ptr(dev)),
+              "allreduce")
+        torch.cuda.synchronize(dev)
+        status = __import__("ctypes").c_int(-1)
+        check(lib().be_device_status(__import__("ctypes").byref(status), None), "status")
+        assert status.value == 0, status.value
+        assert torch.equal(x, xr), (call, (x.float() - xr.float()).abs().max().item())
+        worst = max(worst, (h.float() - hr).abs().max().item())
+    assert worst < (1e-5 if dtype == torch.float32 else 5e-2), worst
+    dist.barrier()
+
+
+def _run(dtype_name, tp_rank, world, port, q, comm="nccl"):
     import torch.distributed as dist
     from beam_engine_b200.beam import BeamSearchGenerator
     from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy
@@ -42,6 +84,9 @@ def _run(dtype_name, tp_rank, world, port, q):
                    hidden_size=512)
         model = BeamLlama(cfg, None, dtype=dtype, device=torch.device("cuda", tp_rank), seed=5,
                           tp=tp)
+        if world > 1 and comm == "peer":
+            assert model.enable_peer_allreduce() is not None
+            _check_peer_kernel(model, tp, dtype, tp_rank)
         g = torch.Generator().manual_seed(2)
         prompts = [torch.randint(0, 1024, (40,), generator=g).tolist() for _ in range(2)]
         gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=16,
@@ -49,6 +94,8 @@ def _run(dtype_name, tp_rank, world, port, q):
         out = gen.generate_ids(prompts, 4, max_new_tokens=12, num_return_sequences=4)
         q.put((tp_rank, [[(list(s), float(x)) for s, x in o] for o in out], gen.use_graph))
         if world > 1:
+            if model.comm is not None:
+                model.comm.close()
             dist.barrier()
             dist.destroy_process_group()
     except Exception:
@@ -57,8 +104,9 @@ def _run(dtype_name, tp_rank, world, port, q):
         raise
 
 
+@pytest.mark.parametrize("comm", ["nccl", "peer"])
 @pytest.mark.parametrize("dtype_name,tol", [("float32", 1e-4), ("bfloat16", 2e-2)])
-def test_tp2_matches_single_gpu(dtype_name, tol):
+def test_tp2_matches_single_gpu(dtype_name, tol, comm):
     if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -70,7 +118,7 @@ def test_tp2_matches_single_gpu(dtype_name, tol):
     single.join(timeout=60)
     assert not isinstance(ref[1], str), ref[1]
     port = _port()
-    procs = [ctx.Process(target=_run, args=(dtype_name, r, WORLD, port, q), daemon=True)
+    procs = [ctx.Process(target=_run, args=(dtype_name, r, WORLD, port, q, comm), daemon=True)
              for r in range(WORLD)]
     for p in procs:
         p.start()
