@@ -13,7 +13,7 @@
 //      (ld.acquire.sys, bounded by %globaltimer: on expiry BE_EDEVICE_TIMEOUT is
 //      recorded and the CTA returns);
 //   3. reads the row from every rank's slot (plain 16-byte loads over NVLink,
-//      L2-only, in rank order so every rank computes identical bits), sums in
+//      volatile, in rank order so every rank computes identical bits), sums in
 //      fp32, rounds to the storage type, adds it to the residual, and writes
 //      the normalised row -- the add_rmsnorm kernel's arithmetic.
 // Consecutive calls alternate between two slots: a rank can only write a slot
@@ -82,9 +82,14 @@ __device__ bool comm_barrier(const CommArgs& a, int cta) {
   return ok != 0;
 }
 
+// 16-byte load of a rank's slot: volatile (system-coherent, no stale L1 line
+// from the call two calls back, when this slot last held other data).
 template <typename T>
-__device__ __forceinline__ void load16_cg(const T* p, float* out) {
-  const int4 raw = __ldcg(reinterpret_cast<const int4*>(p));
+__device__ __forceinline__ void load16_peer(const T* p, float* out) {
+  int4 raw;
+  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
+               : "l"(p));
   if constexpr (sizeof(T) == 2) {
     const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
@@ -143,10 +148,10 @@ __global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(CommArgs a, T* _
     const int64_t base = (int64_t)row * H;
     for (int c = threadIdx.x * V; c < H; c += blockDim.x * V, ++nv) {
       float s[V];
-      load16_cg(reinterpret_cast<const T*>(a.slot[0]) + base + c, s);
+      load16_peer(reinterpret_cast<const T*>(a.slot[0]) + base + c, s);
       for (int p = 1; p < a.world; ++p) {
         float t[V];
-        load16_cg(reinterpret_cast<const T*>(a.slot[p]) + base + c, t);
+        load16_peer(reinterpret_cast<const T*>(a.slot[p]) + base + c, t);
 #pragma unroll
         for (int i = 0; i < V; ++i) s[i] += t[i];
       }
