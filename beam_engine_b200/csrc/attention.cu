@@ -41,7 +41,7 @@ struct AttnParams {
   float* mid_o;
   float* mid_lse;
   int n_work, n_wide;
-  int debug;             // profiling switches (BE_ATTN_DEBUG), 0 in normal runs
+  int debug;             // BE_ATTN_DEBUG switches; bit 3 = BE_ATTN_WIDE_RUNS
   const int32_t* hdr;    // plan header on the device (fixed-grid launches), else null
 };
 
@@ -545,7 +545,8 @@ __global__ void __launch_bounds__(128) merge_kernel(const int32_t* __restrict__ 
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = lane + 32 * h;
-        v[u][h] = (k0 + u < np && c < nv)
+        // parts of weight 0 (LSE -inf: empty, or folded into another part) are not read
+        v[u][h] = (k0 + u < np && c < nv && wgt[u] != 0.f)
                       ? __ldg(reinterpret_cast<const float4*>(mid_o + (row[u] * hq + head) * D) + c)
                       : make_float4(0.f, 0.f, 0.f, 0.f);
       }

@@ -39,6 +39,9 @@ constexpr int WD_ONES = 128 * 128;              // all-ones A operand: 128 rows 
 constexpr int WD_OUT = WD_ROWS * 128 * 4;       // output staging: 64 rows x 128 dims (fp32)
 constexpr int WD_WMAX = 4 * WD_ROWS;            // per-warp row maxima (softmax scratch)
 constexpr int WD_MSLOTS = 4;                    // final row maxima, one slot per task in flight
+// run accumulation (consecutive chunks of one group in one CTA): running row max
+// and sum [64] each, per-task rescale factors a / b [2 task parities][64] each
+constexpr int WD_RUN_FLOATS = 2 * WD_ROWS + 4 * WD_ROWS;
 #ifndef WD_SUSPEND_NS
 #define WD_SUSPEND_NS 0
 #endif
@@ -50,7 +53,8 @@ constexpr uint32_t WD_S_COL = 0, WD_OL_COL = 128;
 static_assert(WD_TOK == 128, "one token per TMEM lane");
 
 constexpr size_t wd_smem_bytes() {
-  return 1024 + 2 * WD_STAGE + WD_ONES + WD_OUT + (WD_WMAX + WD_MSLOTS * WD_ROWS + WD_ROWS) * 4 +
+  return 1024 + 2 * WD_STAGE + WD_ONES + WD_OUT +
+         (WD_WMAX + WD_MSLOTS * WD_ROWS + WD_ROWS + WD_RUN_FLOATS) * 4 +
          16 * 8 + 16;
 }
 
@@ -139,7 +143,11 @@ __global__ void __launch_bounds__(320, 1) attn_wide_kernel(const __grid_constant
   float* sWmax = reinterpret_cast<float*>(sOut + WD_OUT);              // [4 warps][64 rows]
   float* sM = sWmax + WD_WMAX;                                         // [4 slots][64 rows]
   float* sInv = sM + WD_MSLOTS * WD_ROWS;                              // [64] 1 / l per row
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sInv + WD_ROWS);
+  float* sRunM = sInv + WD_ROWS;                                       // [64] running max
+  float* sRunL = sRunM + WD_ROWS;                                      // [64] running sum
+  float* sRunA = sRunL + WD_ROWS;                                      // [2][64] old-run scale
+  float* sRunB = sRunA + 2 * WD_ROWS;                                  // [2][64] chunk scale
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRunB + 2 * WD_ROWS);
   uint64_t* kq_full = bars + 0;      // [2] K pages + Q tile landed (stage)
   uint64_t* v_full = bars + 2;       // [2] V pages landed (stage)
   uint64_t* s_full = bars + 4;       // [2] S^T in TMEM
@@ -479,13 +487,39 @@ __global__ void __launch_bounds__(320, 1) attn_wide_kernel(const __grid_constant
     }
   } else {
     // ---------------- epilogue: thread d owns head dim d ----------------
+    // Consecutive tasks of this CTA that are consecutive chunks of one group
+    // (same KV head, queries and KV list, adjoining token ranges, both writing
+    // partial rows) form a run when BE_ATTN_WIDE_RUNS is set: their O^T rows
+    // accumulate in the fp32 staging rows with the exact online-softmax rescale
+    // (running max M, sum L; old rows x 2^(M_old - M), chunk rows x 2^(m_c - M)),
+    // and only the run's last task writes -- into the partial rows of the run's
+    // first item; the other items' rows get LSE = -inf, which the merge skips.
+    // A one-task run takes the per-task path below unchanged.
     const int e = warp - 4;
     const int d = e * 32 + lane;
+    const bool runs_on = (p.debug & 8) != 0;
+    int run_item = -1;
+    auto same_run = [&](const Work& a, int ka, const Work& b, int kb) {
+      return runs_on && ka == kb && a.part_base >= 0 && b.part_base >= 0 && a.q_off == b.q_off &&
+             a.q_len == b.q_len && a.kv_off == b.kv_off && a.kv_end == b.kv_begin;
+    };
     for (int it = 0; it < my_tasks; ++it) {
       const int s = it & 1;
       const WideTask tk = wide_task(t_begin + it, n_items);
       const Work w = p.work[tk.item];
       const int rows = w.q_len * g;
+      bool first = true, last = true;
+      if (runs_on) {
+        if (it > 0) {
+          const WideTask tp = wide_task(t_begin + it - 1, n_items);
+          first = !same_run(p.work[tp.item], tp.kvh, w, tk.kvh);
+        }
+        if (it + 1 < my_tasks) {
+          const WideTask tn = wide_task(t_begin + it + 1, n_items);
+          last = !same_run(w, tk.kvh, p.work[tn.item], tn.kvh);
+        }
+      }
+      if (first) run_item = tk.item;
       const bool ok = !*abort_flag && warp_wait(&o_full[s], (it >> 1) & 1);
       if (!ok) {
         *abort_flag = 1;
@@ -515,6 +549,63 @@ __global__ void __launch_bounds__(320, 1) attn_wide_kernel(const __grid_constant
       tc_fence_before();
       mbar_arrive(&ol_empty[s]);   // TMEM no longer read: the next O / L may land
       if (d == 0) wstamp(p, it, 8);
+      if (!(first && last)) {
+        // ---- run accumulation (fp32 staging rows hold the run's unnormalised O) ----
+        float* acc = reinterpret_cast<float*>(sOut);
+        float* ra = sRunA + s * WD_ROWS;
+        float* rb = sRunB + s * WD_ROWS;
+        // a finished run's bulk copies must have read the staging rows
+        if (first && d == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        if (d < WD_ROWS) {
+          const float m_c = d < rows ? sM[(it & (WD_MSLOTS - 1)) * WD_ROWS + d] : -INFINITY;
+          const float mo = first ? -INFINITY : sRunM[d];
+          const float lo = first ? 0.f : sRunL[d];
+          const float mn = fmaxf(mo, m_c);
+          const float a = mo == -INFINITY ? 0.f : ex2(mo - mn);
+          const float b = m_c == -INFINITY ? 0.f : ex2(m_c - mn);
+          sRunM[d] = mn;
+          sRunL[d] = lo * a + (d < rows ? l_d : 0.f) * b;
+          ra[d] = a;
+          rb[d] = b;
+        }
+        named_sync(2, 128);
+#pragma unroll
+        for (int j = 0; j < WD_ROWS; ++j) {   // unrolled: uo[] stays in registers
+          float v = __uint_as_float(uo[j]) * rb[j];
+          if (!first) v += acc[j * D + d] * ra[j];
+          acc[j * D + d] = v;
+        }
+        if (last) {
+          const Work w0 = p.work[run_item];
+          if (d < rows) {
+            const int i = d / g, head = tk.kvh * g + d % g;
+            const float lr = sRunL[d];
+            p.mid_lse[(int64_t)(w0.part_base + i) * p.hq + head] =
+                lr > 0.f ? (sRunM[d] + log2f(lr)) * kLn2 : -INFINITY;
+            for (int k = run_item + 1; k <= tk.item; ++k)   // the run's other partial rows
+              p.mid_lse[(int64_t)(p.work[k].part_base + i) * p.hq + head] = -INFINITY;
+            sInv[d] = lr > 0.f ? 1.f / lr : 0.f;
+          }
+          named_sync(2, 128);
+#pragma unroll 8
+          for (int j = 0; j < WD_ROWS; ++j) acc[j * D + d] *= sInv[j];
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          named_sync(2, 128);
+          if (d == 0) {
+            const uint32_t bytes = (uint32_t)(g * D * 4);
+            for (int i = 0; i < w.q_len; ++i) {
+              char* dst = reinterpret_cast<char*>(
+                  p.mid_o + ((int64_t)(w0.part_base + i) * p.hq + (int64_t)tk.kvh * g) * D);
+              asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                           "r"(smem_u32(sOut + (size_t)i * bytes)), "r"(bytes)
+                           : "memory");
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        }
+        if (d == 0) wstamp(p, it, 7);
+        continue;
+      }
       // row d < rows: its LSE, and 1 / l for the rows pass
       if (d < rows) {
         const int i = d / g, head = tk.kvh * g + d % g;

@@ -153,6 +153,10 @@ static void fill_params(AttnParams& p, const void* q, int64_t q_row_stride,
   p.mid_lse = mid_lse;
   const char* e = getenv("BE_ATTN_DEBUG");
   p.debug = e ? atoi(e) : 0;
+  // BE_ATTN_WIDE_RUNS=1: the persistent wide kernel accumulates consecutive
+  // chunks of one group before writing (bit 3 of the switches word)
+  const char* r = getenv("BE_ATTN_WIDE_RUNS");
+  if (r && r[0] == '1') p.debug |= 8;
 }
 
 template <typename... A>

@@ -142,11 +142,13 @@ __global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(CommArgs a, T* _
   if (!comm_barrier(a, cta)) return;
   __shared__ float red[32];
   for (int row = cta; row < rows; row += gridDim.x) {
-    float cache[8][V];
+    float cache[8][V];   // fully unrolled below: stays in registers
     float ss = 0.f;
-    int nv = 0;
     const int64_t base = (int64_t)row * H;
-    for (int c = threadIdx.x * V; c < H; c += blockDim.x * V, ++nv) {
+#pragma unroll
+    for (int nv = 0; nv < 8; ++nv) {
+      const int c = (threadIdx.x + nv * blockDim.x) * V;
+      if (c >= H) break;
       float s[V];
       load16_peer(reinterpret_cast<const T*>(a.slot[0]) + base + c, s);
       for (int p = 1; p < a.world; ++p) {
@@ -183,8 +185,10 @@ __global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(CommArgs a, T* _
     }
     __syncthreads();
     const float inv = rsqrtf(red[0] / (float)H + eps);
-    nv = 0;
-    for (int c = threadIdx.x * V; c < H; c += blockDim.x * V, ++nv) {
+#pragma unroll
+    for (int nv = 0; nv < 8; ++nv) {
+      const int c = (threadIdx.x + nv * blockDim.x) * V;
+      if (c >= H) break;
       float wv[V], r[V];
       load16(w + c, wv);
 #pragma unroll
