@@ -69,14 +69,20 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
       n_parts += it.w.q_len;
     }
   }
-  std::vector<std::vector<int32_t>> parts(num_queries);
+  // partial rows per query as CSR (items in plan order, as a per-query list would hold them)
   std::vector<char> direct_q(num_queries, 0);
+  std::vector<int32_t> pcount(num_queries + 1, 0);
   for (auto& it : items)
     for (int i = 0; i < it.w.q_len; ++i) {
       const int q = qlist[it.w.q_off + i];
       if (it.w.part_base < 0) direct_q[q] = 1;
-      else parts[q].push_back(it.w.part_base + i);
+      else pcount[q + 1]++;
     }
+  for (int q = 0; q < num_queries; ++q) pcount[q + 1] += pcount[q];
+  std::vector<int32_t> pfill(pcount.begin(), pcount.end() - 1), pflat(pcount[num_queries]);
+  for (auto& it : items)
+    for (int i = 0; i < it.w.q_len; ++i)
+      if (it.w.part_base >= 0) pflat[pfill[qlist[it.w.q_off + i]]++] = it.w.part_base + i;
   std::stable_sort(items.begin(), items.end(), [](const W& a, const W& b) {
     if (a.wide != b.wide) return a.wide;
     return a.cost > b.cost;
@@ -85,7 +91,7 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
   for (int q = 0; q < num_queries; ++q) {
     if (direct_q[q]) continue;
     mq.push_back(q);
-    mparts.insert(mparts.end(), parts[q].begin(), parts[q].end());
+    mparts.insert(mparts.end(), pflat.begin() + pcount[q], pflat.begin() + pcount[q + 1]);
     mptr.push_back((int32_t)mparts.size());
   }
   be_attn_plan_info in{};
