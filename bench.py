@@ -147,6 +147,8 @@ def run_b200(args, rank, world, local_rank):
     # replicas: independent models and prompts per rank
     seed = 1234 if tp_mode else 1234 + rank
     model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=dev, seed=seed, tp=tp)
+    if tp_mode and args.tp_comm == "peer":
+        model.enable_peer_allreduce()   # fused peer-memory all-reduce + add + RMSNorm
     gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=PAGE,
                               max_num_pages=args.pages, kernel_type=KERNEL)
     g = torch.Generator().manual_seed(0 if tp_mode else rank)
@@ -274,6 +276,7 @@ def run_b200(args, rank, world, local_rank):
         "config": {"workload": WORKLOAD,
                    "model": f"{MODEL_NAME} shape (random init)", "global_batch": PROMPTS * BEAM * replicas,
                    "seq_len": PROMPT_LEN,
+                   "tp_comm": args.tp_comm if tp_mode else None,
                    "parallelism": f"tp{world}" if tp_mode else (f"replicas x{world}" if world > 1
                                                                 else "tp1"),
                    "l2": f"no flush needed: each step reads {step_bytes / 1e9:.1f} GB of weights "
@@ -550,6 +553,8 @@ def main():
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
                     help="N > 1: tensor parallel over the N GPUs (default) or N independent replicas")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp-comm", default="nccl", choices=["nccl", "peer"],
+                    help="tensor-parallel all-reduce: NCCL, or the fused peer-memory kernel")
     ap.add_argument("--op", default=None, choices=["cfg2"],
                     help="op-level microbench instead of the decode benchmark")
     ap.add_argument("--pool-pages", type=int, default=65536)
