@@ -102,7 +102,7 @@ __device__ __forceinline__ float ex2(float x) {  // hardware base-2 exponential
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(160) attn_umma_kernel(const __grid_constant__ CUtensorMap tmap,
+__global__ void __launch_bounds__(160, 2) attn_umma_kernel(const __grid_constant__ CUtensorMap tmap,
                                                         AttnParams p) {
   constexpr int NH = D / 64;
   extern __shared__ char smem_raw[];

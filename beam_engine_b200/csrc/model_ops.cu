@@ -55,10 +55,13 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(T* __restrict__ residu
   const T* dl = delta ? delta + (int64_t)row * H : nullptr;
   T* o = out + (int64_t)row * H;
   float ss = 0.f;
-  // H <= 256 threads * 8 vectors * V elements (16384 for 2-byte types)
+  // H <= 256 threads * 8 vectors * V elements (16384 for 2-byte types); the
+  // loops are unrolled so the row cache stays in registers
   float cache[8][V];
-  int nv = 0;
-  for (int c = threadIdx.x * V; c < H; c += blockDim.x * V, ++nv) {
+#pragma unroll
+  for (int nv = 0; nv < 8; ++nv) {
+    const int c = (threadIdx.x + nv * blockDim.x) * V;
+    if (c >= H) break;
     float a[V];
     load_vec<T, V>(x + c, a);
     if (dl) {
@@ -87,8 +90,10 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(T* __restrict__ residu
   }
   __syncthreads();
   const float inv = rsqrtf(red[0] / (float)H + eps);
-  nv = 0;
-  for (int c = threadIdx.x * V; c < H; c += blockDim.x * V, ++nv) {
+#pragma unroll
+  for (int nv = 0; nv < 8; ++nv) {
+    const int c = (threadIdx.x + nv * blockDim.x) * V;
+    if (c >= H) break;
     float wv[V], r[V];
     load_vec<T, V>(w + c, wv);
 #pragma unroll
