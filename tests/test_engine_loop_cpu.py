@@ -1,0 +1,124 @@
+"""The engine's host loop (``BeamSearchGenerator.generate_ids``) on CPU with the
+model replaced by a deterministic scorer: root expansion, per-step selection of
+several prompts at once, trie updates, copy-on-write bookkeeping and the final
+ranking must equal the oracle's restatement of the reference loop
+(beam.py:48-352) run prompt by prompt on the same scorer.  The device step is
+covered by the -m gpu tests; this pins everything around it."""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from beam_engine_b200.beam import BeamSearchGenerator
+from beam_engine_b200.beam_strategy import DiverseBeamSearchStrategy, VanillaBeamSearchStrategy
+from beam_engine_b200.page_table import PageTable
+from oracle.beam_state import OracleBeamState, diverse_select, vanilla_select
+from oracle.paging import OraclePageTable
+
+VOCAB = 50
+
+
+def fake_logprobs(seq):
+    """Log-probabilities over VOCAB from the sequence alone (float32, like the
+    device's scores), with frequent exact ties."""
+    h = hashlib.sha256(np.asarray(seq, np.int64).tobytes()).digest()
+    rng = np.random.default_rng(int.from_bytes(h[:8], "little"))
+    x = np.round(rng.normal(0, 2, VOCAB) * 2) / 2
+    x = x - x.max()
+    lp = x - np.log(np.exp(x).sum())
+    return lp.astype(np.float32)
+
+
+def topk(lp, k):
+    """Descending, ties by smaller token id (the device top-k's order)."""
+    order = np.lexsort((np.arange(len(lp)), -lp.astype(np.float64)))[:k]
+    return lp[order].astype(np.float64), order.astype(np.int32)
+
+
+class FakeGenerator(BeamSearchGenerator):
+    """BeamSearchGenerator with the device step replaced by fake_logprobs."""
+
+    def __init__(self, strategy, page_size, pages):
+        self.strategy = strategy
+        self.page_table = PageTable(layer_num=1, page_size=page_size, max_num_pages=pages,
+                                    head_num=1, head_dim=8, device="cpu",
+                                    store_dtype=torch.bfloat16)
+        self.model = type("M", (), {"vocab": VOCAB})()
+        self.use_graph = True          # copies are deferred to the (fake) step graph
+        self.use_graph_tree = False
+        self._pending_fork = None
+        self.forks = []
+        self.steps = 0
+
+    def prefill(self, state, prompts):
+        for p in prompts:
+            state.add_root_sequence(p)
+        return np.stack([fake_logprobs(p) for p in prompts])
+
+    def _topk(self, logits, k, temperature):
+        out = [topk(row, k) for row in logits]
+        return np.stack([v for v, _ in out]), np.stack([i for _, i in out])
+
+    def decode_topk(self, state, k, temperature):
+        self._take_fork_cpu()
+        self.steps += 1
+        return self._topk(np.stack([fake_logprobs(state.sequence(int(l))) for l in state.leaves]),
+                          k, temperature)
+
+    def _take_fork_cpu(self):
+        if self._pending_fork is not None:
+            self.forks.append(tuple(np.asarray(a).tolist() for a in self._pending_fork))
+            self._pending_fork = None
+
+    def _fork_now(self, copies):
+        self.forks.append(tuple(np.asarray(a).tolist() for a in copies))
+
+
+def oracle_generate(prompt, W, new_tokens, ps, strategy):
+    """The reference loop on one prompt (oracle state, same scorer)."""
+    st = OracleBeamState(W, OraclePageTable(1, ps, 4096, 1, 1, storage=False))
+    st.add_root_sequence(prompt)
+    k0 = min(2 * W, VOCAB)
+    v, i = topk(fake_logprobs(prompt), k0)
+    kw = min(W, k0)
+    st.add_filtered_results([[(int(i[j]), float(v[j])) for j in range(kw)]])
+    for _ in range(new_tokens - 1):
+        if not st.cand_leaf:
+            break
+        k = min(2 * W, VOCAB) if W != 1 else 1
+        kids = [topk(fake_logprobs(st.sequence(c)), k) for c in range(len(st.cand_leaf))]
+        toks = [ki.tolist() for _, ki in kids]
+        lps = [kv.tolist() for kv, _ in kids]
+        if isinstance(strategy, DiverseBeamSearchStrategy):
+            seqs = [st.sequence(c) for c in range(len(st.cand_leaf))]
+            res = diverse_select(st.cand_score, seqs, toks, lps, W, strategy.num_groups,
+                                 strategy.diversity_penalty, strategy.diversity_type,
+                                 strategy.length_penalty)
+        else:
+            res = vanilla_select(st.cand_score, toks, lps, W)
+        st.add_filtered_results(res)
+    return st.final_sequences(W, strategy.length_penalty)
+
+
+@pytest.mark.parametrize("strategy", [
+    VanillaBeamSearchStrategy(length_penalty=1.0),
+    DiverseBeamSearchStrategy(num_groups=2, diversity_penalty=0.5, diversity_type="hamming"),
+    DiverseBeamSearchStrategy(num_groups=3, diversity_penalty=0.7, diversity_type="cumulative",
+                              length_penalty=0.5),
+], ids=["vanilla", "diverse_hamming", "diverse_cumulative"])
+@pytest.mark.parametrize("W,ps", [(4, 16), (6, 4)])
+def test_generate_ids_host_loop_matches_oracle(strategy, W, ps):
+    rng = np.random.default_rng(W * 100 + ps)
+    prompts = [rng.integers(0, VOCAB, n).tolist() for n in (9, 23, 16)]
+    new_tokens = 12
+    gen = FakeGenerator(strategy, ps, 2048)
+    out = gen.generate_ids(prompts, W, max_new_tokens=new_tokens, num_return_sequences=W)
+    gen._take_fork_cpu()
+    assert gen.steps == new_tokens - 1
+    for p, got in zip(prompts, out):
+        want = oracle_generate(p, W, new_tokens, ps, strategy)
+        assert [s for s, _ in got] == [s for s, _ in want]
+        np.testing.assert_allclose([x for _, x in got], [x for _, x in want], rtol=0, atol=0)
+    # every copy-on-write copy the updates asked for reached the (fake) device step
+    assert all(len(a) == len(b) == len(c) for a, b, c in gen.forks)
