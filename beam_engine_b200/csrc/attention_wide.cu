@@ -662,6 +662,9 @@ __global__ void __launch_bounds__(320, 1) attn_wide_kernel(const __grid_constant
       // row info buffer s is rewritten two tasks later, after the next task's
       // named barrier, which every thread reaches only after this loop
     }
+    // the last bulk copies read the staging rows: done before the CTA's shared
+    // memory can be handed to another CTA
+    if (d == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
