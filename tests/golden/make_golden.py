@@ -2,7 +2,7 @@
 
 Run in the build container (the reference tree is only present there):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py      # BEAM_REF_SRC=<reference>/src if elsewhere
 
 Writes ``tests/golden/*.json`` / ``*.npz``.  What each fixture pins:
 

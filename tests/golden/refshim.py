@@ -24,7 +24,12 @@ import types
 import numpy as np
 import torch
 
-REF_SRC = os.environ.get("BEAM_REF_SRC", "/root/reference/src")
+# the reference checkout's ``src`` directory (BEAM_REF_SRC); a sibling
+# ``reference`` checkout of this repository's parent directory by default
+REF_SRC = os.environ.get(
+    "BEAM_REF_SRC",
+    os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__))))), "reference", "src"))
 
 
 def _np(t):
