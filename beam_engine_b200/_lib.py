@@ -105,6 +105,9 @@ _SIGS = {
     "be_comm_destroy": (C.c_int, [vp]),
     "be_comm_allreduce_rmsnorm": (C.c_int, [vp, C.c_int, vp, vp, vp, C.c_int, C.c_int, C.c_float,
                                             C.c_int, vp]),
+    "be_tree_plan_pages": (C.c_int, [C.c_int, vp, C.c_int, vp, vp, vp, vp, vp, i64, C.c_int,
+                                      C.c_int, C.c_int, C.c_int, C.c_int, vp, i64,
+                                      C.POINTER(AttnPlanInfo)]),
     "be_leaf_sequences": (i64, [vp, C.c_int, vp, vp, vp, i64]),
     "be_diverse_select": (C.c_int, [C.c_int, vp, C.c_int, vp, vp,
                                     vp, vp, vp, C.c_int, C.c_int, C.c_double,

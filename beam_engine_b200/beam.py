@@ -82,6 +82,19 @@ class PlannedAttention:
         p.place(m.Hq, m.D)
         self.kv_list = None
 
+    def plan_prebuilt(self, info, buf):
+        """Place a plan built elsewhere (a page-list tree plan)."""
+        p = self.plan
+        p.info = info
+        host = torch.from_numpy(np.ascontiguousarray(buf[:info.total_ints]))
+        if p.copied is not None:          # previous H2D still reading the staging buffer
+            p.copied.synchronize()
+        if p.host.numel() < host.numel():
+            p.host = torch.empty(host.numel(), dtype=torch.int32).pin_memory()
+        p.host[:host.numel()].copy_(host)
+        p.place(self.m.Hq, self.m.D)
+        self.kv_list = None
+
     def plan_tree(self, vnodes, batch_size, kv_entries_dev):
         from .fasttree import build_tree_plan
         info, buf = build_tree_plan(vnodes, batch_size, self.pt.page_size, self.m.Hq, self.m.Hkv)
@@ -313,6 +326,11 @@ class BeamSearchGenerator:
         self.graph_regrowth = []      # why a step graph was recorded again
         self._graph_warm = False
         self._pending_fork = None     # copies of the last selection, run by the next graph step
+        # tree steps as page-list plans on the tensor-core kernels (BE_TREE_PAGES=1; the slot-list
+        # plan of the general kernel otherwise, or when a tree is not page aligned)
+        self.tree_pages = (os.environ.get("BE_TREE_PAGES", "0") == "1" and page_size == 16
+                           and self.page_table.store_dtype != torch.float32)
+        self.step_graph_tpages = None
         self.h2d_bytes = 0            # host -> device bytes copied by the engine (inputs, plans)
 
     # ------------------------------------------------------------------
@@ -398,6 +416,19 @@ class BeamSearchGenerator:
                                     logits_rows=d_rows.long())
         return logits
 
+    def _tree_page_plan(self, v, r2t, n):
+        """(info, plan) of the vnodes as a page-list plan, or None."""
+        from .fasttree import build_tree_page_plan
+        if not self.tree_pages:
+            return None
+        m = self.model
+        slots = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)]).astype(np.int32)
+        got = build_tree_page_plan(v, slots, n, self.page_table.page_size, m.Hq, m.Hkv,
+                                   self.attn.plan.num_sms)
+        if got is None or got[0].max_wide_tokens > UMMA_MAX_TOKENS:
+            return None
+        return got
+
     def _tree_vnodes(self, state: BeamState, n: int):
         from .fasttree import plan_vnodes
         par, seql, kids, rptr, rl, r2t = state.tree_arrays(per_node=True, compress=True)
@@ -436,6 +467,9 @@ class BeamSearchGenerator:
         else:
             v, r2t = self._tree_vnodes(state, n)
             info, plan = build_tree_plan(v, n, self.page_table.page_size, m.Hq, m.Hkv)
+        pp = self._tree_page_plan(v, r2t, n)
+        if pp is not None:
+            return self._tree_pages_graph_step(state, n, k, temperature, q, pos, wp, wpos, *pp)
         slots = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)])
         sg = self.step_graph_tree
         if not (sg is not None and sg.fits(n, k, temperature, info, len(slots))):
@@ -454,6 +488,23 @@ class BeamSearchGenerator:
         h[sg.slots_off:sg.slots_off + len(slots)] = slots
         return sg.step_filled(sg.slots_off + len(slots))
 
+    def _tree_pages_graph_step(self, state, n, k, temperature, q, pos, wp, wpos, info, plan):
+        """A tree step whose plan is a page list: replayed from a page-list step graph."""
+        sg = self.step_graph_tpages
+        if not (sg is not None and sg.fits(n, k, temperature, info)):
+            caps = dict(work=3 * info.n_work + 2 * n + 64, wide=2 * info.n_work_wide + 16,
+                        merge=max(n, 1), parts=3 * info.n_parts + 4 * n + 256,
+                        ints=3 * info.total_ints + 64 * n + 4096)
+            if sg is not None and sg.n == n and sg.k == k and sg.temp == temperature:
+                for key in caps:
+                    caps[key] = max(caps[key], sg.caps[key] * 3 // 2)
+            self.step_graph_tpages = sg = StepGraph(self, n, k, temperature, caps, kind="cascade")
+        h = sg.host_buf.numpy()
+        h[0:n], h[n:2 * n], h[2 * n:3 * n], h[3 * n:4 * n] = q, pos, wp, wpos
+        self._take_fork(sg)
+        h[sg.plan_off:sg.plan_off + info.total_ints] = plan[:info.total_ints]
+        return sg.step_filled(sg.plan_off + info.total_ints)
+
     def decode_step(self, state: BeamState, kind: Optional[str] = None):
         """One beam step's forward: returns logits [beams, vocab]."""
         if kind is None:
@@ -466,6 +517,10 @@ class BeamSearchGenerator:
         else:
             v, r2t = self._tree_vnodes(state, len(q))
             flat = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)])
+            pp = self._tree_page_plan(v, r2t, len(q))
+            if pp is not None:              # page-list tree plan on the tensor-core kernels
+                self.attn.plan_prebuilt(*pp)
+                kind = "cascade"
         arrays = [q, pos, wp, wpos]
         if kind != "cascade":
             arrays.append(_i32(flat))

@@ -151,6 +151,81 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
   return BE_OK;
 }
 
+// Queries gq[q_at .. q_at + qlen) attending one contiguous KV range (page list
+// from kv_off); causal groups hold consecutive queries in order.
+struct Grp {
+  bool causal;
+  int q_at, qlen, kv_off, kv_len;
+};
+
+// Groups -> work items: tiles of <= 64 (wide) or <= 16 (narrow) rows, the KV
+// split for ~4 CTAs per SM (decode wide chunks capped at the resident tensor-
+// core tile), then emit_plan.
+int plan_groups(const std::vector<Grp>& groups, const std::vector<int32_t>& gq,
+                const std::vector<int32_t>& kvlist, int num_queries, int page_size, int g, int num_kv_heads, int split_tokens,
+                int num_sms, int32_t* plan, int64_t plan_capacity, be_attn_plan_info* info) {
+  int64_t total_cost = 0;
+  for (const auto& gr : groups)
+    total_cost += (int64_t)gr.kv_len *
+                  ((gr.qlen + tile_queries(gr.qlen, g) - 1) / std::max(1, tile_queries(gr.qlen, g)));
+  // KV split: aim for ~4 CTAs per SM in total (CTAs = items x kv heads), but keep
+  // chunks long enough that the fp32 partial rows stay small next to the KV bytes
+  // they summarise (>= 8 tokens per row of the tile).
+  const int sms = num_sms > 0 ? num_sms : 148;
+  const int64_t target_items = std::max<int64_t>(1, (int64_t)sms * 4 / num_kv_heads);
+  auto round_pages = [&](int64_t t) {
+    return (int)std::max<int64_t>(page_size, (t + page_size - 1) / page_size * page_size);
+  };
+  const int balanced = round_pages((total_cost + target_items - 1) / target_items);
+  std::vector<W> items;
+  std::vector<int32_t> qlist;
+  for (const auto& gr : groups) {
+    if (gr.kv_len <= 0 || gr.qlen <= 0) continue;  // empty KV: lse = -inf, contributes nothing
+    const bool causal = gr.causal;
+    const int tq = tile_queries(gr.qlen, g);
+    const bool wide = tq * g > 16;
+    int chunk;
+    if (split_tokens > 0) {
+      chunk = round_pages(split_tokens);
+    } else {
+      const int min_chunk = round_pages((int64_t)std::min(gr.qlen, tq) * g * 8);
+      chunk = std::max(min_chunk, balanced);
+      // decode-time wide tiles run as one resident tensor-core tile
+      if (wide && !causal) {
+        chunk = std::min(chunk, BE_UMMA_MAX_TOKENS);
+        if (wide_chunk_override() > 0)
+          chunk = std::min(round_pages(wide_chunk_override()), BE_UMMA_MAX_TOKENS);
+      }
+      const int nsplit = (gr.kv_len + chunk - 1) / chunk;
+      chunk = round_pages((gr.kv_len + nsplit - 1) / nsplit);
+    }
+    for (int qs = 0; qs < gr.qlen; qs += tq) {
+      const int ql = std::min(tq, gr.qlen - qs);
+      const int q_off = (int)qlist.size();
+      for (int i = 0; i < ql; ++i) qlist.push_back(gq[gr.q_at + qs + i]);
+      // causal limit of query i of this tile: kv_len - qlen + (qs + i) + 1
+      const int kv_total_eff = gr.kv_len - gr.qlen + qs + ql;
+      for (int t = 0; t < gr.kv_len; t += chunk) {
+        const int t1 = std::min(gr.kv_len, t + chunk);
+        if (causal && t >= kv_total_eff) break;  // no query of the tile sees this chunk
+        W it;
+        it.w.q_off = q_off;
+        it.w.q_len = ql;
+        it.w.kv_off = gr.kv_off;
+        it.w.kv_begin = t;
+        it.w.kv_end = t1;
+        it.w.kv_total = kv_total_eff;
+        it.w.part_base = 0;
+        it.w.flags = causal ? BE_WORK_CAUSAL : 0;
+        it.cost = (int64_t)(t1 - t);
+        it.wide = wide;
+        items.push_back(it);
+      }
+    }
+  }
+  return emit_plan(items, qlist, kvlist, num_queries, true, page_size, g, plan, plan_capacity, info);
+}
+
 }  // namespace
 }  // namespace be
 
@@ -175,12 +250,8 @@ extern "C" int be_cascade_plan(int num_levels, const int32_t* const* qo_indptr,
     set_error("be_cascade_plan: group size %d > 64 unsupported", g);
     return BE_EINVAL;
   }
-  struct Grp {
-    int level, q0, qlen, kv_off, kv_len;
-  };
   std::vector<Grp> groups;
-  std::vector<int32_t> kvlist;
-  int64_t total_cost = 0;
+  std::vector<int32_t> kvlist, gq;
   for (int l = 0; l < num_levels; ++l) {
     const int G = num_groups[l];
     const int base = (int)kvlist.size();
@@ -205,66 +276,13 @@ extern "C" int be_cascade_plan(int num_levels, const int32_t* const* qo_indptr,
         return BE_EINVAL;
       }
       const int kv_len = np > 0 ? (np - 1) * page_size + last : 0;
-      groups.push_back({l, qo_indptr[l][gi], qlen, base + kv_indptr[l][gi], kv_len});
-      total_cost += (int64_t)kv_len * ((qlen + tile_queries(qlen, g) - 1) / std::max(1, tile_queries(qlen, g)));
+      groups.push_back({causal_last != 0 && l == num_levels - 1, (int)gq.size(), qlen,
+                        base + kv_indptr[l][gi], kv_len});
+      for (int i = 0; i < qlen; ++i) gq.push_back(qo_indptr[l][gi] + i);
     }
   }
-  // KV split: aim for ~4 CTAs per SM in total (CTAs = items x kv heads), but keep
-  // chunks long enough that the fp32 partial rows stay small next to the KV bytes
-  // they summarise (>= 8 tokens per row of the tile).
-  const int sms = num_sms > 0 ? num_sms : 148;
-  const int64_t target_items = std::max<int64_t>(1, (int64_t)sms * 4 / num_kv_heads);
-  auto round_pages = [&](int64_t t) {
-    return (int)std::max<int64_t>(page_size, (t + page_size - 1) / page_size * page_size);
-  };
-  const int balanced = round_pages((total_cost + target_items - 1) / target_items);
-  std::vector<W> items;
-  std::vector<int32_t> qlist;
-  for (const auto& gr : groups) {
-    if (gr.kv_len <= 0 || gr.qlen <= 0) continue;  // empty KV: lse = -inf, contributes nothing
-    const bool causal = causal_last && gr.level == num_levels - 1;
-    const int tq = tile_queries(gr.qlen, g);
-    const bool wide = tq * g > 16;
-    int chunk;
-    if (split_tokens > 0) {
-      chunk = round_pages(split_tokens);
-    } else {
-      const int min_chunk = round_pages((int64_t)std::min(gr.qlen, tq) * g * 8);
-      chunk = std::max(min_chunk, balanced);
-      // decode-time wide tiles run as one resident tensor-core tile
-      if (wide && !causal) {
-        chunk = std::min(chunk, BE_UMMA_MAX_TOKENS);
-        if (wide_chunk_override() > 0)
-          chunk = std::min(round_pages(wide_chunk_override()), BE_UMMA_MAX_TOKENS);
-      }
-      const int nsplit = (gr.kv_len + chunk - 1) / chunk;
-      chunk = round_pages((gr.kv_len + nsplit - 1) / nsplit);
-    }
-    for (int qs = 0; qs < gr.qlen; qs += tq) {
-      const int ql = std::min(tq, gr.qlen - qs);
-      const int q_off = (int)qlist.size();
-      for (int i = 0; i < ql; ++i) qlist.push_back(gr.q0 + qs + i);
-      // causal limit of query i of this tile: kv_len - qlen + (qs + i) + 1
-      const int kv_total_eff = gr.kv_len - gr.qlen + qs + ql;
-      for (int t = 0; t < gr.kv_len; t += chunk) {
-        const int t1 = std::min(gr.kv_len, t + chunk);
-        if (causal && t >= kv_total_eff) break;  // no query of the tile sees this chunk
-        W it;
-        it.w.q_off = q_off;
-        it.w.q_len = ql;
-        it.w.kv_off = gr.kv_off;
-        it.w.kv_begin = t;
-        it.w.kv_end = t1;
-        it.w.kv_total = kv_total_eff;
-        it.w.part_base = 0;
-        it.w.flags = causal ? BE_WORK_CAUSAL : 0;
-        it.cost = (int64_t)(t1 - t);
-        it.wide = wide;
-        items.push_back(it);
-      }
-    }
-  }
-  return emit_plan(items, qlist, kvlist, num_queries, true, page_size, g, plan, plan_capacity, info);
+  return plan_groups(groups, gq, kvlist, num_queries, page_size, g, num_kv_heads, split_tokens,
+                     num_sms, plan, plan_capacity, info);
 }
 
 extern "C" int be_tree_plan(int num_vnodes, const int32_t* q_entries, int num_q_entries,
@@ -365,4 +383,67 @@ extern "C" int be_tree_plan(int num_vnodes, const int32_t* q_entries, int num_q_
   put(mptr);
   put(mparts);
   return BE_OK;
+}
+
+// FastTree vnodes as page-list groups (for the tensor-core decode kernels).
+// In the beam trie every node starts at slot 0 of its page and every non-leaf
+// node is full, so a vnode's token range [kv_off, kv_off + kv_len) of the slot
+// table maps to whole pages: token t of the range lives in page
+// slots[kv_off + t - t % ps] / ps at slot t % ps (checked at both ends of every
+// page).  A vnode's requests may be any set (FastTree folds a small parent into
+// some children's vnodes).  Returns BE_EINVAL (nothing written) when a range is
+// not page aligned; the caller then plans with slot lists.
+extern "C" int be_tree_plan_pages(int num_vnodes, const int32_t* q_entries, int num_q_entries,
+                                  const int32_t* q_offs, const int32_t* q_lens,
+                                  const int32_t* kv_offs, const int32_t* kv_lens,
+                                  const int32_t* slots, int64_t num_slots, int batch_size,
+                                  int page_size, int num_qo_heads, int num_kv_heads, int num_sms,
+                                  int32_t* plan, int64_t plan_capacity, be_attn_plan_info* info) {
+  if (num_vnodes < 0 || batch_size < 0 || page_size < 1 || num_kv_heads < 1 ||
+      num_qo_heads % num_kv_heads || !info || !slots) {
+    set_error("be_tree_plan_pages: invalid arguments");
+    return BE_EINVAL;
+  }
+  const int g = num_qo_heads / num_kv_heads;
+  if (g > 64) {
+    set_error("be_tree_plan_pages: group size %d > 64 unsupported", g);
+    return BE_EINVAL;
+  }
+  std::vector<Grp> groups;
+  std::vector<int32_t> kvlist, gq;
+  for (int v = 0; v < num_vnodes; ++v) {
+    const int ql = q_lens[v], len = kv_lens[v];
+    if (ql <= 0 || len <= 0) continue;
+    if (q_offs[v] < 0 || q_offs[v] + ql > num_q_entries) {
+      set_error("be_tree_plan_pages: vnode %d query range outside the entry list", v);
+      return BE_EINVAL;
+    }
+    const int q_at = (int)gq.size();
+    for (int e = 0; e < ql; ++e) {
+      const int r = q_entries[q_offs[v] + e];
+      if (r < 0 || r >= batch_size) {
+        set_error("be_tree_plan_pages: vnode %d request %d outside the batch", v, r);
+        return BE_EINVAL;
+      }
+      gq.push_back(r);
+    }
+    const int64_t off = kv_offs[v];
+    if (off < 0 || off + len > num_slots) {
+      set_error("be_tree_plan_pages: vnode %d token range outside the slot table", v);
+      return BE_EINVAL;
+    }
+    const int kv_off = (int)kvlist.size();
+    for (int t = 0; t < len; t += page_size) {
+      const int m = std::min(page_size, len - t);   // tokens of this page in the range
+      const int32_t s0 = slots[off + t], s1 = slots[off + t + m - 1];
+      if (s0 < 0 || s0 % page_size != 0 || s1 != s0 + m - 1) {
+        set_error("be_tree_plan_pages: vnode %d token %d is not page aligned", v, t);
+        return BE_EINVAL;
+      }
+      kvlist.push_back(s0 / page_size);
+    }
+    groups.push_back({false, q_at, ql, kv_off, len});
+  }
+  return plan_groups(groups, gq, kvlist, batch_size, page_size, g, num_kv_heads, 0, num_sms, plan,
+                     plan_capacity, info);
 }

@@ -134,6 +134,29 @@ def build_tree_plan(v, batch_size, page_size, num_qo_heads, num_kv_heads):
     return info, buf
 
 
+def build_tree_page_plan(v, slots, batch_size, page_size, num_qo_heads, num_kv_heads, num_sms=148):
+    """The vnodes as a page-list plan (``be_tree_plan_pages``) for the tensor-core
+    decode kernels; ``slots`` is the flat slot table the vnodes index.  Returns
+    (info, plan) or None when the tree is not page aligned (use build_tree_plan)."""
+    slots = np.ascontiguousarray(slots, np.int32)
+    info = AttnPlanInfo()
+    keep = [np.ascontiguousarray(v[k], np.int32) for k in
+            ("vnode_to_q_entries", "vnode_to_q_offs", "vnode_to_q_lens", "vnode_to_kv_offs",
+             "vnode_to_kv_lens")]
+    args = [len(keep[1]), _lib.addr(keep[0]), len(keep[0]), _lib.addr(keep[1]), _lib.addr(keep[2]),
+            _lib.addr(keep[3]), _lib.addr(keep[4]), _lib.addr(slots), len(slots), batch_size,
+            page_size, num_qo_heads, num_kv_heads, num_sms]
+    rc = lib().be_tree_plan_pages(*args, None, 0, C.byref(info))
+    if rc == _lib.BE_EINVAL:
+        return None
+    if rc not in (_lib.BE_OK, _lib.BE_ECAPACITY):
+        check(rc, "be_tree_plan_pages")
+    buf = np.zeros(max(info.total_ints, 1), np.int32)
+    check(lib().be_tree_plan_pages(*args, _lib.addr(buf), buf.size, C.byref(info)),
+          "be_tree_plan_pages")
+    return info, buf
+
+
 def prepare_fasttree_metadata_for_paged_cache(tree_info: List[KVTreeNode], req_to_token: torch.Tensor,
                                               batch_size: int, num_qo_heads: int, num_kv_heads: int,
                                               head_dim: int, device="cuda", page_size: int = None):

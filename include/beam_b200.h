@@ -164,6 +164,20 @@ int be_tree_plan(int num_vnodes, const int32_t* q_entries, int num_q_entries,
                  const int32_t* r2v_lens, int batch_size, int page_size, int num_qo_heads,
                  int num_kv_heads, int32_t* plan, int64_t plan_capacity, be_attn_plan_info* info);
 
+/* The FastTree vnodes of be_fasttree_prepare as a page-list plan for the
+ * tensor-core kernels (be_attn_run / be_attn_run_fixed without slot lists):
+ * slots = the slot table the vnodes' kv_offs index (page * page_size + i).
+ * Every vnode must cover whole pages from slot 0 (true of beam-trie trees:
+ * nodes start at slot 0 of their page, non-leaf nodes are full); otherwise
+ * BE_EINVAL and the caller keeps the slot-list plan of be_tree_plan.  Same attention as be_tree_plan,
+ * split for the decode kernels like be_cascade_plan.                         */
+int be_tree_plan_pages(int num_vnodes, const int32_t* q_entries, int num_q_entries,
+                       const int32_t* q_offs, const int32_t* q_lens, const int32_t* kv_offs,
+                       const int32_t* kv_lens, const int32_t* slots, int64_t num_slots,
+                       int batch_size, int page_size, int num_qo_heads, int num_kv_heads,
+                       int num_sms, int32_t* plan, int64_t plan_capacity,
+                       be_attn_plan_info* info);
+
 /* Runs a plan for one layer.  q: [n_queries][num_qo_heads][head_dim] with
  * q_row_stride elements between queries; paged_kv_cache: one layer's pool;
  * out: [n_queries][num_qo_heads][head_dim] (out_row_stride); lse (nullable):

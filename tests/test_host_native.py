@@ -315,3 +315,60 @@ def test_vanilla_select_matches_oracle_with_ties(seed):
     want = vanilla_select(ps.tolist(), toks.tolist(), lp.tolist(), W)
     got = [[(int(ct[j]), float(cs[j])) for j in range(ptr[i], ptr[i + 1])] for i in range(n)]
     assert got == want
+
+
+def plan_token_sets(plan, info, ps, slots=None):
+    """Per query: the sorted list of (slot id) tokens every work item of a plan
+    makes it attend (slot = page * ps + i), from the plan buffer itself."""
+    wk = plan[info.off_work:info.off_work + 8 * info.n_work].reshape(-1, 8)
+    ql = plan[info.off_qlist:]
+    kv = plan[info.off_kvlist:]
+    out = {}
+    for q_off, q_len, kv_off, b, e, _, _, flags in wk:
+        toks = []
+        for t in range(b, e):
+            if flags & 2:
+                toks.append(int(slots[kv_off + t]))
+            else:
+                toks.append(int(kv[kv_off + t // ps]) * ps + t % ps)
+        for i in range(q_len):
+            out.setdefault(int(ql[q_off + i]), []).extend(toks)
+    return {q: sorted(v) for q, v in out.items()}
+
+
+@pytest.mark.parametrize("case", ["ps4_w4", "ps16_w8", "ps8_w6_churn", "ps16_w16"])
+def test_tree_page_plans_attend_what_slot_plans_attend(trajectories, case):
+    """be_tree_plan_pages (page lists for the tensor-core kernels) makes every
+    request attend exactly the tokens of the slot-list plan, each once, along
+    a whole trajectory (forks, frees, merged single-child chains)."""
+    from beam_engine_b200.fasttree import build_tree_page_plan, build_tree_plan
+    rec = trajectories[case]
+    cs = rec["case"]
+    ps = cs["ps"]
+    pt = cpu_table(ps, cs["pages"])
+    bs = BeamState(cs["W"], pt)
+    bs.add_root_sequence(rec["prompt"])
+    toks, sc = rec["root_children"]
+    bs.update_native(bs.leaves, np.array([0, len(toks)]), np.array(toks), np.array(sc))
+    hq, hkv = 32, 8
+    for step in rec["steps"]:
+        B = len(bs.leaves)
+        par, seql, kids, rptr, rl, r2t = bs.tree_arrays(per_node=True, compress=True)
+        v = plan_vnodes(par, seql, kids, rptr, np.ascontiguousarray(rl) if len(rl) else
+                        np.zeros(1, np.int32), r2t.shape[1], B, hq, hkv)
+        slots = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)]).astype(np.int32)
+        info_s, plan_s = build_tree_plan(v, B, ps, hq, hkv)
+        got = build_tree_page_plan(v, slots, B, ps, hq, hkv)
+        assert got is not None
+        info_p, plan_p = got
+        assert info_p.any_slots == 0 and info_p.max_wide_tokens <= 128
+        want = plan_token_sets(plan_s, info_s, ps, slots)
+        have = plan_token_sets(plan_p, info_p, ps)
+        assert have == want
+        for q, t in have.items():
+            assert len(set(t)) == len(t)       # every token once
+            assert len(t) == len(bs.sequence(int(bs.leaves[q])))   # the whole sequence
+        kid_t = np.array([c[0] for c in step["children"]], np.int32)
+        kid_l = np.array([c[1] for c in step["children"]], np.float64)
+        ptr, ct, csc = vanilla_select_arrays(bs.scores, kid_t, kid_l, cs["W"])
+        bs.update_native(bs.leaves, ptr, ct, csc)
