@@ -35,4 +35,4 @@ def test_tree_page_plans_select_like_slot_plans(monkeypatch, graph):
         if pages == "1" and graph:
             assert gen.step_graph_tpages is not None
     for a, b in zip(*outs):
-        np.testing.assert_allclose([x for _, x in a], [x for _, x in b], atol=2e-2, rtol=0)
+        np.testing.assert_allclose([x for _, x in a], [x for _, x in b], atol=5e-2, rtol=0)
