@@ -449,8 +449,10 @@ class BeamSearchGenerator:
                                      num_sms=self.attn.plan.num_sms)
         v, r2t = self._tree_vnodes(state, n)
         tinfo, tplan = build_tree_plan(v, n, ps, m.Hq, m.Hkv)
+        pp = self._tree_page_plan(v, r2t, n)
         elt = 4 if self.page_table.store_dtype == torch.float32 else 2
-        kind = choose(levels, cinfo, tinfo, m.Hkv, m.Hq, m.D, elt=elt)
+        kind = choose(levels, cinfo, pp[0] if pp is not None else tinfo, m.Hkv, m.Hq, m.D,
+                      elt=elt, tree_pages=pp is not None)
         self.picks.append(kind)
         self._tree_stash = (v, r2t, tinfo, tplan) if kind == "fasttree" else None
         return kind

@@ -74,10 +74,13 @@ def cascade_counts_pages_twice(levels) -> bool:
 
 
 def choose(cascade_levels, cascade_info, tree_info, hkv, hq, d, model: PickerModel | None = None,
-           elt=2) -> str:
-    """'cascade' or 'fasttree' for one decode step."""
+           elt=2, tree_pages=False) -> str:
+    """'cascade' or 'fasttree' for one decode step.  ``tree_pages``: the tree
+    step runs as a page-list plan on the same kernels as the cascade step, so it
+    is costed by the cascade model on its own plan (``tree_info``)."""
     if cascade_counts_pages_twice(cascade_levels):
         return "fasttree"
     m = model or PickerModel()
-    return ("cascade" if m.cascade_us(cascade_info, hkv, hq, d, elt)
-            <= m.tree_us(tree_info, hkv, hq, d, elt) else "fasttree")
+    tree = (m.cascade_us(tree_info, hkv, hq, d, elt) if tree_pages
+            else m.tree_us(tree_info, hkv, hq, d, elt))
+    return "cascade" if m.cascade_us(cascade_info, hkv, hq, d, elt) <= tree else "fasttree"
