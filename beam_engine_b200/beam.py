@@ -454,7 +454,7 @@ class BeamSearchGenerator:
         kind = choose(levels, cinfo, pp[0] if pp is not None else tinfo, m.Hkv, m.Hq, m.D,
                       elt=elt, tree_pages=pp is not None)
         self.picks.append(kind)
-        self._tree_stash = (v, r2t, tinfo, tplan) if kind == "fasttree" else None
+        self._tree_stash = (v, r2t, tinfo, tplan, pp) if kind == "fasttree" else None
         return kind
 
     def _tree_graph_step(self, state: BeamState, k: int, temperature: float):
@@ -464,12 +464,12 @@ class BeamSearchGenerator:
         n = len(state.leaves)
         q, wp, wpos, pos = state.step_inputs()
         if self._tree_stash is not None:
-            v, r2t, info, plan = self._tree_stash
+            v, r2t, info, plan, pp = self._tree_stash
             self._tree_stash = None
         else:
             v, r2t = self._tree_vnodes(state, n)
             info, plan = build_tree_plan(v, n, self.page_table.page_size, m.Hq, m.Hkv)
-        pp = self._tree_page_plan(v, r2t, n)
+            pp = self._tree_page_plan(v, r2t, n)
         if pp is not None:
             return self._tree_pages_graph_step(state, n, k, temperature, q, pos, wp, wpos, *pp)
         slots = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)])
