@@ -276,9 +276,8 @@ def run_b200(args, rank, world, local_rank):
         "config": {"workload": WORKLOAD,
                    "model": f"{MODEL_NAME} shape (random init)", "global_batch": PROMPTS * BEAM * replicas,
                    "seq_len": PROMPT_LEN,
-                   "tp_comm": args.tp_comm if tp_mode else None,
-                   "parallelism": f"tp{world}" if tp_mode else (f"replicas x{world}" if world > 1
-                                                                else "tp1"),
+                   "parallelism": (f"tp{world}" + ("-peer" if args.tp_comm == "peer" else "")
+                                   if tp_mode else (f"replicas x{world}" if world > 1 else "tp1")),
                    "l2": f"no flush needed: each step reads {step_bytes / 1e9:.1f} GB of weights "
                          "(> 126 MB L2)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
