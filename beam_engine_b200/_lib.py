@@ -108,6 +108,8 @@ _SIGS = {
     "be_tree_plan_pages": (C.c_int, [C.c_int, vp, C.c_int, vp, vp, vp, vp, vp, i64, C.c_int,
                                       C.c_int, C.c_int, C.c_int, C.c_int, vp, i64,
                                       C.POINTER(AttnPlanInfo)]),
+    "be_beam_select_update": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, vp, vp, vp, C.c_int, vp, vp,
+                                        vp, vp, vp, vp, vp, vp, vp]),
     "be_leaf_sequences": (i64, [vp, C.c_int, vp, vp, vp, i64]),
     "be_diverse_select": (C.c_int, [C.c_int, vp, C.c_int, vp, vp,
                                     vp, vp, vp, C.c_int, C.c_int, C.c_double,

@@ -26,6 +26,7 @@ import torch
 from . import _lib
 from ._lib import check, lib
 from .beam_state import BeamState
+from .beam_strategy import VanillaBeamSearchStrategy
 from .cascade import _Plan
 from .page_table import PageTable, stream_ptr
 from .parallel import vocab_parallel_log_softmax_topk
@@ -631,7 +632,11 @@ class BeamSearchGenerator:
                 with _Range("decode_step"):
                     vals, idx = self.decode_topk(state, k, temperature)
                 with _Range("select"):
-                    if getattr(self.strategy, "needs_state", False):
+                    if type(self.strategy) is VanillaBeamSearchStrategy:
+                        # selection + trie update in one native call
+                        new_seg = state.vanilla_step(seg, idx, vals, W)
+                        self._after_update(state)
+                    elif getattr(self.strategy, "needs_state", False):
                         cp, ct, cs, new_seg = self.strategy.select_segments(seg, state.scores, idx, vals, W,
                                                                             state=state)
                         self._apply(state, cp, ct, cs)
@@ -665,6 +670,10 @@ class BeamSearchGenerator:
 
     def _apply(self, state, child_ptr, child_tokens, child_scores):
         state.update_native(state.leaves, child_ptr, child_tokens, child_scores)
+        self._after_update(state)
+
+    def _after_update(self, state):
+        """Hand the update's copy-on-write copies to the next step (or run them)."""
         self._flush_fork()
         cs, cd, cl = state.last_copies
         if len(cs):

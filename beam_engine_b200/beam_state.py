@@ -236,12 +236,52 @@ class BeamState:
             raise MemoryError("No free pages available")
         check(rc, "add_filtered_results")
         k, c = n_new.value, n_cp.value
+        self.last_child_ptr = np.asarray(child_ptr, np.int32).copy()
         self._leaves = new_leaf[:k].copy()
         self._scores = np.asarray(child_scores, np.float64)[new_child[:k]]
         self._cand_objs = None
         self.last_copies = (cs[:c].copy(), cd[:c].copy(), cl[:c].copy())
         if c and not self.defer_copies and self.page_table.kv_cache.is_cuda:
             self.page_table.copy_blocks(*self.last_copies)
+
+    def vanilla_step(self, seg, tokens, logps, beam_size):
+        """Vanilla selection of every prompt (candidates seg[s]:seg[s+1]) on the
+        top-k (tokens / logps [ncand, k]) plus the trie update, one native call
+        (be_beam_select_update).  Returns the new per-prompt candidate ranges."""
+        seg = np.ascontiguousarray(seg, np.int32)
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        logps = np.ascontiguousarray(logps, np.float64)
+        nseg = len(seg) - 1
+        k = tokens.shape[1] if tokens.ndim == 2 else 0
+        cap = max(1, nseg * beam_size)
+        buf = getattr(self, "_vs_buf", None)
+        ncand = int(seg[-1])
+        if (buf is None or buf[0] < cap or len(buf[5]) != nseg + 1
+                or len(buf[9]) < ncand + 1):
+            buf = self._vs_buf = (cap, np.zeros(cap, np.int32), np.zeros(cap, np.float64),
+                                  np.zeros(cap, np.int32), np.zeros(cap, np.int32),
+                                  np.zeros(nseg + 1, np.int32), np.zeros(cap, np.int32),
+                                  C.c_int32(), C.c_int32(), np.zeros(max(ncand + 1, cap + 1), np.int32))
+        _, nl, ns, cs, cd, nseg_ptr, cl, n_new, n_cp, cptr = buf
+        leaves = np.ascontiguousarray(self._leaves, np.int32)
+        scores = np.ascontiguousarray(self._scores, np.float64)
+        rc = lib().be_beam_select_update(self._t, nseg, _lib.addr(seg), k, _lib.addr(leaves),
+                                         _lib.addr(scores), _lib.addr(tokens), _lib.addr(logps),
+                                         beam_size, _lib.addr(nl), _lib.addr(ns), C.byref(n_new),
+                                         _lib.addr(nseg_ptr), _lib.addr(cs), _lib.addr(cd),
+                                         _lib.addr(cl), C.byref(n_cp), _lib.addr(cptr))
+        if rc == _lib.BE_ENOMEM:
+            raise MemoryError("No free pages available")
+        check(rc, "vanilla step")
+        self.last_child_ptr = cptr[:ncand + 1].copy()
+        m, c = n_new.value, n_cp.value
+        self._leaves = nl[:m].copy()
+        self._scores = ns[:m].copy()
+        self._cand_objs = None
+        self.last_copies = (cs[:c].copy(), cd[:c].copy(), cl[:c].copy())
+        if c and not self.defer_copies and self.page_table.kv_cache.is_cuda:
+            self.page_table.copy_blocks(*self.last_copies)
+        return nseg_ptr.copy()
 
     # -- decode inputs -------------------------------------------------------
     def step_inputs(self):

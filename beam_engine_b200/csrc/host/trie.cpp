@@ -894,6 +894,46 @@ int be_vanilla_select_segments(int nseg, const int32_t* seg_ptr, int k,
   return BE_OK;
 }
 
+// One host call per decode step after the device's top-k: vanilla selection of
+// every prompt (be_vanilla_select_segments) followed by the trie update
+// (be_beam_update) of the selected children.  Outputs: the new candidates'
+// leaves and scores (in the reference's order), the new per-prompt candidate
+// ranges, the copy-on-write copies and (optional) the selection's children per
+// old candidate as CSR.  new_leaf / new_score / copy_* need nseg * beam_size
+// entries, child_ptr ncand + 1.
+int be_beam_select_update(be_trie* t, int nseg, const int32_t* seg_ptr, int k,
+                          const int32_t* cand_leaf, const double* parent_scores,
+                          const int32_t* tokens, const double* logps, int beam_size,
+                          int32_t* new_leaf, double* new_score, int32_t* n_new,
+                          int32_t* new_seg_ptr, int32_t* copy_src, int32_t* copy_dst,
+                          int32_t* copy_len, int32_t* n_copies, int32_t* child_ptr) {
+  if (nseg < 0 || !seg_ptr || beam_size < 1) {
+    set_error("be_beam_select_update: invalid arguments");
+    return BE_EINVAL;
+  }
+  const int ncand = seg_ptr[nseg];
+  struct Scratch {
+    std::vector<int32_t> ptr, ct, child;
+    std::vector<double> cs;
+  };
+  static thread_local Scratch tls;
+  Scratch& S = tls;
+  const int cap = std::max(1, nseg * beam_size);
+  S.ptr.resize(ncand + 1);
+  S.ct.resize(cap);
+  S.cs.resize(cap);
+  S.child.resize(cap);
+  int rc = be_vanilla_select_segments(nseg, seg_ptr, k, parent_scores, tokens, logps, beam_size,
+                                      S.ptr.data(), S.ct.data(), S.cs.data(), new_seg_ptr);
+  if (rc) return rc;
+  rc = be_beam_update(t, ncand, cand_leaf, S.ptr.data(), S.ct.data(), new_leaf, S.child.data(),
+                      n_new, copy_src, copy_dst, copy_len, n_copies);
+  if (rc) return rc;
+  for (int i = 0; i < *n_new; ++i) new_score[i] = S.cs[S.child[i]];
+  if (child_ptr) std::copy(S.ptr.begin(), S.ptr.begin() + ncand + 1, child_ptr);
+  return BE_OK;
+}
+
 // Everything one cascade decode step needs from the host, in one call: the
 // per-candidate inputs (query token, RoPE position, append page, append slot)
 // at out[0 .. 4 * ncand) and the attention plan (header included) at

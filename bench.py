@@ -179,19 +179,19 @@ def run_b200(args, rank, world, local_rank):
             launches["n"] += cfg["num_hidden_layers"] * (4 + 3) + 1 + 1 + 1
 
     gen.plan_hook = plan_hook
-    orig_apply = gen._apply
+    orig_after = gen._after_update
 
     churn = []
 
-    def apply_hook(state, *a):
-        orig_apply(state, *a)
+    def after_hook(state):
+        orig_after(state)
         if timing["on"]:   # share of new beams whose parent is shared with a sibling or gone
-            cp = np.asarray(a[0])
+            cp = np.asarray(state.last_child_ptr)
             kids = int(cp[-1])
             if kids:
                 churn.append(1.0 - int((np.diff(cp) > 0).sum()) / kids)
 
-    gen._apply = apply_hook
+    gen._after_update = after_hook
 
     def on_step(i):
         if i == W:

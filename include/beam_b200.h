@@ -464,6 +464,17 @@ int be_comm_allreduce_rmsnorm(be_comm* comm, int slot, void* residual, const voi
                               void* out, int rows, int hidden, float eps, int dtype,
                               void* stream);
 
+/* One host call per decode step after the device's top-k: vanilla selection
+ * of every prompt (be_vanilla_select_segments, beam_strategy.py:433-488) then
+ * the trie update (be_beam_update, beam_state.py:101-209).  new_leaf /
+ * new_score / copy_* need nseg * beam_size entries, new_seg_ptr nseg + 1;
+ * child_ptr (may be NULL): the selected children per old candidate as CSR.  */
+int be_beam_select_update(be_trie* t, int nseg, const int32_t* seg_ptr, int k,
+                          const int32_t* cand_leaf, const double* parent_scores,
+                          const int32_t* tokens, const double* logps, int beam_size,
+                          int32_t* new_leaf, double* new_score, int32_t* n_new,
+                          int32_t* new_seg_ptr, int32_t* copy_src, int32_t* copy_dst,
+                          int32_t* copy_len, int32_t* n_copies, int32_t* child_ptr);
 /* One call for a cascade decode step's host inputs (beam.py:168-221 decode
  * inputs + BeamState.get_cascade_input beam_state.py:211-412 + the attention
  * plan): out[0..n) query tokens, [n..2n) RoPE positions, [2n..3n) append
