@@ -372,3 +372,30 @@ def test_tree_page_plans_attend_what_slot_plans_attend(trajectories, case):
         kid_l = np.array([c[1] for c in step["children"]], np.float64)
         ptr, ct, csc = vanilla_select_arrays(bs.scores, kid_t, kid_l, cs["W"])
         bs.update_native(bs.leaves, ptr, ct, csc)
+
+
+@pytest.mark.parametrize("case", ["ps4_w4", "ps8_w6_churn", "ps16_w16"])
+def test_fused_select_update_matches_reference_trajectory(trajectories, case):
+    """be_beam_select_update (selection + trie update in one call) reproduces the
+    reference trajectory: selections, copies, free list and final ranking."""
+    rec = trajectories[case]
+    cs = rec["case"]
+    pt = cpu_table(cs["ps"], cs["pages"])
+    bs = BeamState(cs["W"], pt)
+    bs.add_root_sequence(rec["prompt"])
+    toks, sc = rec["root_children"]
+    bs.update_native(bs.leaves, np.array([0, len(toks)]), np.array(toks), np.array(sc))
+    seg = np.array([0, len(bs.leaves)])
+    for step in rec["steps"]:
+        kid_t = np.array([c[0] for c in step["children"]], np.int32)
+        kid_l = np.array([c[1] for c in step["children"]], np.float64)
+        seg = bs.vanilla_step(seg, kid_t, kid_l, cs["W"])
+        sel = step["selected"]
+        cp = bs.last_child_ptr
+        assert [int(cp[i + 1] - cp[i]) for i in range(len(sel))] == [len(s) for s in sel]
+        assert sorted(bs.scores.tolist()) == sorted(x for s in sel for _, x in s)
+        assert [list(map(int, c)) for c in zip(*bs.last_copies)] == step["copies"]
+        assert pt.free_pages == step["free_after"]
+        assert seg.tolist() == [0, len(bs.leaves)]
+    final = bs.get_final_sequences(cs["W"], 1.0)
+    assert [[s, x] for s, x in final] == rec["final"]
