@@ -423,9 +423,8 @@ class BeamSearchGenerator:
         if not self.tree_pages:
             return None
         m = self.model
-        slots = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)]).astype(np.int32)
-        got = build_tree_page_plan(v, slots, n, self.page_table.page_size, m.Hq, m.Hkv,
-                                   self.attn.plan.num_sms)
+        got = build_tree_page_plan(v, np.ascontiguousarray(r2t, np.int32).reshape(-1), n,
+                                   self.page_table.page_size, m.Hq, m.Hkv, self.attn.plan.num_sms)
         if got is None or got[0].max_wide_tokens > UMMA_MAX_TOKENS:
             return None
         return got
