@@ -448,11 +448,10 @@ class BeamSearchGenerator:
         cinfo, _ = cascade_plan_host(levels, n, ps, m.Hq, m.Hkv, causal=True,
                                      num_sms=self.attn.plan.num_sms)
         v, r2t = self._tree_vnodes(state, n)
-        tinfo, tplan = build_tree_plan(v, n, ps, m.Hq, m.Hkv)
         pp = self._tree_page_plan(v, r2t, n)
+        tinfo, tplan = (pp[0], None) if pp is not None else build_tree_plan(v, n, ps, m.Hq, m.Hkv)
         elt = 4 if self.page_table.store_dtype == torch.float32 else 2
-        kind = choose(levels, cinfo, pp[0] if pp is not None else tinfo, m.Hkv, m.Hq, m.D,
-                      elt=elt, tree_pages=pp is not None)
+        kind = choose(levels, cinfo, tinfo, m.Hkv, m.Hq, m.D, elt=elt, tree_pages=pp is not None)
         self.picks.append(kind)
         self._tree_stash = (v, r2t, tinfo, tplan, pp) if kind == "fasttree" else None
         return kind
@@ -468,10 +467,12 @@ class BeamSearchGenerator:
             self._tree_stash = None
         else:
             v, r2t = self._tree_vnodes(state, n)
-            info, plan = build_tree_plan(v, n, self.page_table.page_size, m.Hq, m.Hkv)
             pp = self._tree_page_plan(v, r2t, n)
+            info = plan = None
         if pp is not None:
             return self._tree_pages_graph_step(state, n, k, temperature, q, pos, wp, wpos, *pp)
+        if plan is None:
+            info, plan = build_tree_plan(v, n, self.page_table.page_size, m.Hq, m.Hkv)
         slots = np.concatenate([r2t.reshape(-1), np.full(256, -1, np.int32)])
         sg = self.step_graph_tree
         if not (sg is not None and sg.fits(n, k, temperature, info, len(slots))):
