@@ -122,3 +122,37 @@ def test_generate_ids_host_loop_matches_oracle(strategy, W, ps):
         np.testing.assert_allclose([x for _, x in got], [x for _, x in want], rtol=0, atol=0)
     # every copy-on-write copy the updates asked for reached the (fake) device step
     assert all(len(a) == len(b) == len(c) for a, b, c in gen.forks)
+
+
+@pytest.mark.parametrize("tree_pages", [False, True])
+def test_pick_kernel_host_side(tree_pages):
+    """kernel_type "auto": the per-step picker builds both plans on the host,
+    returns a kind and stashes the tree plan for the step (page-list plan when
+    tree_pages), along a trajectory with uneven beams."""
+    from types import SimpleNamespace
+    gen = FakeGenerator(VanillaBeamSearchStrategy(), 16, 2048)
+    gen.model = SimpleNamespace(vocab=VOCAB, Hq=32, Hkv=8, D=128, Hq_total=32, Hkv_total=8)
+    gen.attn = SimpleNamespace(plan=SimpleNamespace(num_sms=148))
+    gen.picks, gen.tree_pages, gen._tree_stash = [], tree_pages, None
+    from beam_engine_b200.beam_state import BeamState
+    st = BeamState(8, gen.page_table)
+    st.defer_copies = True
+    rng = np.random.default_rng(5)
+    gen.prefill(st, [rng.integers(0, VOCAB, 40).tolist(), rng.integers(0, VOCAB, 23).tolist()])
+    st.update_native(st.leaves, np.array([0, 8, 16], np.int32),
+                     rng.integers(0, VOCAB, 16).astype(np.int32), -rng.random(16))
+    seg = np.array([0, 8, 16])
+    kinds = []
+    for _ in range(10):
+        kind = gen.pick_kernel(st)
+        kinds.append(kind)
+        if kind == "fasttree":
+            v, r2t, tinfo, tplan, pp = gen._tree_stash
+            assert (pp is not None) == tree_pages
+            assert (tplan is None) == tree_pages
+            assert tinfo.n_work > 0
+        else:
+            assert gen._tree_stash is None
+        vals, idx = gen.decode_topk(st, 16, 1.0)
+        seg = st.vanilla_step(seg, idx, vals, 8)
+    assert set(kinds) <= {"cascade", "fasttree"} and len(gen.picks) == 10
