@@ -110,6 +110,7 @@ _SIGS = {
                                       C.POINTER(AttnPlanInfo)]),
     "be_beam_select_update": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, vp, vp, vp, C.c_int, vp, vp,
                                         vp, vp, vp, vp, vp, vp, vp]),
+    "be_cascade_pages_twice": (C.c_int, [C.c_int, vp, vp, vp, vp, C.c_int]),
     "be_leaf_sequences": (i64, [vp, C.c_int, vp, vp, vp, i64]),
     "be_diverse_select": (C.c_int, [C.c_int, vp, C.c_int, vp, vp,
                                     vp, vp, vp, C.c_int, C.c_int, C.c_double,

@@ -348,21 +348,28 @@ class BeamState:
         plans use; the reference's layout is one node per trie node."""
         n = len(self._leaves)
         nn, ml = C.c_int32(), C.c_int32()
-        z = np.zeros(1, np.int32)
-        args = [self._t, n, _lib.ptr32(self._leaves), (1 if per_node else 0) | (2 if compress else 0),
+        leaves = np.ascontiguousarray(self._leaves, np.int32)
+        args = [self._t, n, _lib.ptr32(leaves), (1 if per_node else 0) | (2 if compress else 0),
                 self.page_table.page_size]
-        check(lib().be_tree_build(*args, 0, C.byref(nn), *[_lib.ptr32(z)] * 5, 0, C.byref(ml),
-                                  None, 0), "tree build")
-        N, M = nn.value, ml.value
-        par, seql, kids = (np.zeros(max(N, 1), np.int32) for _ in range(3))
-        rptr = np.zeros(N + 1, np.int32)
-        cap_r = max(1, N * n)
-        rl = np.zeros(cap_r, np.int32)
-        r2t = np.zeros((max(n, 1), max(M, 1)), np.int32)
-        check(lib().be_tree_build(*args, N, C.byref(nn), _lib.ptr32(par), _lib.ptr32(seql),
-                                  _lib.ptr32(kids), _lib.ptr32(rptr), _lib.ptr32(rl), cap_r,
-                                  C.byref(ml), _lib.ptr32(r2t), r2t.size), "tree build")
-        return par[:N], seql[:N], kids[:N], rptr, rl[:rptr[-1]], r2t[:n, :M]
+        # one native pass with the capacities of the last call (grown and retried when short)
+        N, M = getattr(self, "_tree_caps", (64, 64))
+        while True:
+            par, seql, kids = (np.zeros(max(N, 1), np.int32) for _ in range(3))
+            rptr = np.zeros(N + 1, np.int32)
+            cap_r = max(1, N * n)
+            rl = np.zeros(cap_r, np.int32)
+            r2t = np.empty(max(n, 1) * max(M, 1), np.int32)
+            rc = lib().be_tree_build(*args, N, C.byref(nn), _lib.ptr32(par), _lib.ptr32(seql),
+                                     _lib.ptr32(kids), _lib.ptr32(rptr), _lib.ptr32(rl), cap_r,
+                                     C.byref(ml), _lib.ptr32(r2t), r2t.size)
+            if rc != _lib.BE_ECAPACITY:
+                break
+            N, M = max(N, nn.value + nn.value // 4 + 16), max(M, ml.value + 64)
+        check(rc, "tree build")
+        self._tree_caps = (N, M)
+        Nn, Mm = nn.value, ml.value
+        return (par[:Nn], seql[:Nn], kids[:Nn], rptr[:Nn + 1], rl[:rptr[Nn]],
+                r2t[:max(n, 1) * Mm].reshape(max(n, 1), Mm)[:n])
 
     def get_fasttree_input(self, per_node: bool = True):
         """beam_state.py:566-633.  ``seqlen`` is per node by default -- the length

@@ -447,3 +447,40 @@ extern "C" int be_tree_plan_pages(int num_vnodes, const int32_t* q_entries, int 
   return plan_groups(groups, gq, kvlist, batch_size, page_size, g, num_kv_heads, 0, num_sms, plan,
                      plan_capacity, info);
 }
+
+// True (1) when some query attends one page at two levels of a cascade plan:
+// the reference's uneven-tree quirk (a candidate whose branch ends above the
+// deepest level re-uses its deepest nodes at every later level,
+// beam_state.py:299-302).  Pages are marked per query with a stamp.
+extern "C" int be_cascade_pages_twice(int num_levels, const int32_t* const* qo_indptr,
+                                      const int32_t* const* kv_indptr,
+                                      const int32_t* const* kv_indices, const int32_t* num_groups,
+                                      int num_queries) {
+  if (num_levels < 0 || num_queries < 0) {
+    set_error("be_cascade_pages_twice: invalid arguments");
+    return -BE_EINVAL;
+  }
+  int32_t max_page = -1;
+  for (int l = 0; l < num_levels; ++l) {
+    const int G = num_groups[l];
+    const int np = G > 0 ? kv_indptr[l][G] : 0;
+    for (int i = 0; i < np; ++i) max_page = std::max(max_page, kv_indices[l][i]);
+  }
+  std::vector<int32_t> mark((size_t)max_page + 2, -1);
+  std::vector<int> gi(num_levels, 0);   // current group of each level (queries ascend)
+  for (int q = 0; q < num_queries; ++q) {
+    for (int l = 0; l < num_levels; ++l) {
+      const int G = num_groups[l];
+      int& g = gi[l];
+      while (g < G && qo_indptr[l][g + 1] <= q) ++g;
+      if (g >= G || qo_indptr[l][g] > q) continue;   // q in no group of this level
+      for (int i = kv_indptr[l][g]; i < kv_indptr[l][g + 1]; ++i) {
+        const int32_t pg = kv_indices[l][i];
+        if (pg < 0) continue;
+        if (mark[pg] == q) return 1;
+        mark[pg] = q;
+      }
+    }
+  }
+  return 0;
+}

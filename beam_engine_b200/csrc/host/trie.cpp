@@ -521,59 +521,116 @@ int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node,
   // child (a 1024-token prefix is one node, not 64); needs per-node lengths
   const bool compress = (per_node & 2) != 0;
   const bool own_len = (per_node & 1) != 0 || compress;
+  // per-thread scratch, node-indexed arrays validated by stamps (no clearing,
+  // no hash maps): live children lists (compress) and trie node -> tree node
+  struct Scratch {
+    std::vector<std::vector<int32_t>> paths, lk_lists;
+    std::vector<int32_t> lk_stamp, lk_slot, tid_stamp, tid_val, vis_stamp, vis_cand, vis_pos, up;
+    std::vector<int32_t> fresh, src_cand;   // per candidate: first new path index, copied-from
+    int32_t stamp = 0;
+  };
+  static thread_local Scratch tls;
+  Scratch& S = tls;
+  if (S.lk_stamp.size() < t->nodes.size()) {
+    S.lk_stamp.resize(t->nodes.size(), 0);
+    S.lk_slot.resize(t->nodes.size(), 0);
+    S.tid_stamp.resize(t->nodes.size(), 0);
+    S.tid_val.resize(t->nodes.size(), 0);
+    S.vis_stamp.resize(t->nodes.size(), 0);
+    S.vis_cand.resize(t->nodes.size(), 0);
+    S.vis_pos.resize(t->nodes.size(), 0);
+  }
+  const int32_t st = ++S.stamp;
   std::vector<int32_t> roots;
-  std::vector<std::vector<int32_t>> paths(ncand);
+  auto& paths = S.paths;
+  if ((int)paths.size() < ncand) paths.resize(ncand);
+  S.fresh.assign(ncand, 0);
+  S.src_cand.assign(ncand, -1);
   int64_t ml = 0;
   for (int c = 0; c < ncand; ++c) {
     if (!t->valid(cand_leaf[c])) {
       set_error("be_tree_build: bad leaf %d", cand_leaf[c]);
       return BE_EINVAL;
     }
-    t->path(cand_leaf[c], paths[c]);
-    if (std::find(roots.begin(), roots.end(), paths[c][0]) == roots.end())
-      roots.push_back(paths[c][0]);
+    // root path: walk up to the first node an earlier candidate's path holds
+    // and copy that path's prefix (candidates share long prefixes)
+    auto& up = S.up;
+    up.clear();
+    int32_t a = cand_leaf[c];
+    while (a >= 0 && S.vis_stamp[a] != st) {
+      up.push_back(a);
+      a = t->nodes[a].parent;
+    }
+    auto& pc = paths[c];
+    pc.clear();
+    if (a >= 0) {
+      const auto& src = paths[S.vis_cand[a]];
+      pc.insert(pc.end(), src.begin(), src.begin() + S.vis_pos[a] + 1);
+      S.src_cand[c] = S.vis_cand[a];
+    }
+    S.fresh[c] = (int32_t)pc.size();
+    for (auto it = up.rbegin(); it != up.rend(); ++it) {
+      S.vis_stamp[*it] = st;
+      S.vis_cand[*it] = c;
+      S.vis_pos[*it] = (int32_t)pc.size();
+      pc.push_back(*it);
+    }
+    if (std::find(roots.begin(), roots.end(), pc[0]) == roots.end()) roots.push_back(pc[0]);
     ml = std::max(ml, t->seq_len(cand_leaf[c]));
   }
-  // live children (on some candidate's path) of every live trie node
-  std::unordered_map<int32_t, std::vector<int32_t>> live_kids;
+  // live children (on some candidate's path) of every live trie node, in order
+  // of first appearance
+  int n_lists = 0;
+  auto live_list = [&](int32_t n) -> std::vector<int32_t>* {
+    return S.lk_stamp[n] == st ? &S.lk_lists[S.lk_slot[n]] : nullptr;
+  };
   if (compress) {
-    for (int c = 0; c < ncand; ++c)
-      for (size_t i = 0; i + 1 < paths[c].size(); ++i) {
-        auto& v = live_kids[paths[c][i]];
-        if (std::find(v.begin(), v.end(), paths[c][i + 1]) == v.end()) v.push_back(paths[c][i + 1]);
+    for (int c = 0; c < ncand; ++c)   // pairs inside a copied prefix were seen already
+      for (size_t i = (size_t)std::max(0, S.fresh[c] - 1); i + 1 < paths[c].size(); ++i) {
+        const int32_t a = paths[c][i], b = paths[c][i + 1];
+        if (S.lk_stamp[a] != st) {
+          S.lk_stamp[a] = st;
+          S.lk_slot[a] = n_lists;
+          if ((int)S.lk_lists.size() <= n_lists) S.lk_lists.emplace_back();
+          S.lk_lists[n_lists++].clear();
+        }
+        auto& v = S.lk_lists[S.lk_slot[a]];
+        if (std::find(v.begin(), v.end(), b) == v.end()) v.push_back(b);
       }
   }
   auto chain_end = [&](int32_t n) {   // last trie node of the chain starting at n
     if (!compress) return n;
     for (;;) {
-      auto it = live_kids.find(n);
-      if (it == live_kids.end() || it->second.size() != 1) return n;
-      n = it->second[0];
+      const auto* v = live_list(n);
+      if (!v || v->size() != 1) return n;
+      n = (*v)[0];
     }
   };
-  auto kids_of = [&](int32_t last) -> std::vector<int32_t> {
+  static const std::vector<int32_t> kNone;
+  auto kids_of = [&](int32_t last) -> const std::vector<int32_t>& {
     if (!compress) return t->nodes[last].children;
-    auto it = live_kids.find(last);
-    return it == live_kids.end() ? std::vector<int32_t>{} : it->second;
+    const auto* v = live_list(last);
+    return v ? *v : kNone;
   };
+  auto has_tid = [&](int32_t n) { return S.tid_stamp[n] == st; };
   // tree nodes in BFS order; a node is a chain head (one trie node unless compressed)
-  std::unordered_map<int32_t, int32_t> tid;   // trie node -> tree node (every chain member)
   std::vector<int32_t> order, order_last;
   std::deque<int32_t> q(roots.begin(), roots.end());
   while (!q.empty()) {
     const int32_t n = q.front();
     q.pop_front();
-    if (tid.count(n)) continue;
+    if (has_tid(n)) continue;
     const int32_t id = (int32_t)order.size();
     const int32_t last = chain_end(n);
     for (int32_t m = last;; m = t->nodes[m].parent) {
-      tid[m] = id;
+      S.tid_stamp[m] = st;
+      S.tid_val[m] = id;
       if (m == n) break;
     }
     order.push_back(n);
     order_last.push_back(last);
     for (int32_t ch : kids_of(last))
-      if (!tid.count(ch)) q.push_back(ch);
+      if (!has_tid(ch)) q.push_back(ch);
   }
   *num_nodes = (int32_t)order.size();
   *max_len = (int32_t)ml;
@@ -582,18 +639,10 @@ int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node,
     set_error("be_tree_build: capacity exceeded");
     return BE_ECAPACITY;
   }
-  // requests per node (candidate order)
-  std::vector<std::vector<int32_t>> reqs(order.size());
-  for (int c = 0; c < ncand; ++c)
-    for (int32_t n : paths[c]) {
-      auto& r = reqs[tid[n]];
-      if (r.empty() || r.back() != c) r.push_back(c);
-    }
-  int64_t rp = 0;
   for (size_t i = 0; i < order.size(); ++i) {
     const auto& head = t->nodes[order[i]];
     const int32_t last = order_last[i];
-    node_parent[i] = head.parent < 0 ? -1 : (tid.count(head.parent) ? tid[head.parent] : -1);
+    node_parent[i] = head.parent < 0 ? -1 : (has_tid(head.parent) ? S.tid_val[head.parent] : -1);
     int64_t len = 0;
     for (int32_t m = last;; m = t->nodes[m].parent) {
       len += (int64_t)t->nodes[m].tokens.size();
@@ -601,6 +650,14 @@ int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node,
     }
     node_seqlen[i] = own_len ? (int32_t)len : (int32_t)t->seq_len(last);
     node_children[i] = (int32_t)kids_of(last).size();
+  }
+  // requests per node (candidate order): a candidate's path passes whole tree
+  // nodes, so its tree nodes are its leaf's node and that node's ancestors
+  std::vector<std::vector<int32_t>> reqs(order.size());
+  for (int c = 0; c < ncand; ++c)
+    for (int32_t tn = S.tid_val[cand_leaf[c]]; tn >= 0; tn = node_parent[tn]) reqs[tn].push_back(c);
+  int64_t rp = 0;
+  for (size_t i = 0; i < order.size(); ++i) {
     req_ptr[i] = (int32_t)rp;
     for (int32_t r : reqs[i]) {
       if (rp >= cap_req_list) {
@@ -615,8 +672,19 @@ int be_tree_build(be_trie* t, int ncand, const int32_t* cand_leaf, int per_node,
   for (int c = 0; c < ncand; ++c) {
     int32_t* row = req_to_token + (int64_t)c * ml;
     int64_t k = 0;
-    for (int32_t n : paths[c])
-      for (size_t i = 0; i < t->nodes[n].tokens.size(); ++i) row[k++] = t->nodes[n].page * ps + (int32_t)i;
+    size_t i0 = 0;
+    const auto& pc = paths[c];
+    if (S.src_cand[c] >= 0 && S.fresh[c] < (int32_t)pc.size()) {
+      // the prefix shared with an earlier candidate: copy its slots
+      k = t->nodes[pc[S.fresh[c]]].prefix;
+      std::memcpy(row, req_to_token + (int64_t)S.src_cand[c] * ml, (size_t)k * sizeof(int32_t));
+      i0 = (size_t)S.fresh[c];
+    }
+    for (size_t j = i0; j < pc.size(); ++j) {
+      const auto& nd = t->nodes[pc[j]];
+      const int32_t base = nd.page * ps;
+      for (size_t i = 0; i < nd.tokens.size(); ++i) row[k++] = base + (int32_t)i;
+    }
     for (; k < ml; ++k) row[k] = 0;
   }
   return BE_OK;

@@ -54,7 +54,27 @@ class PickerModel:
 
 
 def cascade_counts_pages_twice(levels) -> bool:
-    """True when some query attends one page at two levels (uneven trees)."""
+    """True when some query attends one page at two levels (uneven trees);
+    native (``be_cascade_pages_twice``)."""
+    import ctypes as C
+    from . import _lib
+    from ._lib import check, lib
+    L = len(levels)
+    if L == 0:
+        return False
+    arrs = [[np.ascontiguousarray(lv[k], np.int32) for lv in levels]
+            for k in ("qo_indptr", "kv_indptr", "kv_indices")]
+    ptrs = [(C.c_void_p * L)(*[a.ctypes.data for a in grp]) for grp in arrs]
+    ng = np.asarray([len(a) - 1 for a in arrs[0]], np.int32)
+    nq = max(int(a[-1]) if len(a) else 0 for a in arrs[0])
+    rc = lib().be_cascade_pages_twice(L, ptrs[0], ptrs[1], ptrs[2], _lib.addr(ng), nq)
+    if rc < 0:
+        check(-rc, "be_cascade_pages_twice")
+    return rc == 1
+
+
+def cascade_counts_pages_twice_py(levels) -> bool:
+    """Pure-Python statement of the same check (kept as the test's reference)."""
     seen = {}
     for lv in levels:
         qo = np.asarray(lv["qo_indptr"])

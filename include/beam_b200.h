@@ -475,6 +475,14 @@ int be_beam_select_update(be_trie* t, int nseg, const int32_t* seg_ptr, int k,
                           int32_t* new_leaf, double* new_score, int32_t* n_new,
                           int32_t* new_seg_ptr, int32_t* copy_src, int32_t* copy_dst,
                           int32_t* copy_len, int32_t* n_copies, int32_t* child_ptr);
+/* 1 when some query of a cascade plan attends one page at two levels (the
+ * reference's uneven-tree quirk, beam_state.py:299-302), else 0; the picker
+ * then takes the tree plan (each page once).  Same level arrays as
+ * be_cascade_plan; -BE_EINVAL on bad arguments.                              */
+int be_cascade_pages_twice(int num_levels, const int32_t* const* qo_indptr,
+                           const int32_t* const* kv_indptr, const int32_t* const* kv_indices,
+                           const int32_t* num_groups, int num_queries);
+
 /* One call for a cascade decode step's host inputs (beam.py:168-221 decode
  * inputs + BeamState.get_cascade_input beam_state.py:211-412 + the attention
  * plan): out[0..n) query tokens, [n..2n) RoPE positions, [2n..3n) append

@@ -399,3 +399,20 @@ def test_fused_select_update_matches_reference_trajectory(trajectories, case):
         assert seg.tolist() == [0, len(bs.leaves)]
     final = bs.get_final_sequences(cs["W"], 1.0)
     assert [[s, x] for s, x in final] == rec["final"]
+
+
+def test_native_pages_twice_check_matches_python(trajectories, cascade_trees):
+    """be_cascade_pages_twice against the Python statement of the check, on the
+    reference's cascade levels of every trajectory step and the known trees."""
+    from beam_engine_b200.picker import cascade_counts_pages_twice, cascade_counts_pages_twice_py
+    seen = set()
+    for rec in trajectories.values():
+        for step in rec["steps"]:
+            lv = step["cascade"]["levels"]
+            got = cascade_counts_pages_twice(lv)
+            assert got == cascade_counts_pages_twice_py(lv)
+            seen.add(got)
+    for t in cascade_trees.values():
+        lv = t["expect"]["levels"]
+        assert cascade_counts_pages_twice(lv) == cascade_counts_pages_twice_py(lv)
+    assert seen == {True, False}
