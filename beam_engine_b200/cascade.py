@@ -95,6 +95,9 @@ class _Plan:
         check(rc, "be_attn_run")
 
 
+_plan_cap = 4096     # int32 capacity of the next host plan buffer (grows on demand)
+
+
 def cascade_plan_host(levels, num_queries, page_size, num_qo_heads, num_kv_heads, causal=True,
                       split_tokens=0, num_sms=148, plan_buf=None):
     """Host planner call on python/numpy level arrays; returns (info, plan ints)."""
@@ -110,12 +113,15 @@ def cascade_plan_host(levels, num_queries, page_size, num_qo_heads, num_kv_heads
         return lib().be_cascade_plan(L, *ptrs, _lib.ptr32(ng), num_queries, page_size,
                                      num_qo_heads, num_kv_heads, 1 if causal else 0,
                                      split_tokens, num_sms, buf, cap, C.byref(info))
-    rc = call(None, 0)
-    if rc not in (_lib.BE_OK, _lib.BE_ECAPACITY):
-        check(rc, "be_cascade_plan")
-    buf = np.zeros(info.total_ints, np.int32)
-    check(call(_lib.ptr32(buf), buf.size), "be_cascade_plan")
-    return info, buf
+    global _plan_cap
+    buf = np.empty(_plan_cap, np.int32)       # one call at the last plan's size
+    rc = call(_lib.ptr32(buf), buf.size)
+    if rc == _lib.BE_ECAPACITY:
+        _plan_cap = int(info.total_ints * 1.25) + 1024
+        buf = np.empty(_plan_cap, np.int32)
+        rc = call(_lib.ptr32(buf), buf.size)
+    check(rc, "be_cascade_plan")
+    return info, buf[:info.total_ints]
 
 
 class MultiLevelCascadeAttentionWrapper:
