@@ -398,19 +398,20 @@ class BeamSearchGenerator:
         ids, pos, wpage, wpos = [], [], [], []
         for pr in prompts:
             chain = state.add_root_sequence(pr)
-            pages = [n.page_id for n in chain]
-            pages_all.extend(pages)
+            pages = np.asarray([n.page_id for n in chain], np.int32)
+            pages_all.extend(pages.tolist())
             kvp.append(kvp[-1] + len(pages))
             last.append(len(chain[-1].tokens))
             qo.append(qo[-1] + len(pr))
-            ids.extend(pr)
-            pos.extend(range(len(pr)))
-            for i in range(len(pr)):
-                wpage.append(pages[i // ps])
-                wpos.append(i % ps)
+            ids.append(np.asarray(pr, np.int32))
+            t = np.arange(len(pr), dtype=np.int32)
+            pos.append(t)
+            wpage.append(pages[t // ps])
+            wpos.append(t % ps)
         rows = np.asarray(qo[1:], np.int32) - 1
+        cat = lambda xs: np.concatenate(xs).astype(np.int32) if xs else np.zeros(0, np.int32)
         d_ids, d_pos, d_wp, d_wpos, d_rows = self._to_device(
-            [_i32(ids), _i32(pos), _i32(wpage), _i32(wpos), rows])
+            [cat(ids), cat(pos), cat(wpage), cat(wpos), rows])
         self.attn.plan_levels([dict(qo_indptr=qo, kv_indptr=kvp, kv_indices=pages_all,
                                     kv_last_page_len=last)], len(ids), causal=True)
         logits = self.model.forward(d_ids.long(), d_pos, self.page_table, d_wp, d_wpos, self.attn,
