@@ -156,3 +156,43 @@ def test_pick_kernel_host_side(tree_pages):
         vals, idx = gen.decode_topk(st, 16, 1.0)
         seg = st.vanilla_step(seg, idx, vals, 8)
     assert set(kinds) <= {"cascade", "fasttree"} and len(gen.picks) == 10
+
+
+@pytest.mark.parametrize("ps", [16, 4])
+def test_prefill_inputs(ps):
+    """The prefill's device inputs: token ids, positions, each token's page and
+    in-page slot along its prompt's root chain, and the last row of every prompt."""
+    from beam_engine_b200.beam_state import BeamState
+
+    class Captured(Exception):
+        pass
+
+    gen = FakeGenerator(VanillaBeamSearchStrategy(), ps, 4096)
+    got = {}
+
+    def to_device(arrays):
+        got["a"] = [np.asarray(a).copy() for a in arrays]
+        raise Captured()
+
+    gen._to_device = to_device
+    st = BeamState(4, gen.page_table)
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, 1000, n).tolist() for n in (37, 16, 5, 64)]
+    with pytest.raises(Captured):
+        BeamSearchGenerator.prefill(gen, st, prompts)
+    ids, pos, wp, wpos, rows = got["a"]
+    want = [[], [], [], []]
+    for leaf, pr in zip(st.leaves, prompts):
+        chain = []
+        from beam_engine_b200.beam_state import TrieNode
+        node = TrieNode(trie=st._t, node_id=int(leaf), _owner=gen.page_table)
+        while node is not None:
+            chain.append(node.page_id)
+            node = node.parent
+        pages = chain[::-1]
+        want[0] += pr
+        want[1] += list(range(len(pr)))
+        want[2] += [pages[i // ps] for i in range(len(pr))]
+        want[3] += [i % ps for i in range(len(pr))]
+    assert [a.tolist() for a in (ids, pos, wp, wpos)] == want
+    assert rows.tolist() == (np.cumsum([len(p) for p in prompts]) - 1).tolist()
