@@ -162,3 +162,15 @@ def test_empty_and_invalid():
         diverse_select_segments(np.array([0, 1]), np.zeros(1), np.zeros((1, 2), np.int32),
                                 np.zeros((1, 2)), np.array([0, 1], np.int32), np.zeros(1, np.int32),
                                 0, 2, 0.5, "hamming", 1.0)
+
+
+def test_single_choice_helpers():
+    """The reference's per-choice helpers (beam_strategy.py:105-155) kept on the class."""
+    s = DiverseBeamSearchStrategy(diversity_penalty=0.5)
+    assert s._compute_hamming_diversity(3, {1, 3}) == 0.5
+    assert s._compute_hamming_diversity(4, {1, 3}) == 0.0
+    assert s._compute_cumulative_diversity([1, 2, 3], []) == 0.0
+    # overlaps 2 and 1 -> (2 * 0.5 + 1 * 0.5) / 2
+    assert s._compute_cumulative_diversity([1, 2, 3], [[1, 2, 9], [7, 2]]) == 0.75
+    assert s._apply_length_penalty(-2.0, 4) == -0.5
+    assert DiverseBeamSearchStrategy(length_penalty=0)._apply_length_penalty(-2.0, 4) == -2.0
