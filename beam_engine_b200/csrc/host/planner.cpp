@@ -54,8 +54,16 @@ inline int tile_queries(int qlen, int g) {
 int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
               const std::vector<int32_t>& kvlist, int num_queries, bool allow_direct,
               int page_size, int g, int32_t* plan, int64_t cap, be_attn_plan_info* info) {
+  // per-thread scratch (one lookup per call; the planner runs every decode step)
+  struct Scratch {
+    std::vector<int32_t> cover, pcount, pfill, pflat, mq, mptr, mparts, order;
+    std::vector<char> direct_q;
+  };
+  static thread_local Scratch tls;
+  Scratch& S = tls;
   // Which queries are covered exactly once (direct write) and which need merging.
-  std::vector<int> cover(num_queries, 0);
+  auto& cover = S.cover;
+  cover.assign(num_queries, 0);
   for (auto& it : items)
     for (int i = 0; i < it.w.q_len; ++i) cover[qlist[it.w.q_off + i]]++;
   int n_parts = 0;
@@ -70,8 +78,10 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
     }
   }
   // partial rows per query as CSR (items in plan order, as a per-query list would hold them)
-  std::vector<char> direct_q(num_queries, 0);
-  std::vector<int32_t> pcount(num_queries + 1, 0);
+  auto& direct_q = S.direct_q;
+  auto& pcount = S.pcount;
+  direct_q.assign(num_queries, 0);
+  pcount.assign(num_queries + 1, 0);
   for (auto& it : items)
     for (int i = 0; i < it.w.q_len; ++i) {
       const int q = qlist[it.w.q_off + i];
@@ -79,15 +89,49 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
       else pcount[q + 1]++;
     }
   for (int q = 0; q < num_queries; ++q) pcount[q + 1] += pcount[q];
-  std::vector<int32_t> pfill(pcount.begin(), pcount.end() - 1), pflat(pcount[num_queries]);
+  auto& pfill = S.pfill;
+  auto& pflat = S.pflat;
+  pfill.assign(pcount.begin(), pcount.end() - 1);
+  pflat.resize(pcount[num_queries]);
   for (auto& it : items)
     for (int i = 0; i < it.w.q_len; ++i)
       if (it.w.part_base >= 0) pflat[pfill[qlist[it.w.q_off + i]]++] = it.w.part_base + i;
-  std::stable_sort(items.begin(), items.end(), [](const W& a, const W& b) {
-    if (a.wide != b.wide) return a.wide;
-    return a.cost > b.cost;
-  });
-  std::vector<int32_t> mq, mptr{0}, mparts;
+  // wide items first, each class by cost descending, ties in creation order (the
+  // order of a stable sort), as an index sort: no temporary buffer
+  auto& order = S.order;
+  order.resize(items.size());
+  int64_t maxc = 0;
+  bool small = true;
+  for (const auto& it : items) {
+    maxc = std::max(maxc, it.cost);
+    small = small && it.cost >= 0;
+  }
+  if (small && maxc <= (1 << 16)) {
+    // counting sort on (wide first, cost descending), items in creation order
+    // within a key: the stable order in two linear passes
+    auto& cnt = S.pfill;   // reused scratch
+    const int64_t nk = 2 * (maxc + 1);
+    cnt.assign((size_t)nk + 1, 0);
+    auto key = [&](const W& it) { return (it.wide ? 0 : maxc + 1) + (maxc - it.cost); };
+    for (const auto& it : items) cnt[key(it) + 1]++;
+    for (int64_t k = 0; k < nk; ++k) cnt[k + 1] += cnt[k];
+    for (size_t i = 0; i < items.size(); ++i) order[cnt[key(items[i])]++] = (int32_t)i;
+  } else {
+    for (size_t i = 0; i < items.size(); ++i) order[i] = (int32_t)i;
+    std::sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
+      const W& x = items[a];
+      const W& y = items[b];
+      if (x.wide != y.wide) return x.wide;
+      if (x.cost != y.cost) return x.cost > y.cost;
+      return a < b;
+    });
+  }
+  auto& mq = S.mq;
+  auto& mptr = S.mptr;
+  auto& mparts = S.mparts;
+  mq.clear();
+  mparts.clear();
+  mptr.assign(1, 0);
   for (int q = 0; q < num_queries; ++q) {
     if (direct_q[q]) continue;
     mq.push_back(q);
@@ -135,8 +179,8 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
   std::memset(plan, 0, BE_PLAN_HEADER_INTS * sizeof(int32_t));
   std::memcpy(plan, &in, sizeof(in));
   int32_t* p = plan + BE_PLAN_HEADER_INTS;
-  for (auto& it : items) {
-    std::memcpy(p, &it.w, sizeof(be_attn_work));
+  for (int32_t i : order) {
+    std::memcpy(p, &items[i].w, sizeof(be_attn_work));
     p += 8;
   }
   auto put = [&](const std::vector<int32_t>& v) {
@@ -177,8 +221,12 @@ int plan_groups(const std::vector<Grp>& groups, const std::vector<int32_t>& gq,
     return (int)std::max<int64_t>(page_size, (t + page_size - 1) / page_size * page_size);
   };
   const int balanced = round_pages((total_cost + target_items - 1) / target_items);
-  std::vector<W> items;
-  std::vector<int32_t> qlist;
+  static thread_local std::vector<W> items_tls;
+  static thread_local std::vector<int32_t> qlist_tls;
+  std::vector<W>& items = items_tls;
+  std::vector<int32_t>& qlist = qlist_tls;
+  items.clear();
+  qlist.clear();
   for (const auto& gr : groups) {
     if (gr.kv_len <= 0 || gr.qlen <= 0) continue;  // empty KV: lse = -inf, contributes nothing
     const bool causal = gr.causal;
@@ -250,8 +298,14 @@ extern "C" int be_cascade_plan(int num_levels, const int32_t* const* qo_indptr,
     set_error("be_cascade_plan: group size %d > 64 unsupported", g);
     return BE_EINVAL;
   }
-  std::vector<Grp> groups;
-  std::vector<int32_t> kvlist, gq;
+  static thread_local std::vector<Grp> groups_tls;
+  static thread_local std::vector<int32_t> kvlist_tls, gq_tls;
+  std::vector<Grp>& groups = groups_tls;
+  std::vector<int32_t>& kvlist = kvlist_tls;
+  std::vector<int32_t>& gq = gq_tls;
+  groups.clear();
+  kvlist.clear();
+  gq.clear();
   for (int l = 0; l < num_levels; ++l) {
     const int G = num_groups[l];
     const int base = (int)kvlist.size();
