@@ -415,6 +415,17 @@ class BeamState:
                                     _lib.addr(buf), cap)
         return ptr, buf[:total]
 
+    def get_best_finished(self, num_return: int) -> List[BeamCandidate]:
+        """beam_state.py:635-644: the best finished candidates (else the best
+        active ones) by score / length.  The reference reads ``candidate.length``,
+        which its BeamCandidate does not have (an AttributeError whenever a
+        candidate exists); the length here is the candidate's sequence length."""
+        pool = self.finished_candidates or self.candidates
+
+        def norm(c):
+            return c.score / max(1, len(self.sequence(c.trie_node._id)))
+        return sorted(pool, key=norm, reverse=True)[:num_return]
+
     def get_final_sequences(self, num_return: int, length_penalty: float = 1.0
                             ) -> List[Tuple[List[int], float]]:
         res = []

@@ -416,3 +416,14 @@ def test_native_pages_twice_check_matches_python(trajectories, cascade_trees):
         lv = t["expect"]["levels"]
         assert cascade_counts_pages_twice(lv) == cascade_counts_pages_twice_py(lv)
     assert seen == {True, False}
+
+
+def test_get_best_finished_ranks_active_by_score_per_token():
+    pt = cpu_table(4, 32)
+    bs = BeamState(3, pt)
+    bs.add_root_sequence([1, 2, 3])
+    bs.update_native(bs.leaves, np.array([0, 3], np.int32), np.array([7, 8, 9], np.int32),
+                     np.array([-1.0, -2.0, -0.5]))
+    best = bs.get_best_finished(2)
+    # all sequences have 4 tokens: order by score
+    assert [c.score for c in best] == [-0.5, -1.0]
