@@ -45,6 +45,17 @@ inline int wide_chunk_override() {
   return v;
 }
 
+// BE_ATTN_WIDE_RUNS=1: wide items keep their creation order (each group's chunks
+// adjacent, so the persistent kernel's contiguous task ranges form long runs)
+// instead of being sorted by cost.
+inline bool wide_runs_order() {
+  static const bool v = [] {
+    const char* e = getenv("BE_ATTN_WIDE_RUNS");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 // Wide tiles hold up to 64 rows, narrow tiles 16 (rows = queries x group size).
 inline int tile_queries(int qlen, int g) {
   if (qlen * g <= 16) return qlen;
@@ -112,17 +123,21 @@ int emit_plan(std::vector<W>& items, const std::vector<int32_t>& qlist,
     auto& cnt = S.pfill;   // reused scratch
     const int64_t nk = 2 * (maxc + 1);
     cnt.assign((size_t)nk + 1, 0);
-    auto key = [&](const W& it) { return (it.wide ? 0 : maxc + 1) + (maxc - it.cost); };
+    const bool keep_wide = wide_runs_order();
+    auto key = [&](const W& it) {
+      return it.wide ? (keep_wide ? 0 : maxc - it.cost) : maxc + 1 + (maxc - it.cost);
+    };
     for (const auto& it : items) cnt[key(it) + 1]++;
     for (int64_t k = 0; k < nk; ++k) cnt[k + 1] += cnt[k];
     for (size_t i = 0; i < items.size(); ++i) order[cnt[key(items[i])]++] = (int32_t)i;
   } else {
     for (size_t i = 0; i < items.size(); ++i) order[i] = (int32_t)i;
+    const bool keep_wide = wide_runs_order();
     std::sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
       const W& x = items[a];
       const W& y = items[b];
       if (x.wide != y.wide) return x.wide;
-      if (x.cost != y.cost) return x.cost > y.cost;
+      if (!(x.wide && keep_wide) && x.cost != y.cost) return x.cost > y.cost;
       return a < b;
     });
   }

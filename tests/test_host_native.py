@@ -427,3 +427,56 @@ def test_get_best_finished_ranks_active_by_score_per_token():
     best = bs.get_best_finished(2)
     # all sequences have 4 tokens: order by score
     assert [c.score for c in best] == [-0.5, -1.0]
+
+
+_RUNS_ORDER_SCRIPT = r"""
+import json, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + '/tests')
+from test_host_native import cpu_table, plan_token_sets
+from beam_engine_b200.beam_state import BeamState
+from beam_engine_b200.cascade import cascade_plan_host
+rng = np.random.default_rng(0)
+pt = cpu_table(16, 2048)
+bs = BeamState(16, pt)
+for _ in range(2):
+    bs.add_root_sequence(rng.integers(0, 1000, 1000).tolist())
+bs.update_native(bs.leaves, np.array([0, 16, 32], np.int32),
+                 rng.integers(0, 1000, 32).astype(np.int32), -rng.random(32))
+seg = np.array([0, 16, 32])
+out = []
+for step in range(6):
+    n = len(bs.leaves)
+    info, plan = cascade_plan_host(bs.cascade_levels(), n, 16, 32, 8, causal=True)
+    wk = plan[info.off_work:info.off_work + 8 * info.n_work].reshape(-1, 8)
+    out.append(dict(tokens={str(k): v for k, v in plan_token_sets(plan, info, 16).items()},
+                    wide=[[int(x) for x in w] for w in wk[:info.n_work_wide]]))
+    vals = -np.sort(rng.random((n, 32)) * 3, axis=1)
+    idx = rng.integers(0, 1000, (n, 32)).astype(np.int32)
+    seg = bs.vanilla_step(seg, idx, vals, 16)
+print(json.dumps(out))
+"""
+
+
+def test_wide_runs_order_keeps_the_attention():
+    """BE_ATTN_WIDE_RUNS=1 keeps wide items in creation order (each group's
+    chunks adjacent): every query attends the same tokens as with the cost
+    order, and consecutive wide items of one group have adjoining ranges."""
+    import json
+    import subprocess
+    import sys
+    runs = {}
+    for flag in ("0", "1"):
+        env = dict(os.environ, BE_ATTN_WIDE_RUNS=flag)
+        r = subprocess.run([sys.executable, "-c", _RUNS_ORDER_SCRIPT, ROOT], env=env,
+                           capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        runs[flag] = json.loads(r.stdout)
+    adjoining = 0
+    for a, b in zip(runs["0"], runs["1"]):
+        assert a["tokens"] == b["tokens"]
+        w = b["wide"]
+        for x, y in zip(w, w[1:]):   # q_off, q_len, kv_off, kv_begin, kv_end, ...
+            if x[0] == y[0] and x[2] == y[2] and x[4] == y[3]:
+                adjoining += 1
+    assert adjoining > 0
