@@ -480,3 +480,21 @@ def test_wide_runs_order_keeps_the_attention():
             if x[0] == y[0] and x[2] == y[2] and x[4] == y[3]:
                 adjoining += 1
     assert adjoining > 0
+
+
+def test_ctypes_bindings_match_header_arities():
+    """Every ctypes binding declares as many arguments as the header prototype
+    (a mismatch passes garbage through the ABI without any error)."""
+    src = open(os.path.join(ROOT, "include", "beam_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    protos = {}
+    for m in re.finditer(r"\b(be_\w+)\s*\(([^;{]*?)\)\s*;", src, flags=re.S):
+        args = m.group(2).strip()
+        protos[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    sigs = _lib._SIGS
+    checked = 0
+    for name, (_, argtypes) in sigs.items():
+        assert name in protos, name
+        assert len(argtypes) == protos[name], (name, len(argtypes), protos[name])
+        checked += 1
+    assert checked > 30
