@@ -498,3 +498,18 @@ def test_ctypes_bindings_match_header_arities():
         assert len(argtypes) == protos[name], (name, len(argtypes), protos[name])
         checked += 1
     assert checked > 30
+
+
+def test_ctypes_return_types_match_header():
+    import ctypes as C
+    src = open(os.path.join(ROOT, "include", "beam_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    want = {"int": C.c_int, "int64_t": C.c_int64, "void*": C.c_void_p, "be_trie*": C.c_void_p,
+            "be_comm*": C.c_void_p, "const char*": C.c_char_p, "void": None}
+    for m in re.finditer(r"^\s*((?:const\s+)?\w+\s*\*?)\s*(be_\w+)\s*\(", src, flags=re.M):
+        ret = re.sub(r"\s+", " ", m.group(1)).strip().replace(" *", "*")
+        name = m.group(2)
+        if name not in _lib._SIGS or ret == "typedef":
+            continue
+        assert ret in want, (name, ret)
+        assert _lib._SIGS[name][0] is want[ret], (name, ret, _lib._SIGS[name][0])
