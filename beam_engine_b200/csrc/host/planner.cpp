@@ -45,6 +45,17 @@ inline int wide_chunk_override() {
   return v;
 }
 
+// Tokens per causal (prefill) wide chunk when > 0 (BE_PLAN_CAUSAL_WIDE_CHUNK,
+// e.g. 128: the chunks then fit the resident tcgen05 tile, which masks causally);
+// 0 = balance the split like any other group.
+inline int causal_wide_chunk() {
+  static const int v = [] {
+    const char* e = getenv("BE_PLAN_CAUSAL_WIDE_CHUNK");
+    return e ? std::max(0, atoi(e)) : 0;
+  }();
+  return v;
+}
+
 // BE_ATTN_WIDE_RUNS=1: wide items keep their creation order (each group's chunks
 // adjacent, so the persistent kernel's contiguous task ranges form long runs)
 // instead of being sorted by cost.
@@ -259,6 +270,8 @@ int plan_groups(const std::vector<Grp>& groups, const std::vector<int32_t>& gq,
         if (wide_chunk_override() > 0)
           chunk = std::min(round_pages(wide_chunk_override()), BE_UMMA_MAX_TOKENS);
       }
+      if (wide && causal && causal_wide_chunk() > 0)
+        chunk = std::min(chunk, std::max(page_size, causal_wide_chunk() / page_size * page_size));
       const int nsplit = (gr.kv_len + chunk - 1) / chunk;
       chunk = round_pages((gr.kv_len + nsplit - 1) / nsplit);
     }

@@ -324,7 +324,7 @@ def plan_token_sets(plan, info, ps, slots=None):
     ql = plan[info.off_qlist:]
     kv = plan[info.off_kvlist:]
     out = {}
-    for q_off, q_len, kv_off, b, e, _, _, flags in wk:
+    for q_off, q_len, kv_off, b, e, kv_total, _, flags in wk:
         toks = []
         for t in range(b, e):
             if flags & 2:
@@ -332,7 +332,8 @@ def plan_token_sets(plan, info, ps, slots=None):
             else:
                 toks.append(int(kv[kv_off + t // ps]) * ps + t % ps)
         for i in range(q_len):
-            out.setdefault(int(ql[q_off + i]), []).extend(toks)
+            lim = kv_total - q_len + i + 1 if flags & 1 else e   # causal: t < lim
+            out.setdefault(int(ql[q_off + i]), []).extend(toks[:max(0, min(e, lim) - b)])
     return {q: sorted(v) for q, v in out.items()}
 
 
@@ -513,3 +514,45 @@ def test_ctypes_return_types_match_header():
             continue
         assert ret in want, (name, ret)
         assert _lib._SIGS[name][0] is want[ret], (name, ret, _lib._SIGS[name][0])
+
+
+_PREFILL_PLAN_SCRIPT = r"""
+import json, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + '/tests')
+from test_host_native import plan_token_sets
+from beam_engine_b200.cascade import cascade_plan_host
+rng = np.random.default_rng(1)
+lens = [1000, 300, 1024, 77]
+qo, kvp, kvi, last = [0], [0], [], []
+perm = rng.permutation(4096).tolist()
+for L in lens:
+    m = -(-L // 16)
+    kvi += perm[:m]; perm = perm[m:]
+    kvp.append(len(kvi)); qo.append(qo[-1] + L); last.append(L - (m - 1) * 16)
+lv = [dict(qo_indptr=qo, kv_indptr=kvp, kv_indices=kvi, kv_last_page_len=last)]
+info, plan = cascade_plan_host(lv, qo[-1], 16, 32, 8, causal=True)
+print(json.dumps(dict(max_wide=int(info.max_wide_tokens),
+                      tokens={str(k): v for k, v in plan_token_sets(plan, info, 16).items()})))
+"""
+
+
+def test_causal_wide_chunk_cap_keeps_the_attention():
+    """BE_PLAN_CAUSAL_WIDE_CHUNK=128 splits prefill (causal) wide groups into
+    chunks the tcgen05 tile takes; every query still attends exactly its causal
+    prefix."""
+    import json
+    import subprocess
+    import sys
+    res = {}
+    for cap in ("0", "128"):
+        env = dict(os.environ, BE_PLAN_CAUSAL_WIDE_CHUNK=cap)
+        r = subprocess.run([sys.executable, "-c", _PREFILL_PLAN_SCRIPT, ROOT], env=env,
+                           capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        res[cap] = json.loads(r.stdout)
+    assert res["128"]["max_wide"] <= 128 < res["0"]["max_wide"]
+    assert res["0"]["tokens"] == res["128"]["tokens"]
+    # and each query's set is its own causal prefix: position j of a prompt sees j + 1 tokens
+    t = res["128"]["tokens"]
+    assert len(t["0"]) == 1 and len(t["999"]) == 1000 and len(t["1000"]) == 1
