@@ -159,7 +159,8 @@ def check(rc, what=""):
 
 def addr(arr):
     """Address of a contiguous numpy array, for arguments bound as void* (half
-    the cost of ptr32 on the per-step host path)."""
+    the cost of ptr32 on the per-step host path).  A plain int: unlike ptr32 it
+    does not keep the array alive, so pass a named array, never a temporary."""
     return arr.ctypes.data
 
 

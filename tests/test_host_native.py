@@ -556,3 +556,37 @@ def test_causal_wide_chunk_cap_keeps_the_attention():
     # and each query's set is its own causal prefix: position j of a prompt sees j + 1 tokens
     t = res["128"]["tokens"]
     assert len(t["0"]) == 1 and len(t["999"]) == 1000 and len(t["1000"]) == 1
+
+
+def test_new_entry_points_reject_bad_arguments():
+    """Argument checks of the newer C entry points run before any device work:
+    bad calls return BE_EINVAL with a message (no GPU needed)."""
+    import ctypes as C
+    L = _lib.lib()
+    z = np.zeros(16, np.int32)
+    # tree page plan: a vnode whose range does not start a page
+    slots = np.arange(64, dtype=np.int32) + 3          # slot 3 is not a page start
+    info = _lib.AttnPlanInfo()
+    one, qlen, kvlen = (np.array([x], np.int32) for x in (0, 1, 20))
+    rc = L.be_tree_plan_pages(1, _lib.addr(one), 1, _lib.addr(one), _lib.addr(qlen),
+                              _lib.addr(one), _lib.addr(kvlen), _lib.addr(slots),
+                              len(slots), 1, 16, 32, 8, 148, None, 0, C.byref(info))
+    assert rc == _lib.BE_EINVAL and b"page aligned" in L.be_last_error()
+    # peer all-reduce: no communicator / bad world
+    h = (C.c_char * 64)()
+    out = C.c_void_p()
+    assert L.be_comm_create(9, 0, 1024, 2, 8, h, C.byref(out)) == _lib.BE_EINVAL
+    assert L.be_comm_create(2, 2, 1024, 2, 8, h, C.byref(out)) == _lib.BE_EINVAL
+    assert L.be_comm_allreduce_rmsnorm(None, 0, None, None, _lib.addr(z), 1, 8, 1e-6,
+                                       _lib.BE_BF16, None) == _lib.BE_EINVAL
+    assert L.be_comm_slot(None, 0) is None
+    # fork list: null list
+    assert L.be_fork_tail_copy_list(_lib.addr(z), 16, 1, 4, 16, 1, 8, _lib.BE_BF16, None, 4, 148,
+                                    None) == _lib.BE_EINVAL
+    # fused select + update: no beams
+    seg = np.array([0, 0], np.int32)
+    assert L.be_beam_select_update(None, 1, _lib.addr(seg), 2, None, None,
+                                   None, None, 0, None, None, None, None, None, None, None, None,
+                                   None) == _lib.BE_EINVAL
+    # exactness check: negative level count
+    assert L.be_cascade_pages_twice(-1, None, None, None, None, 0) == -_lib.BE_EINVAL
