@@ -428,15 +428,15 @@ class BeamState:
 
     def get_final_sequences(self, num_return: int, length_penalty: float = 1.0
                             ) -> List[Tuple[List[int], float]]:
-        res = []
-        for c in self.finished_candidates:
-            res.append((self.sequence(c.trie_node._id), c.score))
-        for leaf, sc in zip(self._leaves, self._scores):
-            res.append((self.sequence(int(leaf)), float(sc)))
-        out = []
-        for seq, sc in res:
-            if length_penalty != 0 and len(seq) > 1:
-                sc = sc / (len(seq) ** length_penalty)
-            out.append((seq, sc))
-        out.sort(key=lambda x: x[1], reverse=True)
-        return out[:num_return]
+        # rank by the length-penalised score first (lengths are one native call
+        # each), then materialise only the sequences that are returned
+        nodes = [c.trie_node._id for c in self.finished_candidates] + [int(x) for x in self._leaves]
+        raw = [c.score for c in self.finished_candidates] + [float(x) for x in self._scores]
+        ranked = []
+        for node, sc in zip(nodes, raw):
+            n = lib().be_node_sequence(self._t, node, None, 0)
+            if length_penalty != 0 and n > 1:
+                sc = sc / (n ** length_penalty)
+            ranked.append((node, sc))
+        ranked.sort(key=lambda x: x[1], reverse=True)   # stable: ties keep candidate order
+        return [(self.sequence(node), sc) for node, sc in ranked[:num_return]]
