@@ -236,7 +236,9 @@ class DiverseBeamSearchStrategy(BeamStrategy):
         if self.early_stopping:
             if len(beam_state.leaves) == 0:
                 return True
-            if all(c.finished for c in beam_state.candidates):
+            # candidates only carry a finished flag once a caller materialised them
+            objs = getattr(beam_state, "_cand_objs", None)
+            if objs is not None and all(c.finished for c in objs):
                 return True
         if len(beam_state.finished_candidates) >= beam_state.beam_size:
             return True
