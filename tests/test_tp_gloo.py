@@ -146,3 +146,48 @@ def test_vocab_parallel_topk_uneven_slices():
     # and the size-1 path is the plain one
     v1, i1 = vocab_parallel_log_softmax_topk(logits, 12, 0, None)
     assert torch.equal(i1, ref_i) and torch.allclose(v1, ref_v)
+
+
+def _failing_worker(rank, port, q):
+    """Rank 1 dies before the step's first collective; rank 0 must get an error
+    from the collective within the process group's timeout, not hang."""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=4))
+    from beam_engine_b200.parallel import TensorParallel, vocab_parallel_log_softmax_topk
+    tp = TensorParallel()
+    tp.all_reduce(torch.ones(8))         # one good step: the ranks' connections are up
+    def say(msg):                        # flush the queue before the hard exit
+        q.put((rank, msg))
+        q.close()
+        q.join_thread()
+
+    if rank == 1:
+        say("left")
+        os._exit(0)                      # a rank that disappears between steps
+    import time
+    t0 = time.time()
+    try:
+        logits = torch.randn(4, 100)
+        vocab_parallel_log_softmax_topk(logits, 4, 0, tp)
+        say("no error")
+    except Exception as e:   # the collective reports the dead peer
+        say(f"error after {time.time() - t0:.1f}s: {type(e).__name__}")
+    os._exit(0)
+
+
+def test_rank_failure_surfaces_as_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1] == "left"
+    assert res[0].startswith("error after"), res[0]
+    assert float(res[0].split()[2].rstrip("s:")) < 60
