@@ -22,6 +22,7 @@
 // No TMA, no multicast: peers' memory is only touched by plain loads/stores.
 #include "common.cuh"
 
+#include <cstring>
 #include <vector>
 
 namespace be {
@@ -210,6 +211,7 @@ struct be_comm {
   char* base = nullptr;         // this rank's allocation
   char* peer[COMM_MAX_RANKS] = {};
   bool opened[COMM_MAX_RANKS] = {};
+  cudaIpcMemHandle_t own;       // this rank's handle (a peer given it maps to this buffer)
 };
 
 static size_t comm_flags_bytes(int max_ctas) {
@@ -236,7 +238,8 @@ extern "C" int be_comm_create(int world, int rank, int64_t slot_bytes, int num_s
   cudaError_t e = cudaMalloc(&c->base, total);
   if (e == cudaSuccess) e = cudaMemset(c->base, 0, c->flags_bytes);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
-  if (e == cudaSuccess) e = cudaIpcGetMemHandle((cudaIpcMemHandle_t*)handle_out, c->base);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&c->own, c->base);
+  if (e == cudaSuccess) std::memcpy(handle_out, &c->own, sizeof(c->own));
   if (e != cudaSuccess) {
     set_error("be_comm_create: %s", cudaGetErrorString(e));
     if (c->base) cudaFree(c->base);
@@ -256,6 +259,10 @@ extern "C" int be_comm_open(be_comm* c, const void* handles) {
   const auto* h = reinterpret_cast<const cudaIpcMemHandle_t*>(handles);
   for (int p = 0; p < c->world; ++p) {
     if (p == c->rank || c->opened[p]) continue;
+    if (std::memcmp(&h[p], &c->own, sizeof(c->own)) == 0) {
+      c->peer[p] = c->base;   // loopback: this rank's own buffer stands in for rank p
+      continue;
+    }
     void* ptr = nullptr;
     cudaError_t e = cudaIpcOpenMemHandle(&ptr, h[p], cudaIpcMemLazyEnablePeerAccess);
     if (e != cudaSuccess) {
@@ -267,6 +274,8 @@ extern "C" int be_comm_open(be_comm* c, const void* handles) {
   }
   return BE_OK;
 }
+
+extern "C" void* be_comm_flags(be_comm* c) { return c ? c->base : nullptr; }
 
 extern "C" void* be_comm_slot(be_comm* c, int slot) {
   if (!c || slot < 0 || slot >= c->num_slots) return nullptr;

@@ -452,6 +452,11 @@ int be_comm_create(int world, int rank, int64_t slot_bytes, int num_slots, int m
 int be_comm_open(be_comm* comm, const void* handles);
 /* Device address of this rank's slot (where the GEMM writes its partial).    */
 void* be_comm_slot(be_comm* comm, int slot);
+/* Device address of this rank's incoming flag array: uint32 [max_ctas][8],
+ * entry [cta][r] = the call count rank r last signalled for that CTA.  A
+ * handle equal to this rank's own (be_comm_open) maps this rank's buffer in
+ * that rank's place (loopback, for tests on one GPU).                        */
+void* be_comm_flags(be_comm* comm);
 /* Unmap the other ranks' allocations (after the last call on every rank).    */
 int be_comm_close_peers(be_comm* comm);
 /* Free this rank's allocation -- after every other rank closed its mapping of
