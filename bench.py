@@ -245,12 +245,19 @@ def run_b200(args, rank, world, local_rank):
     gen2_t0 = torch.cuda.Event(enable_timing=True)
     gen2_t1 = torch.cuda.Event(enable_timing=True)
     h2d0 = gen.h2d_bytes
+    gen2_pre = torch.cuda.Event(enable_timing=True)
+
+    def mark_prefill_done(i):   # decode step 0 starts: prefill + root expansion are queued
+        if i == 0:
+            gen2_pre.record()
+
     gen2_t0.record()
     t0 = time.perf_counter()
-    out = gen.generate_ids(prompts, BEAM, max_new_tokens=NEW_TOKENS)
+    out = gen.generate_ids(prompts, BEAM, max_new_tokens=NEW_TOKENS, on_step=mark_prefill_done)
     gen2_t1.record()
     torch.cuda.synchronize()
     e2e_ms = gen2_t0.elapsed_time(gen2_t1)
+    prefill_ms = gen2_t0.elapsed_time(gen2_pre)
     wall_ms = (time.perf_counter() - t0) * 1e3
     t = torch.tensor([e2e_ms], device=dev)
     if world > 1:
@@ -301,7 +308,9 @@ def run_b200(args, rank, world, local_rank):
                 "h2d_bytes_per_step": int((gen.h2d_bytes - h2d0) / steps_e2e),
                 "d2h_bytes_per_step": d2h,
                 "includes": "prefill of 8 x 1024 prompt tokens + 127 decode steps, host ids in, "
-                            "host beams out", "wall_ms": round(wall_ms, 1)},
+                            "host beams out", "wall_ms": round(wall_ms, 1),
+                "prefill_ms": round(prefill_ms, 2)},
+        "sequence_tokens_per_s": round(value / BEAM, 2),
         "gpu_launches": launches["n"],
         "graph_captures": [round(x * 1e3, 1) for x in gen.graph_captures],   # ms, whole run
         "churn": round(float(np.mean(churn)), 3) if churn else None,
