@@ -413,7 +413,7 @@ class BeamSearchGenerator:
         d_ids, d_pos, d_wp, d_wpos, d_rows = self._to_device(
             [cat(ids), cat(pos), cat(wpage), cat(wpos), rows])
         self.attn.plan_levels([dict(qo_indptr=qo, kv_indptr=kvp, kv_indices=pages_all,
-                                    kv_last_page_len=last)], len(ids), causal=True)
+                                    kv_last_page_len=last)], qo[-1], causal=True)
         logits = self.model.forward(d_ids.long(), d_pos, self.page_table, d_wp, d_wpos, self.attn,
                                     logits_rows=d_rows.long())
         return logits

@@ -159,40 +159,60 @@ def test_pick_kernel_host_side(tree_pages):
 
 
 @pytest.mark.parametrize("ps", [16, 4])
-def test_prefill_inputs(ps):
-    """The prefill's device inputs: token ids, positions, each token's page and
-    in-page slot along its prompt's root chain, and the last row of every prompt."""
-    from beam_engine_b200.beam_state import BeamState
-
-    class Captured(Exception):
-        pass
+@pytest.mark.parametrize("lens", [(37, 16, 5, 64), (1,), (16, 1, 17), (200,)])
+def test_prefill_inputs(ps, lens):
+    """The prefill's inputs and its plan: token ids, positions, each token's page
+    and in-page slot along its prompt's root chain, the last row of every
+    prompt, and the causal plan the native planner (be_cascade_plan, host code)
+    builds from them.  Only the device copy and the model forward are stubbed,
+    so every query of the plan must attend exactly positions 0..t of its own
+    prompt (modeling_llama.py:213-283, prompt attention)."""
+    from beam_engine_b200.beam_state import BeamState, TrieNode
+    from beam_engine_b200.cascade import cascade_plan_host
+    from test_host_native import plan_token_sets
 
     gen = FakeGenerator(VanillaBeamSearchStrategy(), ps, 4096)
     got = {}
+    gen._to_device = lambda arrays: [torch.from_numpy(np.asarray(a).copy()) for a in arrays]
 
-    def to_device(arrays):
-        got["a"] = [np.asarray(a).copy() for a in arrays]
-        raise Captured()
+    class Attn:
+        def plan_levels(self, levels, num_queries, causal=True, split_tokens=0):
+            got["plan"] = cascade_plan_host(levels, num_queries, ps, 8, 2, causal=causal)
+            got["num_queries"] = num_queries
 
-    gen._to_device = to_device
+    class Model:
+        def forward(self, ids, pos, pt, wp, wpos, attn, logits_rows=None):
+            got["a"] = [t.numpy() for t in (ids, pos, wp, wpos, logits_rows)]
+            return "logits"
+
+    gen.attn = Attn()
+    gen.model = Model()
     st = BeamState(4, gen.page_table)
     rng = np.random.default_rng(1)
-    prompts = [rng.integers(0, 1000, n).tolist() for n in (37, 16, 5, 64)]
-    with pytest.raises(Captured):
-        BeamSearchGenerator.prefill(gen, st, prompts)
+    prompts = [rng.integers(0, 1000, n).tolist() for n in lens]
+    assert BeamSearchGenerator.prefill(gen, st, prompts) == "logits"
     ids, pos, wp, wpos, rows = got["a"]
     want = [[], [], [], []]
+    want_sets = {}
     for leaf, pr in zip(st.leaves, prompts):
         chain = []
-        from beam_engine_b200.beam_state import TrieNode
         node = TrieNode(trie=st._t, node_id=int(leaf), _owner=gen.page_table)
         while node is not None:
             chain.append(node.page_id)
             node = node.parent
         pages = chain[::-1]
+        base = len(want[0])
+        slots = [pages[i // ps] * ps + i % ps for i in range(len(pr))]
+        for t in range(len(pr)):
+            want_sets[base + t] = sorted(slots[:t + 1])
         want[0] += pr
         want[1] += list(range(len(pr)))
         want[2] += [pages[i // ps] for i in range(len(pr))]
         want[3] += [i % ps for i in range(len(pr))]
     assert [a.tolist() for a in (ids, pos, wp, wpos)] == want
     assert rows.tolist() == (np.cumsum([len(p) for p in prompts]) - 1).tolist()
+    total = sum(lens)
+    assert got["num_queries"] == total
+    info, plan = got["plan"]
+    assert info.n_queries == total
+    assert plan_token_sets(plan, info, ps) == want_sets
