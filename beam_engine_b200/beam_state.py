@@ -389,8 +389,15 @@ class BeamState:
                 torch.tensor(wp, device=dev), torch.tensor(wpos, device=dev))
 
     # -- beam_state.py:646-682 ----------------------------------------------
+    def _seq_len(self, node: int) -> int:
+        n = lib().be_node_sequence(self._t, int(node), None, 0)
+        if n < 0:
+            raise ValueError(f"unknown trie node {node}: "
+                             f"{lib().be_last_error().decode(errors='replace')}")
+        return n
+
     def sequence(self, leaf: int) -> List[int]:
-        n = lib().be_node_sequence(self._t, int(leaf), None, 0)
+        n = self._seq_len(leaf)
         buf = np.zeros(max(n, 1), np.int32)
         lib().be_node_sequence(self._t, int(leaf), _lib.ptr32(buf), n)
         return buf[:n].tolist()
@@ -434,7 +441,7 @@ class BeamState:
         raw = [c.score for c in self.finished_candidates] + [float(x) for x in self._scores]
         ranked = []
         for node, sc in zip(nodes, raw):
-            n = lib().be_node_sequence(self._t, node, None, 0)
+            n = self._seq_len(node)
             if length_penalty != 0 and n > 1:
                 sc = sc / (n ** length_penalty)
             ranked.append((node, sc))

@@ -320,95 +320,130 @@ def run_b200(args, rank, world, local_rank):
     return res
 
 
-def cpu_baseline_sample(threads=None, layers_timed=2):
-    """The oracle (CPU restatement of the reference engine) on a bounded sample
-    of one cfg3 decode step: `layers_timed` decoder layers over all 128 beams
-    (cascade attention over 8 x 1024-token prefixes + suffixes), the lm_head and
-    top-k / selection once; scaled to 32 layers."""
-    import numpy as np
-    import torch
-    from beam_engine_b200.configs import LLAMA3_8B
-    from oracle.attention import cascade_attention
-    from oracle.llama import rmsnorm, silu
-    n_threads = threads or os.cpu_count()
-    torch.set_num_threads(n_threads)
-    cfg = LLAMA3_8B
-    rng = np.random.default_rng(0)
-    H, F, D, Hq, Hkv, V = (cfg["hidden_size"], cfg["intermediate_size"], cfg["head_dim"],
-                           cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["vocab_size"])
-    N = PROMPTS * BEAM
-    # synthetic decode state: per prompt 64 prefix pages, per beam 1-4 suffix pages
-    P = PROMPTS * 64 + N * 4 + 8
-    pool = rng.standard_normal((P, 2, PAGE, Hkv, D), dtype=np.float32)
-    lv0 = dict(qo_indptr=[i * BEAM for i in range(PROMPTS + 1)],
-               kv_indptr=[i * 64 for i in range(PROMPTS + 1)],
-               kv_indices=list(range(PROMPTS * 64)), kv_last_page_len=[PAGE] * PROMPTS)
-    kvp, kvi, last, nxt = [0], [], [], PROMPTS * 64
-    for b in range(N):
-        n = 1 + b % 4
-        kvi += list(range(nxt, nxt + n))
-        nxt += n
-        kvp.append(len(kvi))
-        last.append(1 + b % PAGE)
-    lv1 = dict(qo_indptr=list(range(N + 1)), kv_indptr=kvp, kv_indices=kvi, kv_last_page_len=last)
+class CpuDecodeSample:
+    """The oracle (CPU restatement of the reference engine) on one cfg3 decode
+    step's state: 128 beams, cascade over 8 x 1024-token prefixes plus 1-4 page
+    suffixes, one decoder layer's weights (every layer of the 8B shape has the
+    same shape and cost) and the lm_head.  ``layer()`` runs one decoder layer
+    over all beams (RMSNorm, q/k/v, cascade attention, o_proj, SwiGLU MLP);
+    ``head()`` the final log-softmax + top-2W.  A full step is 32 layers + head."""
 
-    def w(*s):
-        return (rng.standard_normal(s, dtype=np.float32) * 0.02)
-    wq, wk, wv, wo = w(Hq * D, H), w(Hkv * D, H), w(Hkv * D, H), w(H, Hq * D)
-    wg, wu, wd = w(F, H), w(F, H), w(H, F)
-    x = rng.standard_normal((N, H), dtype=np.float32)
-    ones = np.ones(H, np.float32)
-    t_layers = []
-    for _ in range(layers_timed):
-        t0 = time.perf_counter()
-        h = rmsnorm(x, ones, 1e-5)
-        q = (h @ wq.T).reshape(N, Hq, D)
-        _k = h @ wk.T
-        _v = h @ wv.T
-        a = cascade_attention(q, pool, [lv0, lv1], PAGE, D ** -0.5).astype(np.float32)
-        x2 = x + a.reshape(N, -1) @ wo.T
-        h = rmsnorm(x2, ones, 1e-5)
-        m = silu(h @ wg.T) * (h @ wu.T)
-        _ = x2 + m.astype(np.float32) @ wd.T
-        t_layers.append(time.perf_counter() - t0)
-    del wq, wk, wv, wo, wg, wu, wd
-    lm = w(V, H)
-    t0 = time.perf_counter()
-    logits = h @ lm.T
-    lp = logits - logits.max(-1, keepdims=True)
-    lp = lp - np.log(np.exp(lp).sum(-1, keepdims=True))
-    np.argpartition(-lp, 2 * BEAM, axis=-1)[:, :2 * BEAM]
-    t_head = time.perf_counter() - t0
-    step_s = statistics.mean(t_layers) * cfg["num_hidden_layers"] + t_head
-    return {"value": round(N / step_s, 3), "unit": "beam tokens/s", "cores": n_threads,
+    def __init__(self, threads=None):
+        import numpy as np
+        import torch
+        from beam_engine_b200.configs import LLAMA3_8B
+        self.threads = threads or os.cpu_count()
+        torch.set_num_threads(self.threads)
+        cfg = LLAMA3_8B
+        rng = np.random.default_rng(0)
+        H, F, D, Hq, Hkv, V = (cfg["hidden_size"], cfg["intermediate_size"], cfg["head_dim"],
+                               cfg["num_attention_heads"], cfg["num_key_value_heads"],
+                               cfg["vocab_size"])
+        self.L, self.D, self.Hq = cfg["num_hidden_layers"], D, Hq
+        N = self.N = PROMPTS * BEAM
+        P = PROMPTS * 64 + N * 4 + 8
+        self.pool = rng.standard_normal((P, 2, PAGE, Hkv, D), dtype=np.float32)
+        lv0 = dict(qo_indptr=[i * BEAM for i in range(PROMPTS + 1)],
+                   kv_indptr=[i * 64 for i in range(PROMPTS + 1)],
+                   kv_indices=list(range(PROMPTS * 64)), kv_last_page_len=[PAGE] * PROMPTS)
+        kvp, kvi, last, nxt = [0], [], [], PROMPTS * 64
+        for b in range(N):
+            n = 1 + b % 4
+            kvi += list(range(nxt, nxt + n))
+            nxt += n
+            kvp.append(len(kvi))
+            last.append(1 + b % PAGE)
+        lv1 = dict(qo_indptr=list(range(N + 1)), kv_indptr=kvp, kv_indices=kvi,
+                   kv_last_page_len=last)
+        self.levels = [lv0, lv1]
+
+        def w(*sh):
+            return rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02)
+        self.wq, self.wk, self.wv, self.wo = w(Hq * D, H), w(Hkv * D, H), w(Hkv * D, H), w(H, Hq * D)
+        self.wg, self.wu, self.wd = w(F, H), w(F, H), w(H, F)
+        self.lm = w(V, H)
+        self.x = rng.standard_normal((N, H), dtype=np.float32)
+        self.ones = np.ones(H, np.float32)
+        self.h = self.x
+
+    def layer(self):
+        import numpy as np
+        from oracle.attention import cascade_attention
+        from oracle.llama import rmsnorm, silu
+        N, D, Hq = self.N, self.D, self.Hq
+        x = self.x
+        h = rmsnorm(x, self.ones, 1e-5)
+        q = (h @ self.wq.T).reshape(N, Hq, D)
+        _k = h @ self.wk.T
+        _v = h @ self.wv.T
+        a = cascade_attention(q, self.pool, self.levels, PAGE, D ** -0.5).astype(np.float32)
+        x2 = x + a.reshape(N, -1) @ self.wo.T
+        h = rmsnorm(x2, self.ones, 1e-5)
+        m = silu(h @ self.wg.T) * (h @ self.wu.T)
+        self.h = h
+        return x2 + m.astype(np.float32) @ self.wd.T
+
+    def head(self):
+        import numpy as np
+        logits = self.h @ self.lm.T
+        lp = logits - logits.max(-1, keepdims=True)
+        lp = lp - np.log(np.exp(lp).sum(-1, keepdims=True))
+        return np.argpartition(-lp, 2 * BEAM, axis=-1)[:, :2 * BEAM]
+
+    def timed(self, fn, n):
+        out = []
+        for _ in range(n):
+            t0 = time.perf_counter()
+            fn()
+            out.append(time.perf_counter() - t0)
+        return out
+
+
+SAMPLE_TEXT = ("one decoder layer of a cfg3 decode step per sample (128 beams: q/k/v, cascade over "
+               "8 x 1024-token prefixes + 1-4 page suffixes, o_proj, SwiGLU MLP), numpy oracle fp32; "
+               "a full step = 32 layers + lm_head/log-softmax/top-2W (timed once)")
+
+
+def cpu_baseline_sample(threads=None, layers_timed=2):
+    """cpu_baseline of the decode bench line: ``layers_timed`` decoder layers
+    and one head of the oracle, one full step extrapolated from them."""
+    smp = CpuDecodeSample(threads)
+    smp.layer()                                   # warm-up (page faults, BLAS threads)
+    lay = smp.timed(smp.layer, layers_timed)
+    head = smp.timed(smp.head, 1)[0]
+    step_s = statistics.mean(lay) * smp.L + head
+    return {"value": round(smp.N / step_s, 3), "unit": "beam tokens/s", "cores": smp.threads,
             "kind": "port",
-            "sample": f"{layers_timed} of 32 decoder layers of one cfg3 decode step (128 beams, "
-                      "cascade over 8 x 1024 prefixes + 1-4 page suffixes) + lm_head/top-k once, "
-                      "numpy oracle fp32, scaled to 32 layers",
+            "sample": f"{layers_timed} timed layers + 1 head; " + SAMPLE_TEXT,
             "step_s": round(step_s, 3)}
 
 
 def run_reference(args, rank, world):
+    """--impl reference: the CPU restatement of the reference engine, every
+    warm-up and timed step one bounded sample (one decoder layer over the full
+    cfg3 decode state).  ms_per_step is the measured time of one sample; value
+    is the beam-token throughput of a full step built from the measured layer
+    and head times (32 layers + head), reported with that full-step time."""
     if rank != 0:
         return None
-    import numpy as np
-    warm = cpu_baseline_sample(layers_timed=1)
-    vals = []
-    for _ in range(max(1, min(args.steps, 3))):
-        vals.append(cpu_baseline_sample(layers_timed=1)["step_s"])
-    step_s = statistics.mean(vals)
-    value = PROMPTS * BEAM / step_s
-    base = dict(warm)
-    base["value"] = round(value, 3)
-    base["sample"] += f"; {len(vals)} timed samples after 1 warm-up"
+    smp = CpuDecodeSample()
+    head = smp.timed(smp.head, 1)[0]
+    smp.timed(smp.layer, max(args.warmup, 0))
+    lay = smp.timed(smp.layer, max(args.steps, 1))
+    layer_s = statistics.mean(lay)
+    step_s = layer_s * smp.L + head
+    value = smp.N / step_s
+    base = {"value": round(value, 3), "unit": "beam tokens/s", "cores": smp.threads, "kind": "port",
+            "sample": f"{len(lay)} timed samples after {args.warmup} warm-up; " + SAMPLE_TEXT}
     return {
         "metric": METRIC, "value": round(value, 3), "unit": "beam tokens/s", "n_gpus": world,
-        "steps": len(vals), "warmup": 1, "ms_per_step": round(step_s * 1e3, 1),
+        "steps": len(lay), "warmup": args.warmup, "ms_per_step": round(layer_s * 1e3, 2),
+        "step_is": "one bounded sample (one decoder layer over all 128 beams)",
+        "full_step_ms": round(step_s * 1e3, 1), "head_ms": round(head * 1e3, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": "cfg3: Llama-3-8B shape, 8 prompts x 1024 tokens, beam width 16, "
-                               "128 new tokens, page size 16, cascade attention",
-                   "model": "Llama-3-8B-shape (random init)", "global_batch": PROMPTS * BEAM,
+        "config": {"workload": WORKLOAD,
+                   "model": f"{MODEL_NAME} shape (random init)", "global_batch": PROMPTS * BEAM,
                    "seq_len": PROMPT_LEN, "parallelism": "cpu"},
         "cpu_baseline": base,
         "e2e": {"value": round(value, 3), "unit": "beam tokens/s", "h2d_bytes_per_step": 0,
