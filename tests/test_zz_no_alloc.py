@@ -6,7 +6,8 @@ two scratch buffers it needs for partial rows.  be_attn_run_noalloc keeps those
 rows in an array built into the library instead.  This test calls it through
 the C ABI and checks it against be_attn_run (caller-provided scratch) on two
 calls in a row, with the attention tolerance the other tests use (2e-2 in
-bf16).  It lives in its own file, collected last, and needs nothing from the
+bf16), and both against the fp64 cascade oracle (the reference's
+MultiLevelCascadeAttentionWrapper semantics, modeling_llama.py:321-367).  It lives in its own file, collected last, and needs nothing from the
 other tests, so it also passes alone in a fresh process."""
 import ctypes as C
 
@@ -45,7 +46,13 @@ def test_noalloc_matches_caller_scratch_twice():
     Hq, Hkv, D, ps, P, W = 32, 8, 128, 16, 1024, 16
     g = torch.Generator().manual_seed(21)
     pool = torch.randn((P, 2, ps, Hkv, D), generator=g).to(torch.bfloat16).to(d)
-    info, plan = cascade_plan_host(_levels(g, P, W), W, ps, Hq, Hkv, causal=True)
+    from oracle.attention import cascade_attention
+    levels = _levels(g, P, W)
+    info, plan = cascade_plan_host(levels, W, ps, Hq, Hkv, causal=True)
+    used = sorted({p for x in levels for p in x["kv_indices"]})   # compacted pool for the oracle
+    at = {p: i for i, p in enumerate(used)}
+    pool_c = pool[torch.tensor(used, device=d)].double().cpu().numpy()
+    lv_c = [dict(x, kv_indices=[at[p] for p in x["kv_indices"]]) for x in levels]
     assert info.n_parts > 0 and info.n_merge > 0          # the path that needs scratch
     plan_dev = torch.from_numpy(plan).to(d)
     mid_o = torch.empty(info.n_parts * Hq * D, dtype=torch.float32, device=d)
@@ -65,6 +72,9 @@ def test_noalloc_matches_caller_scratch_twice():
         torch.cuda.synchronize()
         err = (got.float() - ref.float()).abs().max().item()
         assert err <= BF16_ATOL, (call, err)
+        want = cascade_attention(q.double().cpu().numpy(), pool_c, lv_c, ps, D ** -0.5)
+        err_o = float(np.abs(got.float().cpu().numpy() - want).max())
+        assert err_o <= BF16_ATOL, (call, err_o)
 
 
 def test_noalloc_rejects_plans_beyond_its_scratch():
