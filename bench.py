@@ -566,6 +566,38 @@ def run_op_bench(args):
     fork1_us = timeit(lambda: fork(1), args.iters) if src_p else 0.0
     forkL_us = timeit(lambda: fork(layers), args.iters) if src_p else 0.0
     fork_bytes = sum(lens) * Hkv * D * 2 * 2 * 2   # K+V, read + write
+    # bandwidth sweep (all layers, one launch): append of SWEEP_TOK tokens to distinct
+    # (page, slot) positions, and SWEEP_COPIES copy-on-write tail copies
+    SWEEP_TOK = min(8192, P2 * ps // 2)
+    sw_i = torch.arange(SWEEP_TOK, dtype=torch.int32, device=dev)
+    sw_pages = (sw_i // ps).contiguous()
+    sw_pos = (sw_i % ps).contiguous()
+    sw_ind = torch.arange(SWEEP_TOK + 1, dtype=torch.int32, device=dev)
+    sw_k = torch.randn((layers, SWEEP_TOK, Hkv, D), device=dev).to(torch.bfloat16)
+    sw_v = torch.randn((layers, SWEEP_TOK, Hkv, D), device=dev).to(torch.bfloat16)
+    # batch b = token i with its own one-page table entry: kv_indices[kv_indptr[i] + pos // ps]
+    # = page, so kv_indices is the per-token page list and kv_indptr[i] = i - pos // ps
+    sw_indptr = (sw_i - sw_pos // ps).contiguous()
+
+    def app_sweep():
+        _lib.check(L.be_append_paged_kv(sw_k.data_ptr(), sw_v.data_ptr(), Hkv * D,
+                                        SWEEP_TOK * Hkv * D, sw_i.data_ptr(), sw_pos.data_ptr(),
+                                        sw_pages.data_ptr(), sw_indptr.data_ptr(), SWEEP_TOK,
+                                        ptL.kv_cache.data_ptr(), ptL.kv_cache.stride(0), layers,
+                                        P2, ps, Hkv, D, _lib.BE_BF16, None))
+    appS_us = timeit(app_sweep, max(3, args.iters // 4))
+    appS_bytes = SWEEP_TOK * 2 * Hkv * D * 2 * 2 * layers
+    n_cp = min(65535 // (2 * layers), P2 // 2)
+    sw_src = torch.randperm(P2 // 2, generator=g)[:n_cp].to(torch.int32).to(dev)
+    sw_dst = (torch.randperm(P2 // 2, generator=g)[:n_cp] + P2 // 2).to(torch.int32).to(dev)
+    sw_len = torch.randint(1, ps, (n_cp,), generator=g).to(torch.int32).to(dev)
+
+    def fork_sweep():
+        _lib.check(L.be_fork_tail_copy(ptL.kv_cache.data_ptr(), ptL.kv_cache.stride(0), layers, P2,
+                                       ps, Hkv, D, _lib.BE_BF16, sw_src.data_ptr(),
+                                       sw_dst.data_ptr(), sw_len.data_ptr(), n_cp, None))
+    forkS_us = timeit(fork_sweep, max(3, args.iters // 4))
+    forkS_bytes = int(sw_len.sum().item()) * Hkv * D * 2 * 2 * 2 * layers
     inf = w._plan.info
 
     def rl(b, us):
@@ -581,6 +613,8 @@ def run_op_bench(args):
         f"append_{layers}layers_1launch": rl(app_bytes * layers, appL_us),
         "fork_1layer": dict(rl(fork_bytes, fork1_us), copies=len(src_p)),
         f"fork_{layers}layers_1launch": rl(fork_bytes * layers, forkL_us),
+        "append_sweep": dict(rl(appS_bytes, appS_us), tokens=SWEEP_TOK, layers=layers),
+        "fork_sweep": dict(rl(forkS_bytes, forkS_us), copies=n_cp, layers=layers),
     }
 
 
