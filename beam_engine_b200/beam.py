@@ -327,9 +327,10 @@ class BeamSearchGenerator:
         self.graph_regrowth = []      # why a step graph was recorded again
         self._graph_warm = False
         self._pending_fork = None     # copies of the last selection, run by the next graph step
-        # tree steps as page-list plans on the tensor-core kernels (BE_TREE_PAGES=1; the slot-list
-        # plan of the general kernel otherwise, or when a tree is not page aligned)
-        self.tree_pages = (os.environ.get("BE_TREE_PAGES", "0") == "1" and page_size == 16
+        # tree steps as page-list plans on the tensor-core kernels (default; BE_TREE_PAGES=0 keeps
+        # the slot-list plan of the general kernel, which also serves trees that are not page
+        # aligned)
+        self.tree_pages = (os.environ.get("BE_TREE_PAGES", "1") == "1" and page_size == 16
                            and self.page_table.store_dtype != torch.float32)
         self.step_graph_tpages = None
         self.h2d_bytes = 0            # host -> device bytes copied by the engine (inputs, plans)
@@ -485,6 +486,8 @@ class BeamSearchGenerator:
                 for key in caps:
                     caps[key] = max(caps[key], sg.caps[key] * 3 // 2)
             self.step_graph_tree = sg = StepGraph(self, n, k, temperature, caps, kind="fasttree")
+        if self.plan_hook is not None:
+            self.plan_hook(n, info)
         h = sg.host_buf.numpy()
         h[0:n], h[n:2 * n], h[2 * n:3 * n], h[3 * n:4 * n] = q, pos, wp, wpos
         self._take_fork(sg)
@@ -503,6 +506,8 @@ class BeamSearchGenerator:
                 for key in caps:
                     caps[key] = max(caps[key], sg.caps[key] * 3 // 2)
             self.step_graph_tpages = sg = StepGraph(self, n, k, temperature, caps, kind="cascade")
+        if self.plan_hook is not None:
+            self.plan_hook(n, info)
         h = sg.host_buf.numpy()
         h[0:n], h[n:2 * n], h[2 * n:3 * n], h[3 * n:4 * n] = q, pos, wp, wpos
         self._take_fork(sg)

@@ -55,6 +55,59 @@ __global__ void __launch_bounds__(256) append_kernel(
   }
 }
 
+// One warp per (layer, token, plane) row: the token's K (or V) row of every KV
+// head is one contiguous run of hkv * row_bytes in the input and in the page
+// slot, so a row is a warp-wide memcpy of 16-byte vectors.  Each lane loads
+// all its vectors of the row before storing any (up to ROW_UNROLL in flight per
+// lane), and the row index is decomposed once per warp in 32-bit arithmetic.
+constexpr int ROW_UNROLL = 8;
+__global__ void __launch_bounds__(256) append_rows_kernel(
+    const char* __restrict__ k, const char* __restrict__ v, int64_t row_stride_b,
+    int64_t in_layer_stride_b, const int32_t* __restrict__ batch_indices,
+    const int32_t* __restrict__ positions, const int32_t* __restrict__ kv_indices,
+    const int32_t* __restrict__ kv_indptr, int nnz, char* __restrict__ pool,
+    int64_t pool_layer_stride_b, int num_pages, int page_size, int tok_vecs /* hkv*row_bytes/16 */,
+    int num_rows /* layers * nnz * 2 */) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < num_rows;
+       row += warps) {
+    const int plane = row & 1;
+    const int li = row >> 1;
+    const int i = li % nnz, layer = li / nnz;
+    int page = 0, pos = 0;
+    if (lane == 0) {
+      pos = positions[i];
+      const int b = batch_indices[i];
+      page = pos >= 0 ? kv_indices[kv_indptr[b] + pos / page_size] : -1;
+    }
+    page = __shfl_sync(0xffffffffu, page, 0);
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+    if (page < 0 || page >= num_pages || pos < 0) {
+      if (lane == 0) flag_range_error();
+      continue;
+    }
+    const int4* src = reinterpret_cast<const int4*>((plane ? v : k) + layer * in_layer_stride_b +
+                                                    i * row_stride_b);
+    int4* dst = reinterpret_cast<int4*>(
+        pool + layer * pool_layer_stride_b +
+        (((int64_t)page * 2 + plane) * page_size + pos % page_size) * (int64_t)tok_vecs * 16);
+    for (int c0 = 0; c0 < tok_vecs; c0 += 32 * ROW_UNROLL) {
+      int4 buf[ROW_UNROLL];
+#pragma unroll
+      for (int u = 0; u < ROW_UNROLL; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < tok_vecs) buf[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < ROW_UNROLL; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < tok_vecs) dst[c] = buf[u];
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Fork: tokens [0, len) of K and V, page src -> page dst, every layer.
 // In one page plane the first `len` tokens are one contiguous run of
@@ -63,24 +116,38 @@ __global__ void __launch_bounds__(256) append_kernel(
 __global__ void __launch_bounds__(256) fork_kernel(
     char* __restrict__ pool, int64_t pool_layer_stride_b, int num_layers, int num_pages,
     int64_t plane_bytes, const int32_t* __restrict__ src_pages,
-    const int32_t* __restrict__ dst_pages, const int32_t* __restrict__ lens, int64_t tok_bytes) {
-  const int seg = blockIdx.y;                  // (copy, layer, plane)
-  const int plane = seg & 1;
-  const int layer = (seg >> 1) % num_layers;
-  const int j = (seg >> 1) / num_layers;
-  const int s = src_pages[j], d = dst_pages[j];
-  const int64_t n16 = (lens[j] * tok_bytes) >> 4;
-  if (s < 0 || s >= num_pages || d < 0 || d >= num_pages) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) flag_range_error();
-    return;
+    const int32_t* __restrict__ dst_pages, const int32_t* __restrict__ lens, int64_t tok_bytes,
+    int num_segs) {
+  // one CTA per (copy, layer, plane) segment at a time (grid-stride); every thread
+  // loads all of its <= ROW_UNROLL vectors of the segment before storing them
+  for (int seg = blockIdx.x; seg < num_segs; seg += gridDim.x) {
+    const int plane = seg & 1;
+    const int layer = (seg >> 1) % num_layers;
+    const int j = (seg >> 1) / num_layers;
+    const int s = src_pages[j], d = dst_pages[j];
+    const int n16 = (int)((lens[j] * tok_bytes) >> 4);
+    if (s < 0 || s >= num_pages || d < 0 || d >= num_pages) {
+      if (threadIdx.x == 0) flag_range_error();
+      continue;
+    }
+    const int4* s4 = reinterpret_cast<const int4*>(pool + layer * pool_layer_stride_b +
+                                                   ((int64_t)s * 2 + plane) * plane_bytes);
+    int4* d4 = reinterpret_cast<int4*>(pool + layer * pool_layer_stride_b +
+                                       ((int64_t)d * 2 + plane) * plane_bytes);
+    for (int c0 = 0; c0 < n16; c0 += 256 * ROW_UNROLL) {
+      int4 buf[ROW_UNROLL];
+#pragma unroll
+      for (int u = 0; u < ROW_UNROLL; ++u) {
+        const int c = c0 + u * 256 + threadIdx.x;
+        if (c < n16) buf[u] = __ldg(s4 + c);
+      }
+#pragma unroll
+      for (int u = 0; u < ROW_UNROLL; ++u) {
+        const int c = c0 + u * 256 + threadIdx.x;
+        if (c < n16) d4[c] = buf[u];
+      }
+    }
   }
-  const char* src = pool + layer * pool_layer_stride_b + ((int64_t)s * 2 + plane) * plane_bytes;
-  char* dst = pool + layer * pool_layer_stride_b + ((int64_t)d * 2 + plane) * plane_bytes;
-  const int4* s4 = reinterpret_cast<const int4*>(src);
-  int4* d4 = reinterpret_cast<int4*>(dst);
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < n16;
-       c += (int64_t)gridDim.x * blockDim.x)
-    d4[c] = __ldg(s4 + c);
 }
 
 }  // namespace be
@@ -126,7 +193,16 @@ extern "C" int be_append_paged_kv(const void* append_key, const void* append_val
   auto* k = (const char*)append_key;
   auto* v = (const char*)append_value;
   auto* pool = (char*)paged_kv_cache;
-  if (vec == 16)
+  const int64_t tok_b = (int64_t)num_kv_heads * row_bytes;
+  const int64_t rows = (int64_t)num_layers * nnz * 2;
+  if (vec == 16 && tok_b / 16 <= (1 << 20) && rows < (1ll << 31)) {
+    // 8 warps per CTA, one row per warp, grid capped at 16 CTAs per SM
+    const int64_t want_r = (rows + 7) / 8;
+    const int blocks_r = (int)(want_r < 148 * 16 ? want_r : 148 * 16);
+    append_rows_kernel<<<blocks_r, 256, 0, st>>>(k, v, rs, ls, batch_indices, positions,
+                                                 kv_indices, kv_indptr, nnz, pool, ps, num_pages,
+                                                 page_size, (int)(tok_b / 16), (int)rows);
+  } else if (vec == 16)
     append_kernel<16><<<blocks, threads, 0, st>>>(k, v, rs, ls, batch_indices, positions, kv_indices,
                                                   kv_indptr, nnz, pool, ps, num_layers, num_pages,
                                                   page_size, num_kv_heads, row_bytes, chunks);
@@ -159,18 +235,18 @@ extern "C" int be_fork_tail_copy(void* paged_kv_cache, int64_t pool_layer_stride
     return BE_EINVAL;
   }
   const int64_t segs = (int64_t)num_copies * num_layers * 2;
-  if (segs > 65535) {
+  if (segs >= (1ll << 31)) {
     set_error("be_fork_tail_copy: too many copies x layers (%lld segments)", (long long)segs);
     return BE_EINVAL;
   }
-  const int64_t max16 = (page_size * tok_bytes) >> 4;
-  const int threads = 256;
-  int bx = (int)((max16 + threads * 2 - 1) / (threads * 2));
-  if (bx < 1) bx = 1;
-  dim3 grid(bx, (unsigned)segs);
-  fork_kernel<<<grid, threads, 0, (cudaStream_t)stream>>>(
+  if (((int64_t)page_size * tok_bytes) >> 4 >= (1ll << 31)) {
+    set_error("be_fork_tail_copy: page too large");
+    return BE_EINVAL;
+  }
+  const int grid = (int)(segs < 148 * 8 ? segs : 148 * 8);
+  fork_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
       (char*)paged_kv_cache, pool_layer_stride * elt, num_layers, num_pages, page_size * tok_bytes,
-      src_pages, dst_pages, lens, tok_bytes);
+      src_pages, dst_pages, lens, tok_bytes, (int)segs);
   BE_LAUNCH_CHECK();
   return BE_OK;
 }

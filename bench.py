@@ -307,8 +307,8 @@ def run_b200(args, rank, world, local_rank):
         "e2e": {"value": round(e2e_tokens / (e2e_ms / 1e3), 2), "unit": "beam tokens/s",
                 "h2d_bytes_per_step": int((gen.h2d_bytes - h2d0) / steps_e2e),
                 "d2h_bytes_per_step": d2h,
-                "includes": "prefill of 8 x 1024 prompt tokens + 127 decode steps, host ids in, "
-                            "host beams out", "wall_ms": round(wall_ms, 1),
+                "includes": f"prefill of {PROMPTS} x {PROMPT_LEN} prompt tokens + {NEW_TOKENS - 1} "
+                            "decode steps, host ids in, host beams out", "wall_ms": round(wall_ms, 1),
                 "prefill_ms": round(prefill_ms, 2)},
         "sequence_tokens_per_s": round(value / BEAM, 2),
         "gpu_launches": launches["n"],

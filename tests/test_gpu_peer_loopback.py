@@ -2,18 +2,14 @@
 "peer" is this process's own buffer): the fused sum + residual add + RMSNorm
 against torch when the other rank's flag is preset, and the bounded flag wait
 when nothing ever sets it (BE_EDEVICE_TIMEOUT after ~2 s, context still
-usable).  Experimental: runs only with BE_PEER_AR_TEST=1 until it has passed
-on a B200 once."""
+usable)."""
 import ctypes as C
-import os
 import time
 
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("BE_PEER_AR_TEST") != "1",
-                                 reason="experimental path: set BE_PEER_AR_TEST=1")]
+pytestmark = pytest.mark.gpu
 
 
 def _comm(world=2, slot_bytes=1 << 20, max_ctas=64):

@@ -1,16 +1,12 @@
 """Tree decode steps as page-list plans on the tensor-core kernels
 (BE_TREE_PAGES=1) select the same beams as the slot-list tree plans of the
-general kernel, eager and from the step graph.  Experimental: runs only with
-BE_TREE_PAGES_TEST=1 until it has passed on a B200 once."""
-import os
+general kernel, eager and from the step graph."""
 
 import numpy as np
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("BE_TREE_PAGES_TEST") != "1",
-                                 reason="experimental path: set BE_TREE_PAGES_TEST=1")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("graph", [False, True])

@@ -1,19 +1,14 @@
 """The persistent wide kernel with run accumulation (BE_ATTN_WIDE_RUNS=1:
 consecutive chunks of one group accumulate in the CTA before one partial row is
 written) against the dense fp32 reference, on plans whose groups span many
-chunks.  Experimental: runs only with BE_ATTN_WIDE_RUNS_TEST=1 until it has
-passed on a B200 once (device code that has never run is kept off the shared
-GPUs' default test pass)."""
-import os
+chunks."""
 
 import pytest
 import torch
 
 from test_gpu_wide import ATOL, LSE_ATOL, dense_reference, dev, prompts_with_beams, run_plan
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("BE_ATTN_WIDE_RUNS_TEST") != "1",
-                                 reason="experimental path: set BE_ATTN_WIDE_RUNS_TEST=1")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
