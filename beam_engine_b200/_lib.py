@@ -17,7 +17,7 @@ P32 = C.POINTER(C.c_int32)
 PP32 = C.POINTER(P32)
 
 (BE_OK, BE_EINVAL, BE_ENOMEM, BE_ECUDA, BE_ENOT_ALLOCATED, BE_ECAPACITY, BE_EDEVICE_RANGE,
- BE_EDEVICE_TIMEOUT) = range(8)
+ BE_EDEVICE_TIMEOUT, BE_ENOTSUP) = range(9)
 BE_F32, BE_F16, BE_BF16 = 0, 1, 2
 BE_CAPS_SLOTS = 1
 
@@ -27,6 +27,13 @@ class AttnPlanInfo(C.Structure):
         "n_work", "n_work_wide", "n_queries", "n_parts", "n_merge", "off_work", "off_qlist",
         "off_kvlist", "off_merge_q", "off_merge_ptr", "off_merge_parts", "total_ints",
         "page_size", "group_size", "any_slots", "max_item_tokens", "total_tokens", "max_wide_tokens")]
+
+
+class TilePlanInfo(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in (
+        "n_tiles", "n_pieces", "n_entries", "n_queries", "off_tiles", "off_pieces", "off_entries",
+        "total_ints", "page_size", "group_size", "tile_rows", "n_part_pieces", "total_tokens",
+        "max_piece_entries", "cluster", "pad1")]
 
 
 class AttnCaps(C.Structure):
@@ -96,6 +103,14 @@ _SIGS = {
                                              vp, vp]),
     "be_beam_decode_inputs": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp, i64,
                                         C.c_int, C.POINTER(AttnPlanInfo)]),
+    "be_tile_plan": (C.c_int, [C.c_int, PP32, PP32, PP32, PP32, P32, C.c_int, C.c_int, C.c_int,
+                               C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P32, i64,
+                               C.POINTER(TilePlanInfo)]),
+    "be_beam_decode_tiles": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                       C.c_int, vp, i64, C.c_int, C.POINTER(TilePlanInfo)]),
+    "be_attn_tiles_run": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp, i64, vp,
+                                    C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, i64, vp,
+                                    vp, vp, C.c_int, C.c_int, vp]),
     "be_fork_tail_copy_list": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                          C.c_int, vp, C.c_int, C.c_int, vp]),
     "be_comm_create": (C.c_int, [C.c_int, C.c_int, i64, C.c_int, C.c_int, vp, C.POINTER(vp)]),

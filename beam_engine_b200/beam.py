@@ -27,7 +27,7 @@ from . import _lib
 from ._lib import check, lib
 from .beam_state import BeamState
 from .beam_strategy import VanillaBeamSearchStrategy
-from .cascade import _Plan
+from .cascade import _Plan, target_pieces, tile_rows_for, tiles_eligible
 from .page_table import PageTable, stream_ptr
 from .parallel import vocab_parallel_log_softmax_topk
 
@@ -74,6 +74,21 @@ class PlannedAttention:
         ng = _i32([len(a) - 1 for a in arrs[0]])
         ptrs = [(_lib.P32 * max(L, 1))(*[_lib.ptr32(a) for a in grp]) for grp in arrs]
         m, ps, p = self.m, self.pt.page_size, self.plan
+        self.kv_list = None
+        if (split_tokens == 0 and self.pt.store_dtype != torch.float32
+                and tiles_eligible(m.D, ps, m.Hq, m.Hkv)):
+            g = m.Hq // m.Hkv
+            qo0 = arrs[0][0] if L else np.zeros(1, np.int32)
+            rows = tile_rows_for(int(np.max(np.diff(qo0))) * g if len(qo0) > 1 else g)
+            tp = target_pieces(p.num_sms, m.Hkv)
+
+            def tfn(buf, cap, info):
+                return lib().be_tile_plan(L, *ptrs, _lib.ptr32(ng), num_queries, ps, m.Hq, m.Hkv,
+                                          1 if causal else 0, rows, tp, -1,
+                                          C.cast(buf, _lib.P32), cap, info)
+            if p.build_tiles(tfn):
+                p.place_tiles(m.Hkv, m.D)
+                return
 
         def fn(buf, cap, info):
             return lib().be_cascade_plan(L, *ptrs, _lib.ptr32(ng), num_queries, ps, m.Hq, m.Hkv,
@@ -81,11 +96,12 @@ class PlannedAttention:
                                          C.cast(buf, _lib.P32), cap, info)
         p.build(fn)
         p.place(m.Hq, m.D)
-        self.kv_list = None
+        p.tinfo = None
 
     def plan_prebuilt(self, info, buf):
         """Place a plan built elsewhere (a page-list tree plan)."""
         p = self.plan
+        p.tinfo = None
         p.info = info
         host = torch.from_numpy(np.ascontiguousarray(buf[:info.total_ints]))
         if p.copied is not None:          # previous H2D still reading the staging buffer
@@ -100,6 +116,7 @@ class PlannedAttention:
         from .fasttree import build_tree_plan
         info, buf = build_tree_plan(vnodes, batch_size, self.pt.page_size, self.m.Hq, self.m.Hkv)
         p = self.plan
+        p.tinfo = None
         p.info = info
         host = torch.from_numpy(buf)
         if p.copied is not None:          # previous H2D still reading the staging buffer
@@ -116,6 +133,13 @@ class PlannedAttention:
         if t is not None:
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
+        if self.plan.tinfo is not None:
+            self.plan.run_tiles(qkv[:, :m.Hq * m.D].view(-1, m.Hq, m.D), self.pt.kv_cache[layer],
+                                m.Hq, m.Hkv, m.D, self.scale, out.view(-1, m.Hq, m.D))
+            if t is not None:
+                e.record()
+                t.append((s, e))
+            return
         rc = lib().be_attn_run(
             C.c_void_p(self.plan.plan_dev), C.byref(self.plan.info), qkv.data_ptr(), qkv.stride(0),
             self.pt.kv_cache[layer].data_ptr(), self.pt.max_num_pages, m.Hq, m.Hkv, m.D,
@@ -166,14 +190,21 @@ class StepGraph:
         self.total = self.slots_off + self.caps["slots"]
         self.dev_buf = torch.zeros(self.total, dtype=torch.int32, device=dev)
         self.host_buf = torch.empty(self.total, dtype=torch.int32).pin_memory()
-        self.mid_o = torch.empty(max(1, self.caps["parts"]) * m.Hq * m.D, dtype=torch.float32,
-                                 device=dev)
-        self.mid_lse = torch.empty(max(1, self.caps["parts"]) * m.Hq, dtype=torch.float32,
-                                   device=dev)
+        if kind == "tiles":
+            # partial rows [part pieces][kv heads][tile rows][D] + LSE
+            slots = max(1, self.caps["part_pieces"]) * m.Hkv * self.caps["rows"]
+            self.mid_o = torch.empty(slots * m.D, dtype=m.dtype, device=dev)
+            self.mid_lse = torch.empty(slots, dtype=torch.float32, device=dev)
+        else:
+            self.mid_o = torch.empty(max(1, self.caps["parts"]) * m.Hq * m.D,
+                                     dtype=torch.float32, device=dev)
+            self.mid_lse = torch.empty(max(1, self.caps["parts"]) * m.Hq, dtype=torch.float32,
+                                       device=dev)
         self.vals_h = torch.empty(n * k, dtype=torch.float32).pin_memory()
         self.idx_h = torch.empty(n * k, dtype=torch.int64).pin_memory()
-        self.ccaps = _lib.AttnCaps(self.caps["work"], self.caps["wide"], self.caps["merge"], 1,
-                                   _lib.BE_CAPS_SLOTS if kind == "fasttree" else 0)
+        if kind != "tiles":
+            self.ccaps = _lib.AttnCaps(self.caps["work"], self.caps["wide"], self.caps["merge"], 1,
+                                       _lib.BE_CAPS_SLOTS if kind == "fasttree" else 0)
         # suffix tiles on a second stream, overlapping the shared-prefix tiles
         self.side = (torch.cuda.Stream(dev) if os.environ.get("BE_ATTN_TWO_STREAMS", "1") != "0"
                      else None)
@@ -191,6 +222,11 @@ class StepGraph:
 
     def fits(self, n, k, temperature, info, n_slots=0):
         c = self.caps
+        if self.kind == "tiles":
+            return (n == self.n and k == self.k and temperature == self.temp
+                    and info.n_pieces <= c["pieces"] and info.n_tiles <= c["tiles"]
+                    and info.n_part_pieces <= c["part_pieces"] and info.total_ints <= c["ints"]
+                    and info.tile_rows == c["rows"] and info.cluster == c["cluster"])
         return (n == self.n and k == self.k and temperature == self.temp
                 and info.n_work <= c["work"] and info.n_work_wide <= c["wide"]
                 and info.n_merge <= c["merge"] and info.n_parts <= c["parts"]
@@ -214,6 +250,17 @@ class StepGraph:
     def run(self, layer, qkv, out):  # attention of one layer (the model calls this)
         m, pt = self.gen.model, self.gen.page_table
         self._mark(2 * layer, qkv)
+        if self.kind == "tiles":
+            c = self.caps
+            rc = lib().be_attn_tiles_run(
+                self.dev_buf.data_ptr() + 4 * self.plan_off, c["pieces"], c["tiles"],
+                c["part_pieces"], c["rows"], pt.page_size, qkv.data_ptr(), qkv.stride(0),
+                pt.kv_cache[layer].data_ptr(), pt.max_num_pages, m.Hq, m.Hkv, m.D, m.dt,
+                m.D ** -0.5, out.data_ptr(), out.stride(0), None, self.mid_o.data_ptr(),
+                self.mid_lse.data_ptr(), c["cluster"], 1, stream_ptr(qkv.device))
+            check(rc, "be_attn_tiles_run")
+            self._mark(2 * layer + 1, qkv)
+            return
         rc = lib().be_attn_run_fixed_2s(
             self.dev_buf.data_ptr() + 4 * self.plan_off, C.byref(self.ccaps), pt.page_size,
             qkv.data_ptr(), qkv.stride(0), pt.kv_cache[layer].data_ptr(), pt.max_num_pages, m.Hq,
@@ -333,6 +380,11 @@ class BeamSearchGenerator:
         self.tree_pages = (os.environ.get("BE_TREE_PAGES", "1") == "1" and page_size == 16
                            and self.page_table.store_dtype != torch.float32)
         self.step_graph_tpages = None
+        self.step_graph_tiles = None
+        # cascade steps on the beam-tile kernel (BE_ATTN_TILES=0: the work-item kernels)
+        self.use_tiles = (self.page_table.store_dtype != torch.float32
+                          and tiles_eligible(model.D, page_size, model.Hq, model.Hkv))
+        self._beam_width = 1
         self.h2d_bytes = 0            # host -> device bytes copied by the engine (inputs, plans)
 
     # ------------------------------------------------------------------
@@ -546,6 +598,10 @@ class BeamSearchGenerator:
         self._tree_stash = None
         if not self.use_graph or kind != "cascade":
             return self._topk(self.decode_step(state, kind), k, temperature)
+        if self.use_tiles:
+            got = self._tiles_graph_step(state, k, temperature)
+            if got is not None:
+                return got
         m = self.model
         n = len(state.leaves)
         leaves = np.ascontiguousarray(state.leaves, np.int32)
@@ -598,6 +654,79 @@ class BeamSearchGenerator:
         self._take_fork(sg)
         return sg.step_filled(sg.plan_off + info.total_ints)
 
+    def _tiles_graph_step(self, state: BeamState, k: int, temperature: float):
+        """A cascade decode step on the beam-tile kernel, replayed from its graph.
+        None when the step's plan is not a decode shape (the caller plans work items)."""
+        m = self.model
+        n = len(state.leaves)
+        leaves = np.ascontiguousarray(state.leaves, np.int32)
+        info = _lib.TilePlanInfo()
+        rows = tile_rows_for(self._beam_width * (m.Hq // m.Hkv))
+        tp = target_pieces(self.attn.plan.num_sms, m.Hkv)
+        sg = self.step_graph_tiles
+
+        same = sg is not None and sg.n == n and sg.k == k and sg.temp == temperature
+
+        def fill(buf_ptr, cap, plan_off, cluster):
+            rc = lib().be_beam_decode_tiles(self.page_table._trie, n, _lib.addr(leaves), m.Hq,
+                                            m.Hkv, rows, tp, cluster, C.c_void_p(buf_ptr), cap,
+                                            plan_off, C.byref(info))
+            if rc == _lib.BE_ENOTSUP:
+                return None
+            if rc not in (_lib.BE_OK, _lib.BE_ECAPACITY):
+                check(rc, "be_beam_decode_tiles")
+            return rc == _lib.BE_OK
+
+        # the graph's cluster size is part of its recorded launch: keep it while the
+        # shape stays (the planner chooses it for a new graph)
+        ok = same and fill(sg.host_buf.data_ptr(), sg.total, sg.plan_off, sg.caps["cluster"])
+        if ok is None:
+            return None
+        if not (ok and sg.fits(n, k, temperature, info)):
+            off = step_plan_offset(n)
+            size = off + 65536
+            cl = sg.caps["cluster"] if same else -1
+            while True:
+                probe = np.empty(size, np.int32)
+                got = fill(probe.ctypes.data, size, off, cl)
+                if got is None:
+                    return None
+                if got:
+                    break
+                size *= 4
+            # headroom: entries grow with the beams' suffixes; pieces and tiles hardly change
+            cl = info.cluster
+            if cl > 1:   # one cluster per (tile, KV head): pieces = tiles x cluster
+                caps = dict(pieces=info.n_pieces, tiles=info.n_tiles, part_pieces=0,
+                            ints=3 * info.total_ints + 64 * n + 4096, rows=info.tile_rows,
+                            cluster=cl)
+            else:
+                caps = dict(pieces=info.n_pieces + 2 * info.n_tiles + tp // 4 + 16,
+                            tiles=2 * info.n_tiles + 8,
+                            part_pieces=info.n_pieces + 2 * info.n_tiles + tp // 4 + 16,
+                            ints=3 * info.total_ints + 64 * n + 4096, rows=info.tile_rows,
+                            cluster=0)
+            # the kernel reads piece records up to max_pieces before the piece count
+            caps["ints"] = max(caps["ints"], 32 + 24 * caps["pieces"] + 64)
+            if sg is not None and sg.n == n and sg.k == k and sg.temp == temperature:
+                got = dict(pieces=info.n_pieces, tiles=info.n_tiles,
+                           part_pieces=info.n_part_pieces, ints=info.total_ints)
+                self.graph_regrowth.append({key: (got[key], sg.caps[key]) for key in got
+                                            if got[key] > sg.caps[key]})
+                for key in ("pieces", "tiles", "part_pieces", "ints"):
+                    if cl <= 1 or key == "ints":
+                        caps[key] = max(caps[key], sg.caps[key] * 3 // 2)
+                caps["ints"] = max(caps["ints"], 32 + 24 * caps["pieces"] + 64)
+            elif sg is not None:
+                self.graph_regrowth.append({"shape": (sg.n, n, sg.k, k)})
+            self.step_graph_tiles = sg = StepGraph(self, n, k, temperature, caps, kind="tiles")
+            if not fill(sg.host_buf.data_ptr(), sg.total, sg.plan_off, cl):
+                raise RuntimeError("decode step graph sized too small for its own plan")
+        if self.plan_hook is not None:
+            self.plan_hook(n, info)
+        self._take_fork(sg)
+        return sg.step_filled(sg.plan_off + info.total_ints)
+
     def generate_ids(self, prompts: List[List[int]], beam_size: int = 4,
                      max_length: Optional[int] = None, max_new_tokens: Optional[int] = None,
                      num_return_sequences: int = 1, temperature: float = 1.0, on_step=None):
@@ -616,6 +745,7 @@ class BeamSearchGenerator:
         else:
             n_steps = max_new_tokens - 1
         W = beam_size
+        self._beam_width = W
         self._pending_fork = None    # copies left by an interrupted earlier call are void
         state = BeamState(W, self.page_table)
         state.defer_copies = True

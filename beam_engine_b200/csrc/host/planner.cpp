@@ -566,3 +566,200 @@ extern "C" int be_cascade_pages_twice(int num_levels, const int32_t* const* qo_i
   }
   return 0;
 }
+
+// ---------------------------------------------------------------------------
+// Beam-tile plans (decode): tiles of consecutive queries, per-tile page entries
+// with query ranges, pieces balanced by pages.
+// ---------------------------------------------------------------------------
+static_assert(sizeof(be_tile_plan_info) <= BE_PLAN_HEADER_INTS * sizeof(int32_t), "tile header");
+static_assert(sizeof(be_attn_tile) == 8 * sizeof(int32_t), "tile layout");
+static_assert(sizeof(be_attn_piece) == 24 * sizeof(int32_t), "piece layout");
+static_assert(sizeof(be_attn_entry) == 4 * sizeof(int32_t), "entry layout");
+
+extern "C" int be_tile_plan(int num_levels, const int32_t* const* qo_indptr,
+                            const int32_t* const* kv_indptr, const int32_t* const* kv_indices,
+                            const int32_t* const* last_page_len, const int32_t* num_groups,
+                            int num_queries, int page_size, int num_qo_heads, int num_kv_heads,
+                            int causal_last, int tile_rows, int target_pieces, int cluster,
+                            int32_t* plan, int64_t plan_capacity, be_tile_plan_info* info) {
+  if (num_levels < 0 || num_queries < 0 || page_size < 1 || num_kv_heads < 1 ||
+      num_qo_heads % num_kv_heads || !info || (tile_rows != 64 && tile_rows != 128) ||
+      cluster < -1 || cluster > 16) {
+    set_error("be_tile_plan: invalid arguments");
+    return BE_EINVAL;
+  }
+  const int g = num_qo_heads / num_kv_heads;
+  const int R = tile_rows / g;   // queries per tile
+  if (R < 1) {
+    set_error("be_tile_plan: group size %d exceeds %d tile rows", g, tile_rows);
+    return BE_ENOTSUP;
+  }
+  const int nq = num_queries;
+  // level checks; a causal last level must be decode-shaped (<= 1 query per group)
+  for (int l = 0; l < num_levels; ++l) {
+    const int G = num_groups[l];
+    if (G < 0) {
+      set_error("be_tile_plan: level %d has a negative group count", l);
+      return BE_EINVAL;
+    }
+    if (G > 0 && (qo_indptr[l][0] != 0 || kv_indptr[l][0] != 0 || qo_indptr[l][G] > nq)) {
+      set_error("be_tile_plan: level %d indptr does not start at 0 or exceeds %d queries", l, nq);
+      return BE_EINVAL;
+    }
+    for (int gi = 0; gi < G; ++gi) {
+      const int qlen = qo_indptr[l][gi + 1] - qo_indptr[l][gi];
+      const int np = kv_indptr[l][gi + 1] - kv_indptr[l][gi];
+      if (qlen < 0 || np < 0) {
+        set_error("be_tile_plan: level %d group %d has negative extent", l, gi);
+        return BE_EINVAL;
+      }
+      const int last = last_page_len[l][gi];
+      if (np > 0 && (last < 0 || last > page_size)) {
+        set_error("be_tile_plan: level %d group %d last_page_len %d outside [0, %d]", l, gi, last,
+                  page_size);
+        return BE_EINVAL;
+      }
+      if (causal_last && l == num_levels - 1 && qlen > 1 && np > 0) {
+        set_error("be_tile_plan: causal group with %d queries (prefill) is not a decode plan",
+                  qlen);
+        return BE_ENOTSUP;
+      }
+    }
+  }
+  // tiles: cut at level-0 group boundaries and every R queries
+  struct TL {
+    std::vector<int32_t> cut, q0, q1, tile_of, ecount, estart, efill, ents;
+  };
+  static thread_local TL S;
+  S.cut.assign(nq + 1, 0);
+  if (num_levels > 0)
+    for (int gi = 0; gi <= num_groups[0]; ++gi) {
+      const int q = qo_indptr[0][gi];
+      if (q >= 0 && q <= nq) S.cut[q] = 1;
+    }
+  S.q0.clear();
+  S.q1.clear();
+  S.tile_of.assign(nq, 0);
+  for (int q = 0; q < nq;) {
+    const int a = q++;
+    while (q < nq && !S.cut[q] && q - a < R) ++q;
+    for (int i = a; i < q; ++i) S.tile_of[i] = (int32_t)S.q0.size();
+    S.q0.push_back(a);
+    S.q1.push_back(q);
+  }
+  const int nt = (int)S.q0.size();
+  // entries: count per tile, then fill (tile-major, levels in order within a tile)
+  S.ecount.assign(nt + 1, 0);
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1) {
+      S.estart.assign(nt + 1, 0);
+      for (int t = 0; t < nt; ++t) S.estart[t + 1] = S.estart[t] + S.ecount[t];
+      S.efill.assign(S.estart.begin(), S.estart.end() - 1);
+      S.ents.resize((size_t)S.estart[nt] * 4);
+    }
+    for (int l = 0; l < num_levels; ++l) {
+      for (int gi = 0; gi < num_groups[l]; ++gi) {
+        const int a = qo_indptr[l][gi], b = std::min(nq, qo_indptr[l][gi + 1]);
+        const int p0 = kv_indptr[l][gi], np = kv_indptr[l][gi + 1] - p0;
+        if (a >= b || np <= 0) continue;
+        for (int j = 0; j < np; ++j) {
+          const int ntok = j == np - 1 ? last_page_len[l][gi] : page_size;
+          if (ntok <= 0) continue;
+          for (int t = S.tile_of[a]; t < nt && S.q0[t] < b; ++t) {
+            if (pass == 0) {
+              S.ecount[t]++;
+            } else {
+              int32_t* e = &S.ents[(size_t)S.efill[t]++ * 4];
+              e[0] = kv_indices[l][p0 + j];
+              e[1] = ntok;
+              e[2] = std::max(a, S.q0[t]) - S.q0[t];
+              e[3] = std::min(b, S.q1[t]) - S.q0[t];
+            }
+          }
+        }
+      }
+    }
+  }
+  const int64_t n_ent = nt ? S.estart[nt] : 0;
+  if (cluster < 0) {
+    // auto: about target_pieces pieces over the tiles; a cluster per (tile, KV head)
+    // when that takes 2..16 pieces per tile, else the merge kernel (1 piece per
+    // tile needs no merge)
+    const int per_tile = nt ? std::max(1, target_pieces) / nt : 1;
+    cluster = per_tile <= 1 ? 0 : (per_tile <= 16 ? per_tile : 0);
+  }
+  // pieces: about target_pieces in all, >= 8 entries (two 4-page chunks) each,
+  // sizes rounded to whole chunks
+  const int64_t per = std::max<int64_t>(8, (n_ent + std::max(1, target_pieces) - 1) /
+                                               std::max(1, target_pieces));
+  static thread_local std::vector<int32_t> tiles, pieces;
+  tiles.assign((size_t)nt * 8, 0);
+  pieces.clear();
+  int n_part = 0, max_pe = 0;
+  int64_t tokens = 0;
+  for (int t = 0; t < nt; ++t) {
+    const int e0 = S.estart[t], e = S.estart[t + 1] - e0;
+    int np, base;
+    if (cluster > 1) {          // exactly `cluster` pieces, trailing ones may be empty
+      np = cluster;
+      base = std::max(4, ((e + np - 1) / np + 3) / 4 * 4);
+    } else {
+      np = (int)std::max<int64_t>(1, (e + per / 2) / per);
+      base = (e + np - 1) / np;
+      base = std::max(4, (base + 3) / 4 * 4);
+      np = std::max(1, (e + base - 1) / base);
+    }
+    int32_t* T = &tiles[(size_t)t * 8];
+    T[0] = S.q0[t];
+    T[1] = S.q1[t] - S.q0[t];
+    T[2] = (int32_t)(pieces.size() / 24);
+    T[3] = np;
+    T[4] = (np > 1 && cluster <= 1) ? n_part : -1;   // clusters merge on chip
+    if (np > 1 && cluster <= 1) n_part += np;
+    for (int k = 0; k < np; ++k) {
+      const int b0 = e0 + std::min(e, k * base), b1 = e0 + std::min(e, (k + 1) * base);
+      pieces.insert(pieces.end(), {t, b0, b1, k, T[0], T[1], T[3], T[4]});
+      for (int j = 0; j < 4; ++j)       // the first chunk's entries, read with the piece
+        for (int f = 0; f < 4; ++f)
+          pieces.push_back(b0 + j < b1 ? S.ents[(size_t)(b0 + j) * 4 + f] : 0);
+      max_pe = std::max(max_pe, b1 - b0);
+    }
+    for (int i = e0; i < e0 + e; ++i) tokens += S.ents[(size_t)i * 4 + 1];
+  }
+  be_tile_plan_info in{};
+  in.n_tiles = nt;
+  in.n_pieces = (int32_t)(pieces.size() / 24);
+  in.n_entries = (int32_t)n_ent;
+  in.n_queries = nq;
+  int64_t off = BE_PLAN_HEADER_INTS;   // pieces first: a CTA finds its piece without the header
+  in.off_pieces = (int32_t)off;
+  off += pieces.size();
+  in.off_tiles = (int32_t)off;
+  off += tiles.size();
+  in.off_entries = (int32_t)off;
+  off += n_ent * 4;
+  if (off > INT32_MAX || tokens > INT32_MAX) {
+    set_error("be_tile_plan: plan too large (%lld ints)", (long long)off);
+    return BE_EINVAL;
+  }
+  in.total_ints = (int32_t)off;
+  in.page_size = page_size;
+  in.group_size = g;
+  in.tile_rows = tile_rows;
+  in.n_part_pieces = n_part;
+  in.total_tokens = (int32_t)tokens;
+  in.max_piece_entries = max_pe;
+  in.cluster = cluster > 1 ? cluster : 0;
+  *info = in;
+  if (off > plan_capacity || !plan) {
+    set_error("plan buffer too small: need %lld ints, have %lld", (long long)off,
+              (long long)plan_capacity);
+    return BE_ECAPACITY;
+  }
+  std::memset(plan, 0, BE_PLAN_HEADER_INTS * sizeof(int32_t));
+  std::memcpy(plan, &in, sizeof(in));
+  if (!tiles.empty()) std::memcpy(plan + in.off_tiles, tiles.data(), tiles.size() * 4);
+  if (!pieces.empty()) std::memcpy(plan + in.off_pieces, pieces.data(), pieces.size() * 4);
+  if (n_ent) std::memcpy(plan + in.off_entries, S.ents.data(), (size_t)n_ent * 16);
+  return BE_OK;
+}

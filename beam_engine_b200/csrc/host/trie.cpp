@@ -1007,6 +1007,51 @@ int be_beam_select_update(be_trie* t, int nseg, const int32_t* seg_ptr, int k,
 // at out[0 .. 4 * ncand) and the attention plan (header included) at
 // out[plan_offset ..).  Semantics: be_beam_step_inputs + be_cascade_build +
 // be_cascade_plan.  BE_ECAPACITY reports the plan size in info->total_ints.
+namespace {
+// The cascade levels of a decode step (be_cascade_build into growable scratch)
+// as per-level array pointers.
+struct StepLevels {
+  std::vector<int32_t> lg, lp, qo, kvp, kvi, last, ng;
+  std::vector<const int32_t*> a_qo, a_kvp, a_kvi, a_last;
+  int nlev = 0;
+};
+int build_step_levels(be_trie* t, int ncand, const int32_t* cand_leaf, StepLevels& L) {
+  int cap_l = 64, cap_g = 64 * (ncand + 1), cap_p = 8192;
+  for (;;) {
+    L.lg.resize(cap_l + 1);
+    L.lp.resize(cap_l + 1);
+    L.qo.resize(cap_g + cap_l);
+    L.kvp.resize(cap_g + cap_l);
+    L.kvi.resize(cap_p);
+    L.last.resize(cap_g);
+    L.nlev = be_cascade_build(t, ncand, cand_leaf, cap_l, cap_g, cap_p, L.lg.data(), L.lp.data(),
+                              L.qo.data(), L.kvp.data(), L.kvi.data(), L.last.data());
+    if (L.nlev == -BE_ECAPACITY) {
+      cap_l *= 2;
+      cap_g *= 2;
+      cap_p *= 4;
+      continue;
+    }
+    if (L.nlev < 0) return -L.nlev;
+    break;
+  }
+  const int nlev = L.nlev;
+  L.a_qo.resize(nlev);
+  L.a_kvp.resize(nlev);
+  L.a_kvi.resize(nlev);
+  L.a_last.resize(nlev);
+  L.ng.resize(nlev);
+  for (int l = 0; l < nlev; ++l) {
+    L.a_qo[l] = L.qo.data() + L.lg[l] + l;
+    L.a_kvp[l] = L.kvp.data() + L.lg[l] + l;
+    L.a_kvi[l] = L.kvi.data() + L.lp[l];
+    L.a_last[l] = L.last.data() + L.lg[l];
+    L.ng[l] = L.lg[l + 1] - L.lg[l];
+  }
+  return BE_OK;
+}
+}  // namespace
+
 int be_beam_decode_inputs(be_trie* t, int ncand, const int32_t* cand_leaf, int num_qo_heads,
                           int num_kv_heads, int num_sms, int32_t* out, int64_t cap,
                           int32_t plan_offset, be_attn_plan_info* info) {
@@ -1018,40 +1063,32 @@ int be_beam_decode_inputs(be_trie* t, int ncand, const int32_t* cand_leaf, int n
   int rc = be_beam_step_inputs(t, ncand, cand_leaf, out, out + 2 * ncand, out + 3 * ncand,
                                out + ncand);
   if (rc) return rc;
-  // cascade levels into growable scratch
-  static thread_local std::vector<int32_t> lg, lp, qo, kvp, kvi, last;
-  int cap_l = 64, cap_g = 64 * (ncand + 1), cap_p = 8192;
-  int nlev;
-  for (;;) {
-    lg.resize(cap_l + 1);
-    lp.resize(cap_l + 1);
-    qo.resize(cap_g + cap_l);
-    kvp.resize(cap_g + cap_l);
-    kvi.resize(cap_p);
-    last.resize(cap_g);
-    nlev = be_cascade_build(t, ncand, cand_leaf, cap_l, cap_g, cap_p, lg.data(), lp.data(),
-                            qo.data(), kvp.data(), kvi.data(), last.data());
-    if (nlev == -BE_ECAPACITY) {
-      cap_l *= 2;
-      cap_g *= 2;
-      cap_p *= 4;
-      continue;
-    }
-    if (nlev < 0) return -nlev;
-    break;
+  static thread_local StepLevels L;
+  rc = build_step_levels(t, ncand, cand_leaf, L);
+  if (rc) return rc;
+  return be_cascade_plan(L.nlev, L.a_qo.data(), L.a_kvp.data(), L.a_kvi.data(), L.a_last.data(),
+                         L.ng.data(), ncand, t->page_size, num_qo_heads, num_kv_heads, 1, 0,
+                         num_sms, out + plan_offset, cap - plan_offset, info);
+}
+
+int be_beam_decode_tiles(be_trie* t, int ncand, const int32_t* cand_leaf, int num_qo_heads,
+                         int num_kv_heads, int tile_rows, int target_pieces, int cluster,
+                         int32_t* out, int64_t cap, int32_t plan_offset,
+                         be_tile_plan_info* info) {
+  if ((int64_t)4 * ncand > plan_offset || plan_offset > cap) {
+    set_error("be_beam_decode_tiles: plan_offset %d too small for %d candidates", plan_offset,
+              ncand);
+    return BE_EINVAL;
   }
-  std::vector<const int32_t*> a_qo(nlev), a_kvp(nlev), a_kvi(nlev), a_last(nlev);
-  std::vector<int32_t> ng(nlev);
-  for (int l = 0; l < nlev; ++l) {
-    a_qo[l] = qo.data() + lg[l] + l;
-    a_kvp[l] = kvp.data() + lg[l] + l;
-    a_kvi[l] = kvi.data() + lp[l];
-    a_last[l] = last.data() + lg[l];
-    ng[l] = lg[l + 1] - lg[l];
-  }
-  return be_cascade_plan(nlev, a_qo.data(), a_kvp.data(), a_kvi.data(), a_last.data(), ng.data(),
-                         ncand, t->page_size, num_qo_heads, num_kv_heads, 1, 0, num_sms,
-                         out + plan_offset, cap - plan_offset, info);
+  int rc = be_beam_step_inputs(t, ncand, cand_leaf, out, out + 2 * ncand, out + 3 * ncand,
+                               out + ncand);
+  if (rc) return rc;
+  static thread_local StepLevels L;
+  rc = build_step_levels(t, ncand, cand_leaf, L);
+  if (rc) return rc;
+  return be_tile_plan(L.nlev, L.a_qo.data(), L.a_kvp.data(), L.a_kvi.data(), L.a_last.data(),
+                      L.ng.data(), ncand, t->page_size, num_qo_heads, num_kv_heads, 1, tile_rows,
+                      target_pieces, cluster, out + plan_offset, cap - plan_offset, info);
 }
 
 }  // extern "C"

@@ -7,6 +7,7 @@
 #include "attention_umma.cu"
 #include "attention_wide.cu"
 #include "attention_narrow.cu"
+#include "attention_tiles.cu"
 #include "attn_api.cu"
 #include "attn_noalloc.cu"
 #include "model_ops.cu"

@@ -164,19 +164,26 @@ def run_b200(args, rank, world, local_rank):
     launches = {"n": 0}
     plan_bytes = []
     plan_stats = []
+    plan_kind = set()
     timing = {"on": False}
     gen.time_attention = True          # per-layer attention events recorded inside the step graph
 
     def plan_hook(nq, inf):
         if timing["on"]:
-            # every work item's token range is read once: K and V of all its tokens, q in, o out
+            # every planned token is read once per KV head: K and V, q in, o out
             plan_bytes.append(inf.total_tokens * 2 * model.Hkv * model.D * 2
                               + 2 * nq * model.Hq * model.D * 2)
-            plan_stats.append((nq, inf.n_work, inf.n_work_wide, inf.n_parts, inf.n_merge))
-            # per layer: 2 add_rmsnorm, rope_append, silu_mul + attention (tcgen05 wide,
-            # all-heads narrow, LSE merge); final norm; fused log-softmax / top-k; the
-            # copy-on-write fork list at the head of the step
-            launches["n"] += cfg["num_hidden_layers"] * (4 + 3) + 1 + 1 + 1
+            tiles = hasattr(inf, "n_pieces")
+            if tiles:
+                plan_stats.append((nq, inf.n_tiles, inf.n_pieces, inf.n_part_pieces,
+                                   inf.n_entries))
+            else:
+                plan_stats.append((nq, inf.n_work, inf.n_work_wide, inf.n_parts, inf.n_merge))
+            plan_kind.add("tiles" if tiles else "items")
+            # per layer: 2 add_rmsnorm, rope_append, silu_mul + attention (one beam-tile
+            # launch, or tcgen05 wide + all-heads narrow + LSE merge); final norm; fused
+            # log-softmax / top-k; the copy-on-write fork list at the head of the step
+            launches["n"] += cfg["num_hidden_layers"] * (4 + (1 if tiles else 3)) + 1 + 1 + 1
 
     gen.plan_hook = plan_hook
     orig_after = gen._after_update
@@ -291,13 +298,17 @@ def run_b200(args, rank, world, local_rank):
                      "frac": round(achieved / hbm, 4),
                      "traffic": round(TRAFFIC_RATIO * bytes_total / max(len(attn_ms), 1)),
                      "traffic_source": TRAFFIC_SOURCE,
-                     "kernel": "be_attn_run_fixed_2s per layer (tcgen05 prefix tiles, all-heads "
-                               "suffix tiles on a second stream, LSE merge), timed by event "
-                               "nodes inside the step graph",
+                     "kernel": ("be_attn_tiles_run per layer (one beam-tile tcgen05 launch, "
+                                "in-kernel LSE merge)" if plan_kind == {"tiles"} else
+                                "be_attn_run_fixed_2s per layer (tcgen05 prefix tiles, all-heads "
+                                "suffix tiles on a second stream, LSE merge)")
+                               + ", timed by event nodes inside the step graph",
                      "peak_source": src,
                      "avg_launch_us": round(attn_total_ms / max(len(attn_ms), 1) * 1e3, 2),
                      "bytes_per_launch": round(bytes_total / max(len(attn_ms), 1)),
-                     "plan_avg": dict(zip(("queries", "work_items", "wide_items", "partial_rows",
+                     "plan_avg": dict(zip(("queries", "tiles", "pieces", "partial_pieces",
+                                           "entries") if plan_kind == {"tiles"} else
+                                          ("queries", "work_items", "wide_items", "partial_rows",
                                            "merged_queries"),
                                           [round(float(np.mean([p[i] for p in plan_stats])), 1)
                                            for i in range(5)])) if plan_stats else None},
@@ -598,7 +609,10 @@ def run_op_bench(args):
                                        sw_dst.data_ptr(), sw_len.data_ptr(), n_cp, None))
     forkS_us = timeit(fork_sweep, max(3, args.iters // 4))
     forkS_bytes = int(sw_len.sum().item()) * Hkv * D * 2 * 2 * 2 * layers
-    inf = w._plan.info
+    inf = w._plan.tinfo if w.tiles else w._plan.info
+    plan_desc = (dict(kind="tiles", tiles=inf.n_tiles, pieces=inf.n_pieces,
+                      entries=inf.n_entries, rows=inf.tile_rows) if w.tiles else
+                 dict(kind="items", work=inf.n_work, wide=inf.n_work_wide, parts=inf.n_parts))
 
     def rl(b, us):
         a = b / (us / 1e6) / 1e9 if us else 0.0
@@ -607,8 +621,7 @@ def run_op_bench(args):
         "config": {"workload": "cfg2 op microbench", "pool_pages": P, "layers_for_multi": layers,
                    "prefix": prefix, "beams": W, "suffix_tokens": suf, "l2": "256 MB flush per iter"},
         "peak_gbs": hbm, "peak_source": src,
-        "cascade_attention": dict(rl(attn_bytes, attn_us), prefix_bytes=pre_bytes,
-                                  plan=dict(work=inf.n_work, wide=inf.n_work_wide, parts=inf.n_parts)),
+        "cascade_attention": dict(rl(attn_bytes, attn_us), prefix_bytes=pre_bytes, plan=plan_desc),
         "append_1layer": rl(app_bytes, app1_us),
         f"append_{layers}layers_1launch": rl(app_bytes * layers, appL_us),
         "fork_1layer": dict(rl(fork_bytes, fork1_us), copies=len(src_p)),

@@ -28,7 +28,8 @@ typedef enum {
   BE_ENOT_ALLOCATED = 4,   /* free of a page that is not allocated (a warning, page_table.py:117-119) */
   BE_ECAPACITY = 5,        /* caller buffer too small; required size reported   */
   BE_EDEVICE_RANGE = 6,    /* device status: an index was out of range and skipped */
-  BE_EDEVICE_TIMEOUT = 7   /* device status: a bounded pipeline wait expired; output invalid */
+  BE_EDEVICE_TIMEOUT = 7,  /* device status: a bounded pipeline wait expired; output invalid */
+  BE_ENOTSUP = 8           /* plan shape this path does not serve (the caller takes another) */
 } be_status;
 
 typedef enum { BE_F32 = 0, BE_F16 = 1, BE_BF16 = 2 } be_dtype;
@@ -251,6 +252,88 @@ int be_attn_run_fixed_2s(const int32_t* plan_dev, const be_attn_caps* caps, int 
                          int dtype, float sm_scale, void* out, int64_t out_row_stride, float* lse,
                          float* mid_o, float* mid_lse, const int32_t* kv_list_override,
                          void* stream, void* side_stream);
+
+/* ------------------------------------------------------------------------
+ * Beam-tile decode attention (the default decode path for 2-byte pools with
+ * head_dim 128 and page size 16).  Same attention as be_cascade_plan +
+ * be_attn_run -- MultiLevelCascadeAttentionWrapper.plan / .run
+ * (modeling_llama.py:733-755, :362) -- in another plan form:
+ *   - a tile is a run of consecutive queries (one prompt's beams, cut at the
+ *     level-0 groups) of at most tile_rows query-head rows;
+ *   - an entry is one page a tile reads: (page id, valid tokens from slot 0,
+ *     query range [q_lo, q_hi) relative to the tile).  Every level-l group
+ *     contributes one entry per page and per tile its query range overlaps;
+ *     the last page has last_page_len tokens, the others page_size.  A page
+ *     listed at two levels is attended twice, as the reference's cascade does;
+ *   - a piece is a range of one tile's entries; one CTA per (piece, KV head)
+ *     streams the pages through shared memory (TMA) into tcgen05 tiles
+ *     (S = Q K^T, O = P V in TMEM, online softmax).  A tile of several pieces
+ *     leaves partial rows that a second kernel, launched right after, merges
+ *     by log-sum-exp.
+ * Decode only: a causal last level whose groups hold more than one query
+ * (a prompt) returns BE_ENOTSUP, and the caller plans with be_cascade_plan.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t n_tiles, n_pieces, n_entries, n_queries;
+  int32_t off_tiles, off_pieces, off_entries, total_ints;
+  int32_t page_size, group_size, tile_rows, n_part_pieces; /* pieces with partial rows */
+  int32_t total_tokens;     /* sum of the entries' valid tokens                   */
+  int32_t max_piece_entries;
+  int32_t cluster;          /* > 1: every tile has exactly `cluster` pieces, merged in
+                               the kernel through distributed shared memory        */
+  int32_t pad1;
+} be_tile_plan_info;
+typedef struct {
+  int32_t q_begin, q_len;   /* queries [q_begin, q_begin + q_len), rows = q_len * g */
+  int32_t piece_begin, n_pieces;
+  int32_t part_base;        /* first partial slot of the tile's pieces, -1 if one piece */
+  int32_t pad0, pad1, pad2;
+} be_attn_tile;
+typedef struct { int32_t page, ntok, q_lo, q_hi; } be_attn_entry;
+typedef struct {
+  int32_t tile, ent_begin, ent_end, index;   /* entries [ent_begin, ent_end) of `tile` */
+  int32_t q_begin, q_len, n_pieces, part_base; /* copies of the tile's fields          */
+  be_attn_entry first[4];                      /* copies of the piece's first entries  */
+} be_attn_piece;
+/* Plan buffer: header (be_tile_plan_info, BE_PLAN_HEADER_INTS ints), pieces
+ * (from off_pieces == BE_PLAN_HEADER_INTS), tiles, entries.                  */
+
+/* Cascade levels (the arrays of be_cascade_plan) -> tile plan.  tile_rows is
+ * 64 or 128.  cluster <= 1: about target_pieces pieces in all (~2 x SMs /
+ * num_kv_heads), partial rows merged by a second kernel.  cluster in 2..16:
+ * exactly `cluster` pieces per tile (some may be empty), run as one thread-
+ * block cluster per (tile, KV head) that merges its partial rows through
+ * distributed shared memory (no partial rows in global memory).  cluster -1:
+ * chosen from target_pieces and the tile count (info->cluster reports it; 0 =
+ * no cluster).  On BE_ECAPACITY info->total_ints holds the size needed.      */
+int be_tile_plan(int num_levels, const int32_t* const* qo_indptr, const int32_t* const* kv_indptr,
+                 const int32_t* const* kv_indices, const int32_t* const* last_page_len,
+                 const int32_t* num_groups, int num_queries, int page_size, int num_qo_heads,
+                 int num_kv_heads, int causal_last, int tile_rows, int target_pieces,
+                 int cluster, int32_t* plan, int64_t plan_capacity, be_tile_plan_info* info);
+
+/* Runs a tile plan in device memory (header included) on `stream`: the tile
+ * kernel, and for plans made with cluster <= 1 the merge kernel.  The grid is
+ * (max_pieces, num_kv_heads), clusters of `cluster` CTAs along x when
+ * cluster > 1 (max_pieces a multiple of it; the plan must have been made with
+ * the same cluster).  CTAs past the plan's piece count exit, so a recorded
+ * launch serves every plan with n_pieces <= max_pieces, n_tiles <= max_tiles
+ * and n_part_pieces <= max_part_pieces.  Every CTA reads its piece record
+ * before the piece count, so the plan buffer must hold at least
+ * BE_PLAN_HEADER_INTS + 24 * max_pieces ints.
+ * part_o: [max_part_pieces][num_kv_heads][tile_rows][head_dim] elements of
+ * `dtype` (partial rows are normalised, O / l) and
+ * part_lse: [max_part_pieces][num_kv_heads][tile_rows] fp32 scratch (unused
+ * with clusters; calls that share them must not overlap on the GPU).
+ * lse (optional): natural-log LSE per (query, qo head).  plan_early != 0: the
+ * plan is in device memory before the kernel preceding this call starts
+ * (read before the programmatic-launch wait).                                */
+int be_attn_tiles_run(const int32_t* plan_dev, int max_pieces, int max_tiles, int max_part_pieces,
+                      int tile_rows, int page_size, const void* q, int64_t q_row_stride,
+                      const void* paged_kv_cache, int num_pages, int num_qo_heads,
+                      int num_kv_heads, int head_dim, int dtype, float sm_scale, void* out,
+                      int64_t out_row_stride, float* lse, void* part_o, float* part_lse,
+                      int cluster, int plan_early, void* stream);
 
 /* ------------------------------------------------------------------------
  * Decoder-layer kernels of the model runner (the reference runs these as
@@ -495,6 +578,13 @@ int be_cascade_pages_twice(int num_levels, const int32_t* const* qo_indptr,
 int be_beam_decode_inputs(be_trie* t, int ncand, const int32_t* cand_leaf, int num_qo_heads,
                           int num_kv_heads, int num_sms, int32_t* out, int64_t cap,
                           int32_t plan_offset, be_attn_plan_info* info);
+
+/* be_beam_decode_inputs with a tile plan (be_tile_plan) from out[plan_offset].
+ * BE_ENOTSUP when the step's cascade is not a decode shape.                 */
+int be_beam_decode_tiles(be_trie* t, int ncand, const int32_t* cand_leaf, int num_qo_heads,
+                         int num_kv_heads, int tile_rows, int target_pieces, int cluster,
+                         int32_t* out, int64_t cap, int32_t plan_offset,
+                         be_tile_plan_info* info);
 
 #ifdef __cplusplus
 }
