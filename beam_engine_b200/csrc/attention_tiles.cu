@@ -65,6 +65,7 @@ struct TileParams {
   int max_part_pieces, max_tiles;
   int plan_early;
   int cluster;           // > 1: CTAs of a (tile, KV head) form a cluster, merged on chip
+  int merge_next;        // tile_merge_kernel follows on the stream
   int debug;             // BE_ATTN_DEBUG & 4: globaltimer stamps into lse (per CTA x 16)
 };
 
@@ -268,7 +269,11 @@ __global__ void __launch_bounds__(192, 2) attn_tile_kernel(const __grid_constant
   uint64_t* odone = bars + 3 * NS + 4;    // O += P V of a chunk completed
   uint64_t* qfull = bars + 3 * NS + 5;    // Q in shared memory (128 threads)
   uint64_t* drain = bars + 3 * NS + 6;    // abort path: every issued MMA completed
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 3 * NS + 7);
+  // the last O += P V completed.  (A parity wait on `odone` cannot tell the last
+  // completion from the one before it: two PV products may be in flight when
+  // the softmax finishes its last chunk.)
+  uint64_t* ofinal = bars + 3 * NS + 7;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 3 * NS + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* issued = abort_flag + 1;  // chunks whose loads the producer issued
 
@@ -315,6 +320,7 @@ __global__ void __launch_bounds__(192, 2) attn_tile_kernel(const __grid_constant
     mbar_init(odone, 1);
     mbar_init(qfull, 128);
     mbar_init(drain, 1);
+    mbar_init(ofinal, 1);
     *abort_flag = 0;
     *issued = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -450,6 +456,7 @@ __global__ void __launch_bounds__(192, 2) attn_tile_kernel(const __grid_constant
           }
           umma_commit(odone);
           umma_commit(sfree + s);
+          if (cp == nch - 1) umma_commit(ofinal);
           if (cp < 8) tstamp(p, 32 + cp);
           ++cp;
           progressed = true;
@@ -474,6 +481,7 @@ __global__ void __launch_bounds__(192, 2) attn_tile_kernel(const __grid_constant
         // release the softmax warps from their waits so the CTA can drain
         for (int b = 0; b < 2; ++b) mbar_arrive(sfull + b);
         mbar_arrive(odone);
+        mbar_arrive(ofinal);
       }
     }
     __syncwarp();
@@ -636,9 +644,9 @@ __global__ void __launch_bounds__(192, 2) attn_tile_kernel(const __grid_constant
         if (tid == 0 && c < 8) tstamp(p, 16 + c);
       }
       if (tid == 0) tstamp(p, 4);
-      pdl_trigger();
+      if (p.merge_next) pdl_trigger();              // only our merge kernel may start early
       // ---------------- epilogue (M = 64) ----------------
-      const bool have_o = alive && nch > 0 && tl_warp_wait(odone, (nch - 1) & 1) && !*abort_flag;
+      const bool have_o = alive && nch > 0 && tl_warp_wait(ofinal, 0) && !*abort_flag;
       if (nch > 0 && !have_o) alive = false;
       tc_fence_after();
       lA = quad_sum(lA);
@@ -822,9 +830,11 @@ __global__ void __launch_bounds__(192, 2) attn_tile_kernel(const __grid_constant
       if (tid == 0 && c < 8) tstamp(p, 16 + c);
     }
     if (tid == 0) tstamp(p, 4);
-    pdl_trigger();                                   // the merge kernel may get resident
+    // only our merge kernel may start early: it waits for this grid before reading;
+    // another library's kernel launched next may read the output without waiting
+    if (p.merge_next) pdl_trigger();
     // ---------------- epilogue ----------------
-    const bool have_o = alive && nch > 0 && tl_warp_wait(odone, (nch - 1) & 1) && !*abort_flag;
+    const bool have_o = alive && nch > 0 && tl_warp_wait(ofinal, 0) && !*abort_flag;
     if (nch > 0 && !have_o) alive = false;
     tc_fence_after();
     const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
@@ -985,7 +995,7 @@ __global__ void __launch_bounds__(128) tile_merge_kernel(TileParams p) {
 }
 
 template <typename T, int M>
-int launch_tiles(const TileParams& p, const CUtensorMap& map, int max_pieces, int merge,
+int launch_tiles(TileParams p, const CUtensorMap& map, int max_pieces, int merge,
                  cudaStream_t st) {
   const size_t smem = TileShape<M>::smem();
   static bool set = false;
@@ -998,6 +1008,7 @@ int launch_tiles(const TileParams& p, const CUtensorMap& map, int max_pieces, in
     set = true;
   }
   if (p.cluster > 1) {
+    p.merge_next = 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(max_pieces, p.hkv);
     cfg.blockDim = dim3(192);
@@ -1015,8 +1026,9 @@ int launch_tiles(const TileParams& p, const CUtensorMap& map, int max_pieces, in
     BE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, attn_tile_kernel<T, M>, map, p));
     return BE_OK;
   }
+  p.merge_next = merge && p.max_part_pieces > 0;
   BE_CUDA_CHECK(launch_pdl(attn_tile_kernel<T, M>, dim3(max_pieces, p.hkv), 192, smem, st, map, p));
-  if (merge && p.max_part_pieces > 0) {
+  if (p.merge_next) {
     const int64_t warps = (int64_t)p.hkv * p.max_tiles * M;
     const int grid = (int)std::min<int64_t>((warps + 3) / 4, 148 * 8);
     BE_CUDA_CHECK(launch_pdl(tile_merge_kernel<T, M>, dim3(grid), 128, 0, st, p));

@@ -89,9 +89,12 @@ def test_multi_prompt_batch_matches_single_runs():
     assert [s for s, _ in outs[0][1]] == [s for s, _ in outs[2][0]]
 
 
-def test_graph_step_matches_eager_bf16():
+@pytest.mark.parametrize("tiles", ["1", "0"])
+def test_graph_step_matches_eager_bf16(monkeypatch, tiles):
     """The CUDA-graph decode step (fixed-shape attention launches, plan on the
-    device) selects the same beams as the eager step."""
+    device) selects the same beams as the eager step, on the beam-tile kernel
+    (default) and on the work-item kernels (BE_ATTN_TILES=0)."""
+    monkeypatch.setenv("BE_ATTN_TILES", tiles)
     from beam_engine_b200.beam import BeamSearchGenerator
     from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy
     from beam_engine_b200.configs import TINY
@@ -106,8 +109,10 @@ def test_graph_step_matches_eager_bf16():
                                   max_num_pages=512, use_graph=graph)
         outs.append(gen.generate_ids(prompts, 8, max_new_tokens=24, num_return_sequences=8))
         assert gen.use_graph == graph
+        assert gen.use_tiles == (tiles == "1")
         if graph:
-            assert gen.step_graph is not None and gen.step_graph.graph is not None
+            sg = gen.step_graph_tiles if tiles == "1" else gen.step_graph
+            assert sg is not None and sg.graph is not None
     for a, b in zip(*outs):
         assert [s for s, _ in a] == [s for s, _ in b]
         np.testing.assert_allclose([x for _, x in a], [x for _, x in b], rtol=1e-6)
@@ -134,9 +139,12 @@ def test_auto_picker_runs_and_agrees_when_it_picks_cascade():
         assert [s for s, _ in out] == [s for s, _ in runs["fasttree"][0]]
 
 
-def test_tree_graph_step_matches_eager_bf16():
-    """Tree-attention decode steps replayed from a CUDA graph (slot-list plans
-    through the fixed-grid kernel) select the same beams as eager tree steps."""
+@pytest.mark.parametrize("pages", ["1", "0"])
+def test_tree_graph_step_matches_eager_bf16(monkeypatch, pages):
+    """Tree-attention decode steps replayed from a CUDA graph (page-list plans on
+    the tensor-core kernels by default, slot-list plans through the fixed-grid
+    kernel with BE_TREE_PAGES=0) select the same beams as eager tree steps."""
+    monkeypatch.setenv("BE_TREE_PAGES", pages)
     from beam_engine_b200.beam import BeamSearchGenerator
     from beam_engine_b200.beam_strategy import VanillaBeamSearchStrategy
     from beam_engine_b200.configs import TINY
@@ -152,7 +160,8 @@ def test_tree_graph_step_matches_eager_bf16():
         outs.append(gen.generate_ids(prompts, 8, max_new_tokens=12, num_return_sequences=8))
         assert gen.use_graph_tree == graph
         if graph:
-            assert gen.step_graph_tree is not None and gen.step_graph_tree.graph is not None
+            sg = gen.step_graph_tpages if pages == "1" else gen.step_graph_tree
+            assert sg is not None and sg.graph is not None
     for a, b in zip(*outs):
         assert [s for s, _ in a] == [s for s, _ in b]
         np.testing.assert_allclose([x for _, x in a], [x for _, x in b], rtol=1e-6)

@@ -211,3 +211,22 @@ def test_empty_queries_and_non_finite_stale_slots():
     assert torch.isfinite(out).all()
     assert (out[1] == 0).all() and torch.isinf(l[1]).all() and (l[1] < 0).all()
     check(out, levels, q, pool, l)
+
+
+@pytest.mark.parametrize("hq", [32, 64])
+@pytest.mark.parametrize("cluster", [0, 4])
+def test_large_logits_rescale_paths(hq, cluster):
+    """Scores of large spread (q x 12, keys growing along the sequence) make the
+    running maximum jump by more than 2^8 inside a piece, so the lazy O rescale
+    in TMEM runs often; M = 64 and M = 128 rows, merged by kernel or cluster."""
+    d = dev()
+    g = torch.Generator().manual_seed(11)
+    P = 4096
+    levels = cfg2_levels(g, P, prefix=1024, max_suffix=200)
+    pool = torch.randn((P, 2, 16, 8, 128), generator=g)
+    ramp = torch.linspace(0.2, 3.0, P).view(P, 1, 1, 1, 1)      # later pages score higher
+    pool[:, 0:1] = pool[:, 0:1] * ramp
+    pool = pool.to(torch.bfloat16).to(d)
+    q = (torch.randn((16, hq, 128), generator=g) * 12).to(torch.bfloat16).to(d)
+    info, outs = run_tiles(levels, 16, q, pool, hq, 8, lse=True, cluster=cluster, pieces=8)
+    check(outs[0][0], levels, q, pool, outs[0][1])
