@@ -127,6 +127,10 @@ _SIGS = {
     "be_beam_select_update": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, vp, vp, vp, C.c_int, vp, vp,
                                         vp, vp, vp, vp, vp, vp, vp]),
     "be_cascade_pages_twice": (C.c_int, [C.c_int, vp, vp, vp, vp, C.c_int]),
+    "be_vanilla_select_device": (C.c_int, [C.c_int, vp, C.c_int, vp, vp, vp, C.c_int, C.c_int,
+                                           vp, vp, vp, vp]),
+    "be_beam_update_selected": (C.c_int, [vp, C.c_int, vp, vp, vp, vp, vp, C.c_int, vp, vp, vp, vp,
+                                          vp, vp, vp, vp, vp]),
     "be_leaf_sequences": (i64, [vp, C.c_int, vp, vp, vp, i64]),
     "be_diverse_select": (C.c_int, [C.c_int, vp, C.c_int, vp, vp,
                                     vp, vp, vp, C.c_int, C.c_int, C.c_double,

@@ -152,14 +152,33 @@ class PlannedAttention:
             t.append((s, e))
 
 
+def step_sel_offsets(n):
+    """Offsets (int32 units) of the device-selection inputs in a step buffer of n
+    beams: prompt ranges seg_ptr [<= n + 1] after the fork list, then the
+    parents' accumulated scores as n doubles (8-byte aligned)."""
+    seg_off = 7 * n + 1
+    scores_off = (seg_off + n + 2) // 2 * 2
+    return seg_off, scores_off
+
+
 def step_plan_offset(n):
     """Offset (int32 units) of the attention plan in a step buffer of n beams."""
-    return -(-(7 * n + 1) // 32) * 32
+    return -(-(step_sel_offsets(n)[1] + 2 * n) // 32) * 32
 
 
 def _pool_dtype(pt):
     return (_lib.BE_F32 if pt.store_dtype == torch.float32 else
             (_lib.BE_BF16 if pt.store_dtype == torch.bfloat16 else _lib.BE_F16))
+
+
+class DeviceSelection:
+    """A step's vanilla selection made on the device (be_vanilla_select_device):
+    per prompt, beam_size (parent candidate, token, accumulated score) in rank
+    order, parent -1 past the prompt's entries."""
+    __slots__ = ("parent", "token", "score")
+
+    def __init__(self, parent, token, score):
+        self.parent, self.token, self.score = parent, token, score
 
 
 class StepGraph:
@@ -202,6 +221,17 @@ class StepGraph:
                                        device=dev)
         self.vals_h = torch.empty(n * k, dtype=torch.float32).pin_memory()
         self.idx_h = torch.empty(n * k, dtype=torch.int64).pin_memory()
+        # global top-W on the device (vanilla strategy): nseg prompts of beam width W
+        self.select = caps.get("select")          # None or (nseg, W, max candidates per prompt)
+        if self.select is not None:
+            nseg, W, _ = self.select
+            self.seg_off, self.scores_off = step_sel_offsets(n)
+            self.sel_d = (torch.empty(nseg * W, dtype=torch.int32, device=dev),
+                          torch.empty(nseg * W, dtype=torch.int32, device=dev),
+                          torch.empty(nseg * W, dtype=torch.float64, device=dev))
+            self.sel_h = (torch.empty(nseg * W, dtype=torch.int32).pin_memory(),
+                          torch.empty(nseg * W, dtype=torch.int32).pin_memory(),
+                          torch.empty(nseg * W, dtype=torch.float64).pin_memory())
         if kind != "tiles":
             self.ccaps = _lib.AttnCaps(self.caps["work"], self.caps["wide"], self.caps["merge"], 1,
                                        _lib.BE_CAPS_SLOTS if kind == "fasttree" else 0)
@@ -298,6 +328,18 @@ class StepGraph:
         logits = self.gen.model.forward(d[0:n], d[n:2 * n], self.gen.page_table, d[2 * n:3 * n],
                                         d[3 * n:4 * n], self)
         v, i = self.gen._logprob_topk(logits, self.k, self.temp)
+        if self.select is not None:
+            # selection on the device; only beam_size (parent, token, score) per prompt leave it
+            nseg, W, maxc = self.select
+            v, i = v.contiguous(), i.contiguous()
+            sp, st, ss = self.sel_d
+            check(lib().be_vanilla_select_device(
+                nseg, d.data_ptr() + 4 * self.seg_off, self.k, d.data_ptr() + 4 * self.scores_off,
+                v.data_ptr(), i.data_ptr(), W, maxc, sp.data_ptr(), st.data_ptr(), ss.data_ptr(),
+                stream_ptr(self.gen.device)), "device selection")
+            for h, x in zip(self.sel_h, self.sel_d):
+                h.copy_(x, non_blocking=True)
+            return
         self.vals_h.copy_(v.reshape(-1), non_blocking=True)
         self.idx_h.copy_(i.reshape(-1), non_blocking=True)
 
@@ -328,8 +370,18 @@ class StepGraph:
         if self.timing and self.gen.attn_times is not None:
             self.gen.attn_times.extend(self.attention_ms())
         k = self.k
+        if self.select is not None:
+            self.gen.d2h_bytes += sum(h.numel() * h.element_size() for h in self.sel_h)
+            return DeviceSelection(*(h.numpy().copy() for h in self.sel_h))
+        self.gen.d2h_bytes += n * k * (4 + 8)
         return (self.vals_h.numpy()[:n * k].reshape(n, k).astype(np.float64),
                 self.idx_h.numpy()[:n * k].reshape(n, k).astype(np.int32))
+
+    def set_selection_inputs(self, seg, scores):
+        """Prompt ranges and parent scores of this step for the device selection."""
+        h = self.host_buf.numpy()
+        h[self.seg_off:self.seg_off + len(seg)] = seg
+        h[self.scores_off:self.scores_off + 2 * len(scores)].view(np.float64)[:] = scores
 
 
 class BeamSearchGenerator:
@@ -385,7 +437,11 @@ class BeamSearchGenerator:
         self.use_tiles = (self.page_table.store_dtype != torch.float32
                           and tiles_eligible(model.D, page_size, model.Hq, model.Hkv))
         self._beam_width = 1
-        self.h2d_bytes = 0            # host -> device bytes copied by the engine (inputs, plans)
+        # vanilla selection on the device inside the tile step graph (BE_DEVICE_SELECT=0: host)
+        self.device_select = os.environ.get("BE_DEVICE_SELECT", "1") == "1"
+        self._sel_ctx = None          # (prompt ranges, beam width) of the step being run
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0            # device -> host bytes of the scoring / selection results            # host -> device bytes copied by the engine (inputs, plans)
 
     # ------------------------------------------------------------------
     def generate(self, input_text: str, beam_size: int = 4, max_length: int = 50,
@@ -439,6 +495,7 @@ class BeamSearchGenerator:
         hv, hi = self.topk_host
         hv[:n * k].copy_(vals.reshape(-1), non_blocking=True)
         hi[:n * k].copy_(idx.reshape(-1), non_blocking=True)
+        self.d2h_bytes += n * k * (4 + 8)
         torch.cuda.current_stream(self.device).synchronize()
         return (hv[:n * k].numpy().reshape(n, k).astype(np.float64),
                 hi[:n * k].numpy().reshape(n, k).astype(np.int32))
@@ -665,7 +722,13 @@ class BeamSearchGenerator:
         tp = target_pieces(self.attn.plan.num_sms, m.Hkv)
         sg = self.step_graph_tiles
 
-        same = sg is not None and sg.n == n and sg.k == k and sg.temp == temperature
+        want_sel = None
+        if self._sel_ctx is not None:
+            seg, W = self._sel_ctx
+            want_sel = (len(seg) - 1, W)
+        same = (sg is not None and sg.n == n and sg.k == k and sg.temp == temperature
+                and (sg.select[:2] if sg.select is not None else None) == want_sel
+                and (want_sel is None or int(np.max(np.diff(self._sel_ctx[0]))) <= sg.select[2]))
 
         def fill(buf_ptr, cap, plan_off, cluster):
             rc = lib().be_beam_decode_tiles(self.page_table._trie, n, _lib.addr(leaves), m.Hq,
@@ -696,6 +759,10 @@ class BeamSearchGenerator:
                 size *= 4
             # headroom: entries grow with the beams' suffixes; pieces and tiles hardly change
             cl = info.cluster
+            sel = None
+            if self._sel_ctx is not None:
+                seg, W = self._sel_ctx
+                sel = (len(seg) - 1, W, int(np.max(np.diff(seg))))
             if cl > 1:   # one cluster per (tile, KV head): pieces = tiles x cluster
                 caps = dict(pieces=info.n_pieces, tiles=info.n_tiles, part_pieces=0,
                             ints=3 * info.total_ints + 64 * n + 4096, rows=info.tile_rows,
@@ -706,6 +773,7 @@ class BeamSearchGenerator:
                             part_pieces=info.n_pieces + 2 * info.n_tiles + tp // 4 + 16,
                             ints=3 * info.total_ints + 64 * n + 4096, rows=info.tile_rows,
                             cluster=0)
+            caps["select"] = sel
             # the kernel reads piece records up to max_pieces before the piece count
             caps["ints"] = max(caps["ints"], 32 + 24 * caps["pieces"] + 64)
             if sg is not None and sg.n == n and sg.k == k and sg.temp == temperature:
@@ -725,6 +793,9 @@ class BeamSearchGenerator:
         if self.plan_hook is not None:
             self.plan_hook(n, info)
         self._take_fork(sg)
+        if sg.select is not None:
+            seg, W = self._sel_ctx
+            sg.set_selection_inputs(seg, state.scores)
         return sg.step_filled(sg.plan_off + info.total_ints)
 
     def generate_ids(self, prompts: List[List[int]], beam_size: int = 4,
@@ -765,10 +836,22 @@ class BeamSearchGenerator:
                 if on_step is not None:
                     on_step(step)
                 k = min(2 * W, V) if W != 1 else 1
+                vanilla = type(self.strategy) is VanillaBeamSearchStrategy
+                self._sel_ctx = ((np.asarray(seg, np.int32), W)
+                                 if vanilla and getattr(self, "device_select", False) and k <= 64
+                                 and int(np.max(np.diff(seg))) * k <= 8192 else None)
                 with _Range("decode_step"):
-                    vals, idx = self.decode_topk(state, k, temperature)
+                    res = self.decode_topk(state, k, temperature)
+                self._sel_ctx = None
                 with _Range("select"):
-                    if type(self.strategy) is VanillaBeamSearchStrategy:
+                    if isinstance(res, DeviceSelection):
+                        new_seg = state.vanilla_step_selected(seg, res.parent, res.token,
+                                                              res.score, W)
+                        self._after_update(state)
+                        seg = np.asarray(new_seg)
+                        continue
+                    vals, idx = res
+                    if vanilla:
                         # selection + trie update in one native call
                         new_seg = state.vanilla_step(seg, idx, vals, W)
                         self._after_update(state)

@@ -244,6 +244,42 @@ class BeamState:
         if c and not self.defer_copies and self.page_table.kv_cache.is_cuda:
             self.page_table.copy_blocks(*self.last_copies)
 
+    def vanilla_step_selected(self, seg, sel_parent, sel_token, sel_score, beam_size):
+        """The trie update of a vanilla step whose selection ran on the device
+        (be_vanilla_select_device: per prompt, beam_size (parent, token, score)
+        in rank order, parent -1 past the prompt's entries).  Returns the new
+        per-prompt candidate ranges, like vanilla_step."""
+        seg = np.ascontiguousarray(seg, np.int32)
+        nseg = len(seg) - 1
+        ncand = int(seg[-1])
+        cap = max(1, nseg * beam_size)
+        nl, cs, cd, cl = (np.zeros(cap, np.int32) for _ in range(4))
+        ns = np.zeros(cap, np.float64)
+        nseg_ptr = np.zeros(nseg + 1, np.int32)
+        cptr = np.zeros(ncand + 1, np.int32)
+        n_new, n_cp = C.c_int32(), C.c_int32()
+        leaves = np.ascontiguousarray(self._leaves, np.int32)
+        sp = np.ascontiguousarray(sel_parent, np.int32)
+        st = np.ascontiguousarray(sel_token, np.int32)
+        sc = np.ascontiguousarray(sel_score, np.float64)
+        rc = lib().be_beam_update_selected(self._t, nseg, _lib.addr(seg), _lib.addr(leaves),
+                                           _lib.addr(sp), _lib.addr(st), _lib.addr(sc), beam_size,
+                                           _lib.addr(nl), _lib.addr(ns), C.byref(n_new),
+                                           _lib.addr(nseg_ptr), _lib.addr(cs), _lib.addr(cd),
+                                           _lib.addr(cl), C.byref(n_cp), _lib.addr(cptr))
+        if rc == _lib.BE_ENOMEM:
+            raise MemoryError("No free pages available")
+        check(rc, "vanilla step (device selection)")
+        self.last_child_ptr = cptr.copy()
+        m, c = n_new.value, n_cp.value
+        self._leaves = nl[:m].copy()
+        self._scores = ns[:m].copy()
+        self._cand_objs = None
+        self.last_copies = (cs[:c].copy(), cd[:c].copy(), cl[:c].copy())
+        if c and not self.defer_copies and self.page_table.kv_cache.is_cuda:
+            self.page_table.copy_blocks(*self.last_copies)
+        return nseg_ptr.copy()
+
     def vanilla_step(self, seg, tokens, logps, beam_size):
         """Vanilla selection of every prompt (candidates seg[s]:seg[s+1]) on the
         top-k (tokens / logps [ncand, k]) plus the trie update, one native call

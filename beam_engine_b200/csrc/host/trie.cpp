@@ -1002,6 +1002,64 @@ int be_beam_select_update(be_trie* t, int nseg, const int32_t* seg_ptr, int k,
   return BE_OK;
 }
 
+int be_beam_update_selected(be_trie* t, int nseg, const int32_t* seg_ptr, const int32_t* cand_leaf,
+                            const int32_t* sel_parent, const int32_t* sel_token,
+                            const double* sel_score, int beam_size, int32_t* new_leaf,
+                            double* new_score, int32_t* n_new, int32_t* new_seg_ptr,
+                            int32_t* copy_src, int32_t* copy_dst, int32_t* copy_len,
+                            int32_t* n_copies, int32_t* child_ptr) {
+  if (nseg < 0 || !seg_ptr || beam_size < 1 || !sel_parent || !sel_token || !sel_score) {
+    set_error("be_beam_update_selected: invalid arguments");
+    return BE_EINVAL;
+  }
+  const int ncand = seg_ptr[nseg];
+  struct Scratch {
+    std::vector<int32_t> ptr, fill, ct, child;
+    std::vector<double> cs;
+  };
+  static thread_local Scratch tls;
+  Scratch& S = tls;
+  const int cap = std::max(1, nseg * beam_size);
+  S.ptr.assign(ncand + 1, 0);
+  S.ct.resize(cap);
+  S.cs.resize(cap);
+  S.child.resize(cap);
+  // children per candidate, counted then placed in rank order (results_map of
+  // select_candidates, beam_strategy.py:470-476)
+  new_seg_ptr[0] = 0;
+  for (int s = 0; s < nseg; ++s) {
+    int got = 0;
+    for (int r = 0; r < beam_size; ++r) {
+      const int c = sel_parent[(int64_t)s * beam_size + r];
+      if (c < 0) break;
+      if (c < seg_ptr[s] || c >= seg_ptr[s + 1]) {
+        set_error("be_beam_update_selected: prompt %d selection %d names candidate %d", s, r, c);
+        return BE_EINVAL;
+      }
+      S.ptr[c + 1]++;
+      ++got;
+    }
+    new_seg_ptr[s + 1] = new_seg_ptr[s] + got;
+  }
+  for (int c = 0; c < ncand; ++c) S.ptr[c + 1] += S.ptr[c];
+  S.fill.assign(S.ptr.begin(), S.ptr.end() - 1);
+  for (int s = 0; s < nseg; ++s)
+    for (int r = 0; r < beam_size; ++r) {
+      const int64_t o = (int64_t)s * beam_size + r;
+      const int c = sel_parent[o];
+      if (c < 0) break;
+      const int at = S.fill[c]++;
+      S.ct[at] = sel_token[o];
+      S.cs[at] = sel_score[o];
+    }
+  int rc = be_beam_update(t, ncand, cand_leaf, S.ptr.data(), S.ct.data(), new_leaf, S.child.data(),
+                          n_new, copy_src, copy_dst, copy_len, n_copies);
+  if (rc) return rc;
+  for (int i = 0; i < *n_new; ++i) new_score[i] = S.cs[S.child[i]];
+  if (child_ptr) std::copy(S.ptr.begin(), S.ptr.begin() + ncand + 1, child_ptr);
+  return BE_OK;
+}
+
 // Everything one cascade decode step needs from the host, in one call: the
 // per-candidate inputs (query token, RoPE position, append page, append slot)
 // at out[0 .. 4 * ncand) and the attention plan (header included) at

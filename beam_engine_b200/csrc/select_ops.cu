@@ -136,21 +136,32 @@ __global__ void __launch_bounds__(TK_THREADS) logsoftmax_topk_kernel(
     }
     tk.offer(valid ? val : -INFINITY, valid ? col : INT_MAX, k, tv, ti);
   };
-  for (int base = c0; base < c1; base += 128) {
-    const int col = base + lane * 4;
-    float e[4];
-    if (vec && col + 3 < c1) {
-      const float4 q = *reinterpret_cast<const float4*>(x + col);
-      e[0] = q.x;
-      e[1] = q.y;
-      e[2] = q.z;
-      e[3] = q.w;
-    } else {
+  // TK_DEPTH 16-byte loads per lane in flight before any is consumed: the row is
+  // read at memory speed instead of one DRAM round trip per 128 elements
+  constexpr int TK_DEPTH = 4;
+  for (int base0 = c0; base0 < c1; base0 += 128 * TK_DEPTH) {
+    float4 buf[TK_DEPTH];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) e[j] = col + j < c1 ? x[col + j] : -INFINITY;
+    for (int u = 0; u < TK_DEPTH; ++u) {
+      const int col = base0 + u * 128 + lane * 4;
+      if (vec && col + 3 < c1) {
+        buf[u] = __ldcs(reinterpret_cast<const float4*>(x + col));   // read once: streaming
+      } else {
+        buf[u].x = col < c1 ? x[col] : -INFINITY;
+        buf[u].y = col + 1 < c1 ? x[col + 1] : -INFINITY;
+        buf[u].z = col + 2 < c1 ? x[col + 2] : -INFINITY;
+        buf[u].w = col + 3 < c1 ? x[col + 3] : -INFINITY;
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) consume(e[j], col + j, col + j < c1);
+    for (int u = 0; u < TK_DEPTH; ++u) {
+      const int col = base0 + u * 128 + lane * 4;
+      if (base0 + u * 128 >= c1) break;              // warp-uniform
+      consume(buf[u].x, col, col < c1);
+      consume(buf[u].y, col + 1, col + 1 < c1);
+      consume(buf[u].z, col + 2, col + 2 < c1);
+      consume(buf[u].w, col + 3, col + 3 < c1);
+    }
   }
   // log-sum-exp: warp, then block
 #pragma unroll
@@ -227,5 +238,96 @@ extern "C" int be_logsoftmax_topk(const float* logits, int64_t ld, int rows, int
                            logits, ld, v, temperature, k, vocab_offset, full_vocab, out_val, out_idx,
                            row_max, row_sumexp));
   BE_LAUNCH_CHECK();
+  return BE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Global top-W of every prompt on the device: VanillaBeamSearchStrategy
+// .select_candidates (src/beam_engine/beam_strategy.py:433-488).  Candidate c
+// of prompt s (c in seg_ptr[s]..seg_ptr[s+1]) offers its top-k children with
+// accumulated score parent_scores[c] + logps[c][j] (double, as the reference's
+// Python floats); the prompt keeps the beam_size best by a stable descending
+// sort of the flattened (candidate, j) list: equal scores keep the earlier
+// candidate, then the earlier top-k position.  One CTA per prompt: every
+// entry counts the entries ranked before it.  Entries at top-k position
+// j >= beam_size cannot be selected (the row is sorted, so j entries of the
+// same candidate rank before it) and only take part as competitors.
+// ---------------------------------------------------------------------------
+namespace be {
+
+constexpr int SEL_THREADS = 512;
+constexpr int SEL_MAX = 8192;          // entries per prompt (candidates x k) held in shared memory
+
+__global__ void __launch_bounds__(SEL_THREADS) vanilla_select_kernel(
+    const int32_t* __restrict__ seg_ptr, int k, const double* __restrict__ parent_scores,
+    const float* __restrict__ logps, const int64_t* __restrict__ tokens, int beam_size,
+    int cap_entries, int32_t* __restrict__ sel_parent, int32_t* __restrict__ sel_token,
+    double* __restrict__ sel_score) {
+  extern __shared__ double s_tot[];
+  pdl_wait();
+  const int s = blockIdx.x;
+  const int c0 = seg_ptr[s], c1 = seg_ptr[s + 1];
+  const int m = (c1 - c0) * k;
+  if (m > cap_entries || c1 < c0) {                // more than the launch's shared memory
+    if (threadIdx.x == 0) flag_range_error();
+    return;
+  }
+  for (int e = threadIdx.x; e < m; e += blockDim.x) {
+    const int c = c0 + e / k;
+    s_tot[e] = parent_scores[c] + (double)logps[(int64_t)c * k + e % k];
+  }
+  __syncthreads();
+  const int jmax = min(k, beam_size);
+  const int cands = (c1 - c0) * jmax;
+  for (int x = threadIdx.x; x < cands; x += blockDim.x) {
+    const int e = (x / jmax) * k + x % jmax;
+    const double te = s_tot[e];
+    int rank = 0;
+    for (int f = 0; f < m && rank < beam_size; ++f) {
+      const double tf = s_tot[f];
+      rank += (tf > te) || (tf == te && f < e);
+    }
+    if (rank < beam_size) {
+      const int c = c0 + e / k;
+      const int64_t o = (int64_t)s * beam_size + rank;
+      sel_parent[o] = c;
+      sel_token[o] = (int32_t)tokens[(int64_t)c * k + e % k];
+      sel_score[o] = te;
+    }
+  }
+  for (int r = min(beam_size, m) + threadIdx.x; r < beam_size; r += blockDim.x)
+    sel_parent[(int64_t)s * beam_size + r] = -1;
+}
+
+}  // namespace be
+
+extern "C" int be_vanilla_select_device(int nseg, const int32_t* seg_ptr, int k,
+                                        const double* parent_scores, const float* logps,
+                                        const int64_t* tokens, int beam_size, int max_seg_cands,
+                                        int32_t* sel_parent, int32_t* sel_token,
+                                        double* sel_score, void* stream) {
+  using namespace be;
+  if (nseg < 0 || k < 1 || beam_size < 1 || max_seg_cands < 0 || !seg_ptr || !parent_scores ||
+      !logps || !tokens || !sel_parent || !sel_token || !sel_score) {
+    set_error("be_vanilla_select_device: invalid arguments");
+    return BE_EINVAL;
+  }
+  if ((int64_t)max_seg_cands * k > SEL_MAX) {
+    set_error("be_vanilla_select_device: %d candidates x top-%d exceed %d entries per prompt",
+              max_seg_cands, k, SEL_MAX);
+    return BE_EINVAL;
+  }
+  if (nseg == 0) return BE_OK;
+  const size_t smem = (size_t)max_seg_cands * k * sizeof(double);
+  static bool set = false;
+  if (!set) {
+    BE_CUDA_CHECK(cudaFuncSetAttribute(vanilla_select_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)(SEL_MAX * sizeof(double))));
+    set = true;
+  }
+  BE_CUDA_CHECK(launch_pdl(vanilla_select_kernel, nseg, SEL_THREADS, smem, (cudaStream_t)stream,
+                           seg_ptr, k, parent_scores, logps, tokens, beam_size,
+                           max_seg_cands * k, sel_parent, sel_token, sel_score));
   return BE_OK;
 }

@@ -37,12 +37,13 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "beam decode tokens/s, Llama-3-8B-shape W=16; paged attn HBM GB/s vs peak"
-# DRAM bytes per algorithmic byte of the attention launch, from one ncu capture of
-# the tcgen05 prefix kernel on the cfg2 op case (dram read+write 8.57 MB for
-# 8.39 MB of K+V; partial rows stay in L2); traffic scales with the tokens read
-TRAFFIC_RATIO = 8.57 / 8.388608
-TRAFFIC_SOURCE = ("scaled: ncu dram__bytes_read+write of attn_umma_kernel on the cfg2 op case "
-                  "(profiles/attn_umma_cfg2.md) x this launch's algorithmic bytes")
+# DRAM bytes per algorithmic byte of the attention launch, from one ncu capture of the
+# beam-tile kernel on a cfg3 decode state (bench.py --op tiles3 --pool-pages 8192: dram
+# read+write 45.31 MB for 52.63 MB of planned K/V + Q/O; pages listed at two cascade levels
+# are read from L2 the second time); traffic scales with the tokens read
+TRAFFIC_RATIO = (45.306112 + 0.00384) / 52.625408
+TRAFFIC_SOURCE = ("scaled: ncu dram__bytes_read+write of attn_tile_kernel on a cfg3 decode state "
+                  "(bench.py --op tiles3) x this launch's algorithmic bytes")
 PROMPTS, PROMPT_LEN, BEAM, NEW_TOKENS, PAGE = 8, 1024, 16, 128, 16
 MODEL_NAME, KERNEL = "LLAMA3_8B", "cascade"
 WORKLOAD = ("cfg3: Llama-3-8B shape, 8 prompts x 1024 tokens, beam width 16, 128 new tokens, "
@@ -252,6 +253,7 @@ def run_b200(args, rank, world, local_rank):
     gen2_t0 = torch.cuda.Event(enable_timing=True)
     gen2_t1 = torch.cuda.Event(enable_timing=True)
     h2d0 = gen.h2d_bytes
+    d2h0 = gen.d2h_bytes
     gen2_pre = torch.cuda.Event(enable_timing=True)
 
     def mark_prefill_done(i):   # decode step 0 starts: prefill + root expansion are queued
@@ -272,7 +274,6 @@ def run_b200(args, rank, world, local_rank):
     e2e_ms = float(t.item())
     e2e_tokens = PROMPTS * BEAM * NEW_TOKENS * replicas
     steps_e2e = NEW_TOKENS
-    d2h = PROMPTS * BEAM * 2 * BEAM * (4 + 8)   # top-2W values (f32) + ids (i64) per beam
     assert len(out) == PROMPTS and all(len(o) == 1 for o in out)
     res = {
         "metric": METRIC,
@@ -299,7 +300,8 @@ def run_b200(args, rank, world, local_rank):
                      "traffic": round(TRAFFIC_RATIO * bytes_total / max(len(attn_ms), 1)),
                      "traffic_source": TRAFFIC_SOURCE,
                      "kernel": ("be_attn_tiles_run per layer (one beam-tile tcgen05 launch, "
-                                "in-kernel LSE merge)" if plan_kind == {"tiles"} else
+                                "pieces merged on chip by clusters or by the merge kernel)"
+                                if plan_kind == {"tiles"} else
                                 "be_attn_run_fixed_2s per layer (tcgen05 prefix tiles, all-heads "
                                 "suffix tiles on a second stream, LSE merge)")
                                + ", timed by event nodes inside the step graph",
@@ -317,7 +319,7 @@ def run_b200(args, rank, world, local_rank):
                           "frac": round(step_bytes / (ms_max / K / 1e3) / 1e9 / hbm, 4)},
         "e2e": {"value": round(e2e_tokens / (e2e_ms / 1e3), 2), "unit": "beam tokens/s",
                 "h2d_bytes_per_step": int((gen.h2d_bytes - h2d0) / steps_e2e),
-                "d2h_bytes_per_step": d2h,
+                "d2h_bytes_per_step": int((gen.d2h_bytes - d2h0) / steps_e2e),
                 "includes": f"prefill of {PROMPTS} x {PROMPT_LEN} prompt tokens + {NEW_TOKENS - 1} "
                             "decode steps, host ids in, host beams out", "wall_ms": round(wall_ms, 1),
                 "prefill_ms": round(prefill_ms, 2)},
@@ -631,6 +633,84 @@ def run_op_bench(args):
     }
 
 
+def run_op_tiles(args):
+    """Decode attention of one layer at a cfg3 decode state, on the beam-tile
+    kernel: 8 prompts x 1024 tokens, 16 beams each, after `--op-steps` random
+    selection steps (half the beams of a prompt fork, half die), Hq 32 / Hkv 8 /
+    D 128, page size 16, bf16, one layer's pool of `--pool-pages` pages; 256 MB
+    L2 flush before every timed launch, CUDA events, median of --iters."""
+    import numpy as np
+    import torch
+    from beam_engine_b200 import _lib
+    from beam_engine_b200.beam_state import BeamState
+    from beam_engine_b200.cascade import target_pieces, tile_plan_host
+    from beam_engine_b200.page_table import PageTable, dtype_code
+    dev = torch.device("cuda", 0)
+    Hq, Hkv, D, ps = 32, 8, 128, 16
+    pt = PageTable(1, ps, args.pool_pages, Hkv, D, device=dev, store_dtype=torch.bfloat16)
+    rng = np.random.default_rng(0)
+    bs = BeamState(BEAM, pt)
+    for _ in range(PROMPTS):
+        bs.add_root_sequence(rng.integers(0, 1000, PROMPT_LEN).tolist())
+    bs.update_native(bs.leaves, np.arange(PROMPTS + 1, dtype=np.int32) * BEAM,
+                     rng.integers(0, 1000, PROMPTS * BEAM).astype(np.int32),
+                     -rng.random(PROMPTS * BEAM))
+    for _ in range(args.op_steps):
+        n = len(bs.leaves)
+        cnt = np.zeros(n, np.int32)
+        for p_ in range(PROMPTS):
+            c = np.zeros(BEAM, np.int32)
+            c[: BEAM // 2] = 2
+            rng.shuffle(c)
+            cnt[p_ * BEAM:(p_ + 1) * BEAM] = c
+        ptr = np.concatenate([[0], np.cumsum(cnt)]).astype(np.int32)
+        bs.update_native(bs.leaves, ptr, rng.integers(0, 1000, int(ptr[-1])).astype(np.int32),
+                         -rng.random(int(ptr[-1])))
+    pt.kv_cache.normal_(generator=torch.Generator(device=dev).manual_seed(1))
+    levels = bs.cascade_levels()
+    n = len(bs.leaves)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    info, plan = tile_plan_host(levels, n, ps, Hq, Hkv, num_sms=sms, cluster=args.cluster,
+                                pieces=target_pieces(sms, Hkv))
+    plan_d = torch.from_numpy(np.ascontiguousarray(plan)).to(dev)
+    slots = max(1, info.n_part_pieces) * Hkv * info.tile_rows
+    po = torch.empty(slots * D, dtype=torch.bfloat16, device=dev)
+    pl = torch.empty(slots, dtype=torch.float32, device=dev)
+    q = torch.randn((n, Hq, D), device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    pool = pt.kv_cache_at_layer[0]
+    L = _lib.lib()
+
+    def run():
+        _lib.check(L.be_attn_tiles_run(plan_d.data_ptr(), info.n_pieces, info.n_tiles,
+                                       info.n_part_pieces, info.tile_rows, ps, q.data_ptr(),
+                                       q.stride(0), pool.data_ptr(), pool.shape[0], Hq, Hkv, D,
+                                       dtype_code(pool.dtype), D ** -0.5, out.data_ptr(),
+                                       out.stride(0), None, po.data_ptr(), pl.data_ptr(),
+                                       info.cluster, 0, None))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        run()
+    ts = []
+    for _ in range(args.iters):
+        flush.zero_()
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record()
+        run()
+        e_.record()
+        torch.cuda.synchronize()
+        ts.append(s_.elapsed_time(e_) * 1e3)
+    us = statistics.median(ts)
+    byts = info.total_tokens * 2 * Hkv * D * 2 + 2 * n * Hq * D * 2
+    hbm, _, src = peaks()
+    return {"config": {"workload": "cfg3 decode attention, one layer", "beams": n,
+                       "selection_steps": args.op_steps, "l2": "256 MB flush per iter"},
+            "plan": {"tiles": info.n_tiles, "pieces": info.n_pieces, "entries": info.n_entries,
+                     "tile_rows": info.tile_rows, "cluster": info.cluster},
+            "us": round(us, 2), "bytes": byts, "gbs": round(byts / us / 1e3, 1),
+            "frac": round(byts / us / 1e3 / hbm, 4), "peak_gbs": hbm, "peak_source": src}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -645,9 +725,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-comm", default="nccl", choices=["nccl", "peer"],
                     help="tensor-parallel all-reduce: NCCL, or the fused peer-memory kernel")
-    ap.add_argument("--op", default=None, choices=["cfg2"],
+    ap.add_argument("--op", default=None, choices=["cfg2", "tiles3"],
                     help="op-level microbench instead of the decode benchmark")
     ap.add_argument("--pool-pages", type=int, default=65536)
+    ap.add_argument("--op-steps", type=int, default=60,
+                    help="--op tiles3: random selection steps before the timed launches")
+    ap.add_argument("--cluster", type=int, default=-1,
+                    help="--op tiles3: cluster size (-1: the planner's choice, 0: merge kernel)")
     ap.add_argument("--op-layers", type=int, default=32)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--split", type=int, default=0)
@@ -663,7 +747,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.op:
-        print(json.dumps(run_op_bench(args)), flush=True)
+        fn = run_op_tiles if args.op == "tiles3" else run_op_bench
+        print(json.dumps(fn(args)), flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args, rank, world)

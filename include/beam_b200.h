@@ -498,6 +498,31 @@ int be_vanilla_select_segments(int nseg, const int32_t* seg_ptr, int k,
                                const double* logps, int beam_size, int32_t* child_ptr,
                                int32_t* child_tokens, double* child_scores,
                                int32_t* new_seg_ptr);
+/* VanillaBeamSearchStrategy.select_candidates (src/beam_engine/beam_strategy.py:433-488)
+ * for every prompt in one launch, on the device: candidates seg_ptr[s] ..
+ * seg_ptr[s+1] of prompt s offer their top-k children (logps / tokens
+ * [ncand][k], each row sorted as be_logsoftmax_topk writes it) with
+ * accumulated score parent_scores[c] + logps[c][j] in double; the prompt keeps
+ * the beam_size best of a stable descending sort (ties: earlier candidate,
+ * then earlier top-k position).  Out, for slot r < beam_size of prompt s at
+ * s * beam_size + r, in rank order: sel_parent (candidate index; -1 past the
+ * prompt's entry count), sel_token, sel_score.  All pointers are device
+ * memory; every prompt has at most max_seg_cands candidates and
+ * max_seg_cands * k <= 8192.                                                  */
+int be_vanilla_select_device(int nseg, const int32_t* seg_ptr, int k, const double* parent_scores,
+                             const float* logps, const int64_t* tokens, int beam_size,
+                             int max_seg_cands, int32_t* sel_parent, int32_t* sel_token,
+                             double* sel_score, void* stream);
+/* The trie update (be_beam_update, beam_state.py:101-209) from selections in
+ * the form be_vanilla_select_device writes (host copies): children per old
+ * candidate in rank order, prompts in order.  Same outputs as
+ * be_beam_select_update.                                                      */
+int be_beam_update_selected(be_trie* t, int nseg, const int32_t* seg_ptr, const int32_t* cand_leaf,
+                            const int32_t* sel_parent, const int32_t* sel_token,
+                            const double* sel_score, int beam_size, int32_t* new_leaf,
+                            double* new_score, int32_t* n_new, int32_t* new_seg_ptr,
+                            int32_t* copy_src, int32_t* copy_dst, int32_t* copy_len,
+                            int32_t* n_copies, int32_t* child_ptr);
 /* DiverseBeamSearchStrategy.select_candidates (src/beam_engine/beam_strategy.py:173-317)
  * for several prompts at once (candidates seg_ptr[s]..seg_ptr[s+1] form prompt s).
  * tokens/logps [ncand][k] in top-k order; seq_ptr [ncand + 1] / seq_tokens are the
