@@ -553,9 +553,15 @@ class BeamSearchGenerator:
         from .cascade import cascade_plan_host
         from .fasttree import build_tree_plan
         from .picker import choose
+        from .picker import cascade_counts_pages_twice
         m, ps = self.model, self.page_table.page_size
         n = len(state.leaves)
         levels = state.cascade_levels()
+        if getattr(self, "use_tiles", False) and not cascade_counts_pages_twice(levels):
+            # an exact cascade step runs on the beam-tile kernel (picker.py)
+            self.picks.append("cascade")
+            self._tree_stash = None
+            return "cascade"
         cinfo, _ = cascade_plan_host(levels, n, ps, m.Hq, m.Hkv, causal=True,
                                      num_sms=self.attn.plan.num_sms)
         v, r2t = self._tree_vnodes(state, n)

@@ -12,7 +12,13 @@ decode step from the two plans the host builds anyway:
   ``beam_state.py:299-302``), so those pages enter the softmax twice.  When a
   step's cascade levels do that, the tree plan (one vnode per trie node, each
   page once) is taken;
-* otherwise the cheaper plan by a launch-level model of these kernels:
+* otherwise, when the step runs on the beam-tile kernel (2-byte pools, head_dim
+  128, page size 16), the cascade: measured on B200 at the cfg3 decode state
+  (bench.py, CUDA events inside the step graph) it takes 28.3 us per layer for
+  43 MB of K/V where the work-item kernels that run a tree page plan take
+  55.6 us for the same tokens, so an exact cascade step is always cheaper;
+* otherwise (fp32 parity mode, other shapes) the cheaper plan by a
+  launch-level model of the work-item kernels:
   ``time = launches * t_launch + waves * t_cta + bytes / HBM``, where a wave
   is one CTA per SM (two for the tcgen05 prefix tiles), the bytes are every
   work item's K/V plus the partial rows written and merged.  The per-CTA times
@@ -94,12 +100,16 @@ def cascade_counts_pages_twice_py(levels) -> bool:
 
 
 def choose(cascade_levels, cascade_info, tree_info, hkv, hq, d, model: PickerModel | None = None,
-           elt=2, tree_pages=False) -> str:
+           elt=2, tree_pages=False, cascade_tiles=False) -> str:
     """'cascade' or 'fasttree' for one decode step.  ``tree_pages``: the tree
     step runs as a page-list plan on the same kernels as the cascade step, so it
-    is costed by the cascade model on its own plan (``tree_info``)."""
+    is costed by the cascade model on its own plan (``tree_info``).
+    ``cascade_tiles``: the cascade step runs on the beam-tile kernel (the plan
+    infos are not needed then)."""
     if cascade_counts_pages_twice(cascade_levels):
         return "fasttree"
+    if cascade_tiles:
+        return "cascade"
     m = model or PickerModel()
     tree = (m.cascade_us(tree_info, hkv, hq, d, elt) if tree_pages
             else m.tree_us(tree_info, hkv, hq, d, elt))

@@ -124,13 +124,17 @@ def test_generate_ids_host_loop_matches_oracle(strategy, W, ps):
     assert all(len(a) == len(b) == len(c) for a, b, c in gen.forks)
 
 
-@pytest.mark.parametrize("tree_pages", [False, True])
-def test_pick_kernel_host_side(tree_pages):
+@pytest.mark.parametrize("tree_pages,tiles", [(False, False), (True, False), (True, True)])
+def test_pick_kernel_host_side(tree_pages, tiles):
     """kernel_type "auto": the per-step picker builds both plans on the host,
     returns a kind and stashes the tree plan for the step (page-list plan when
-    tree_pages), along a trajectory with uneven beams."""
+    tree_pages), along a trajectory with uneven beams.  With the beam-tile
+    kernel every exact cascade step is a cascade step; a step whose cascade
+    lists a page twice is always a tree step."""
     from types import SimpleNamespace
+    from beam_engine_b200.picker import cascade_counts_pages_twice
     gen = FakeGenerator(VanillaBeamSearchStrategy(), 16, 2048)
+    gen.use_tiles = tiles
     gen.model = SimpleNamespace(vocab=VOCAB, Hq=32, Hkv=8, D=128, Hq_total=32, Hkv_total=8)
     gen.attn = SimpleNamespace(plan=SimpleNamespace(num_sms=148))
     gen.picks, gen.tree_pages, gen._tree_stash = [], tree_pages, None
@@ -144,8 +148,13 @@ def test_pick_kernel_host_side(tree_pages):
     seg = np.array([0, 8, 16])
     kinds = []
     for _ in range(10):
+        twice = cascade_counts_pages_twice(st.cascade_levels())
         kind = gen.pick_kernel(st)
         kinds.append(kind)
+        if twice:
+            assert kind == "fasttree"
+        elif tiles:
+            assert kind == "cascade"
         if kind == "fasttree":
             v, r2t, tinfo, tplan, pp = gen._tree_stash
             assert (pp is not None) == tree_pages

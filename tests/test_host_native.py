@@ -215,6 +215,10 @@ def test_picker_exactness_and_cost(cascade_trees):
     assert m.cascade_us(shared, 8, 32, 128) < m.tree_us(tree_dup, 8, 32, 128)
     assert choose(cascade_trees["uneven"]["expect"]["levels"], shared, tree_dup, 8, 32, 128) == \
         "fasttree"
+    # on the beam-tile kernel an exact cascade always wins; exactness still comes first
+    assert choose(lv, heavy, light, 8, 32, 128, cascade_tiles=True) == "cascade"
+    assert choose(cascade_trees["uneven"]["expect"]["levels"], shared, tree_dup, 8, 32, 128,
+                  cascade_tiles=True) == "fasttree"
 
 
 @pytest.mark.parametrize("case", ["ps16_w8", "ps8_w6_churn", "ps16_w16"])
