@@ -4,10 +4,7 @@
 // library GEMMs; torch.mm takes cuBLASLt's first heuristic for each.  Here the
 // first call of a shape (outside stream capture) times the heuristic's top
 // candidates -- split-K variants included -- on the caller's stream and keeps
-// the fastest; later calls, and calls inside a capture, reuse it.  Each timed
-// run starts with the weights out of L2 (a 256 MB memset in between, not
-// timed): in a decode step every layer's weights come from HBM, and timing
-// back-to-back runs would rank the candidates by L2 speed instead.
+// the fastest; later calls, and calls inside a capture, reuse it.
 //
 //   Y[T][N] = X[T][K] * W[N][K]^T    (row-major, bf16 operands, fp32 accumulate)
 // is computed column-major as Y^T (N x T) = op_T(W_cm: K x N) * X_cm (K x T).
@@ -105,9 +102,9 @@ extern "C" int be_gemm_lt(const void* x, int64_t ldx, const void* w, int64_t ldw
     uint64_t wsb = (uint64_t)std::max<int64_t>(workspace_bytes, 0);
     BE_LT_CHECK(cublasLtMatmulPreferenceSetAttribute(
         pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &wsb, sizeof(wsb)));
-    cublasLtMatmulHeuristicResult_t res[32];
+    cublasLtMatmulHeuristicResult_t res[16];
     int n_res = 0;
-    cublasStatus_t hs = cublasLtMatmulAlgoGetHeuristic(h, p.op, p.a, p.b, p.c, p.c, pref, 32, res,
+    cublasStatus_t hs = cublasLtMatmulAlgoGetHeuristic(h, p.op, p.a, p.b, p.c, p.c, pref, 16, res,
                                                        &n_res);
     cublasLtMatmulPreferenceDestroy(pref);
     if (hs != CUBLAS_STATUS_SUCCESS || n_res == 0) {
@@ -116,12 +113,6 @@ extern "C" int be_gemm_lt(const void* x, int64_t ldx, const void* w, int64_t ldw
     }
     int best = 0;
     if (cs == cudaStreamCaptureStatusNone && n_res > 1) {   // time the candidates once
-      static void* flush = nullptr;                            // L2 eviction buffer (tuning only)
-      const size_t flush_bytes = 256u << 20;
-      if (!flush && cudaMalloc(&flush, flush_bytes) != cudaSuccess) {
-        flush = nullptr;
-        cudaGetLastError();
-      }
       cudaEvent_t e0, e1;
       BE_CUDA_CHECK(cudaEventCreate(&e0));
       BE_CUDA_CHECK(cudaEventCreate(&e1));
@@ -133,20 +124,16 @@ extern "C" int be_gemm_lt(const void* x, int64_t ldx, const void* w, int64_t ldw
           ok = cublasLtMatmul(h, p.op, &alpha, w, p.a, x, p.b, &beta, y, p.c, y, p.c, &res[i].algo,
                               workspace, wsb, st) == CUBLAS_STATUS_SUCCESS;
         if (!ok) continue;
-        float ms_best = 1e30f;
-        for (int r = 0; r < 5; ++r) {       // best of five runs, each from a cold L2
-          if (flush) BE_CUDA_CHECK(cudaMemsetAsync(flush, r, flush_bytes, st));
-          BE_CUDA_CHECK(cudaEventRecord(e0, st));
+        BE_CUDA_CHECK(cudaEventRecord(e0, st));
+        for (int r = 0; r < 5; ++r)
           cublasLtMatmul(h, p.op, &alpha, w, p.a, x, p.b, &beta, y, p.c, y, p.c, &res[i].algo,
                          workspace, wsb, st);
-          BE_CUDA_CHECK(cudaEventRecord(e1, st));
-          BE_CUDA_CHECK(cudaEventSynchronize(e1));
-          float ms = 0.f;
-          BE_CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
-          ms_best = std::min(ms_best, ms);
-        }
-        if (ms_best < best_ms) {
-          best_ms = ms_best;
+        BE_CUDA_CHECK(cudaEventRecord(e1, st));
+        BE_CUDA_CHECK(cudaEventSynchronize(e1));
+        float ms = 0.f;
+        BE_CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+        if (ms < best_ms) {
+          best_ms = ms;
           best = i;
         }
       }

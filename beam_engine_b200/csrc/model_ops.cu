@@ -159,6 +159,70 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
   }
 }
 
+// The same RoPE + append with one CTA per row: the row's cos / sin are computed
+// once into shared memory (rope_append_kernel computes them again for every
+// head), and every q / k / v access is a 16-byte vector.  Arithmetic per
+// element is the same as rope_append_kernel's.  Needs D / 2 a multiple of the
+// vector width, D / 2 <= 256, and 16-byte aligned rows and pool.
+template <typename T>
+__global__ void __launch_bounds__(256) rope_append_rows_kernel(
+    T* __restrict__ qkv, int64_t row_stride, int n, int hq, int hkv, int D,
+    const int32_t* __restrict__ positions, const float* __restrict__ inv_freq,
+    T* __restrict__ pool, int num_pages, int page_size, const int32_t* __restrict__ write_page,
+    const int32_t* __restrict__ write_pos, int write_rope_k_in_place) {
+  constexpr int V = 16 / sizeof(T);
+  __shared__ float cs[256], sn[256];
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x, half = D / 2;
+  const float pos = (float)positions[row];
+  for (int d = threadIdx.x; d < half; d += blockDim.x) {
+    float s, c;
+    sincosf(pos * inv_freq[d], &s, &c);
+    cs[d] = c;
+    sn[d] = s;
+  }
+  const int page = write_page[row], slot = write_pos[row];
+  const bool kv_ok = page >= 0 && page < num_pages && slot >= 0 && slot < page_size;
+  if (!kv_ok && threadIdx.x == 0) flag_range_error();
+  __syncthreads();
+  T* src_row = qkv + row * row_stride;
+  const int64_t kdst = ((int64_t)page * 2 * page_size + slot) * hkv * D;      // K half of the page
+  const int64_t vdst = (((int64_t)page * 2 + 1) * page_size + slot) * hkv * D;
+  const int nvec = half / V;
+  const int rot = (kv_ok ? hq + hkv : hq) * nvec;
+  for (int i = threadIdx.x; i < rot; i += blockDim.x) {
+    const int h = i / nvec, d0 = (i - h * nvec) * V;
+    T* src = src_row + (int64_t)h * D;
+    float x1[V], x2[V], y1[V], y2[V];
+    load_vec<T, V>(src + d0, x1);
+    load_vec<T, V>(src + d0 + half, x2);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const float c = cs[d0 + j], s = sn[d0 + j];
+      y1[j] = x1[j] * c - x2[j] * s;
+      y2[j] = x2[j] * c + x1[j] * s;
+    }
+    if (h < hq) {
+      store_vec<T, V>(src + d0, y1);
+      store_vec<T, V>(src + d0 + half, y2);
+    } else {
+      T* dst = pool + kdst + (int64_t)(h - hq) * D;
+      store_vec<T, V>(dst + d0, y1);
+      store_vec<T, V>(dst + d0 + half, y2);
+      if (write_rope_k_in_place) {
+        store_vec<T, V>(src + d0, y1);
+        store_vec<T, V>(src + d0 + half, y2);
+      }
+    }
+  }
+  if (!kv_ok) return;
+  const int vv = hkv * D / V;   // v heads: a straight 16-byte copy
+  const int4* vsrc = reinterpret_cast<const int4*>(src_row + (int64_t)(hq + hkv) * D);
+  int4* vd = reinterpret_cast<int4*>(pool + vdst);
+  for (int i = threadIdx.x; i < vv; i += blockDim.x) vd[i] = vsrc[i];
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu,
                                                        T* __restrict__ out, int n, int F) {
@@ -229,6 +293,24 @@ extern "C" int be_rope_qkv_append(void* qkv, int64_t row_stride, int n, int num_
   const int threads = 256;
   const int blocks = (int)((warps * 32 + threads - 1) / threads);
   cudaStream_t st = (cudaStream_t)stream;
+  const int V = 16 / dtype_size(dtype);
+  const bool rows_form = (head_dim / 2) % V == 0 && head_dim / 2 <= 256 && row_stride % V == 0 &&
+                         ((uintptr_t)qkv & 15) == 0 && ((uintptr_t)paged_kv_cache & 15) == 0;
+  if (rows_form) {
+#define BE_ROPE_ROWS(T)                                                                        \
+  BE_CUDA_CHECK(launch_pdl(rope_append_rows_kernel<T>, n, threads, 0, st, (T*)qkv, row_stride, n, \
+                           num_qo_heads, num_kv_heads, head_dim, positions, inv_freq,            \
+                           (T*)paged_kv_cache, num_pages, page_size, write_page, write_pos,      \
+                           rope_k_in_place))
+    switch (dtype) {
+      case BE_BF16: BE_ROPE_ROWS(__nv_bfloat16); break;
+      case BE_F16: BE_ROPE_ROWS(__half); break;
+      default: BE_ROPE_ROWS(float);
+    }
+#undef BE_ROPE_ROWS
+    BE_LAUNCH_CHECK();
+    return BE_OK;
+  }
 #define BE_ROPE(T)                                                                           \
   BE_CUDA_CHECK(launch_pdl(rope_append_kernel<T>, blocks, threads, 0, st, (T*)qkv, row_stride, n, \
                            num_qo_heads, num_kv_heads, head_dim, positions, inv_freq,            \

@@ -9,7 +9,8 @@
 //     sorted by (value desc, id asc), KMAX / 32 entries per lane; a candidate
 //     enters only if it beats the current k-th entry (ballot), so after the
 //     first few hundred elements almost nothing is inserted;
-//   * the warps' lists meet in shared memory and warp 0 merges them the same way;
+//   * the warps' lists meet in shared memory, where every entry finds its rank
+//     among all lists by binary search (no serial merge);
 //   * out: log-probabilities (x - max) - log(sum) of the k best with global
 //     vocabulary ids, or -- for a vocabulary slice under tensor parallelism --
 //     the raw scaled logits plus the slice's max and sum for a cross-rank
@@ -182,7 +183,7 @@ __global__ void __launch_bounds__(TK_THREADS) logsoftmax_topk_kernel(
     s_s[warp] = s;
   }
   __syncthreads();
-  if (warp != 0) return;
+  // block log-sum-exp, reduced by every warp (32 partials)
   m = s_m[lane];
   s = s_s[lane];
 #pragma unroll
@@ -193,24 +194,33 @@ __global__ void __launch_bounds__(TK_THREADS) logsoftmax_topk_kernel(
     s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
     m = mm;
   }
-  // merge the other warps' lists into warp 0's (only their first k entries matter)
-  for (int w = 1; w < TK_WARPS; ++w)
-    for (int e0 = 0; e0 < k; e0 += 32) {
-      const int e = e0 + lane;
-      const bool in = e < k;
-      tk.offer(in ? s_v[w][e] : -INFINITY, in ? s_i[w][e] : INT_MAX, k, tv, ti);
-    }
   const float log_s = logf(s);
-#pragma unroll
-  for (int q = 0; q < TK_PER_LANE; ++q) {
-    const int e = q * 32 + lane;
-    if (e < k) {
-      const float val = tk.v[q];
-      out_val[(int64_t)row * k + e] = full_vocab ? (val - m) - log_s : val;
-      out_idx[(int64_t)row * k + e] = (int64_t)tk.id[q] + vocab_offset;
+  // the block's top k: the first k entries of every warp's sorted list are
+  // ranked against all other lists at once (rank = entries strictly better,
+  // a binary search per list); (value, id) pairs are distinct, so ranks
+  // 0..k-1 are each taken by exactly one entry
+  for (int i = tid; i < TK_WARPS * k; i += TK_THREADS) {
+    const int w = i / k, e = i - w * k;
+    const float xv = s_v[w][e];
+    const int xi = s_i[w][e];
+    int rank = e;
+    for (int w2 = 0; w2 < TK_WARPS; ++w2) {
+      if (w2 == w) continue;
+      int lo = 0, hi = k;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (tk_better(s_v[w2][mid], s_i[w2][mid], xv, xi)) lo = mid + 1;
+        else hi = mid;
+      }
+      rank += lo;
+      if (rank >= k) break;
+    }
+    if (rank < k) {
+      out_val[(int64_t)row * k + rank] = full_vocab ? (xv - m) - log_s : xv;
+      out_idx[(int64_t)row * k + rank] = (int64_t)xi + vocab_offset;
     }
   }
-  if (!full_vocab && lane == 0) {
+  if (!full_vocab && tid == 0) {
     row_max[row] = m;
     row_sum[row] = s;
   }
