@@ -7,15 +7,16 @@
 // all-reduce is latency-bound, so each rank instead:
 //   1. has its GEMM write the partial straight into its own slot of a buffer
 //      the other ranks have mapped (CUDA IPC, one process per GPU);
-//   2. per CTA (one CTA per row, grid-stride beyond the flag capacity): signals
-//      every rank with a per-CTA counter (st.release.sys to the peer's flag
-//      array) and waits until every rank has signalled the same count
-//      (ld.acquire.sys, bounded by %globaltimer: on expiry BE_EDEVICE_TIMEOUT is
-//      recorded and the CTA returns);
-//   3. reads the row from every rank's slot (plain 16-byte loads over NVLink,
-//      volatile, in rank order so every rank computes identical bits), sums in
-//      fp32, rounds to the storage type, adds it to the residual, and writes
-//      the normalised row -- the add_rmsnorm kernel's arithmetic.
+//   2. per CTA (one CTA per row, grid-stride beyond the flag capacity): thread
+//      p signals rank p with a per-CTA counter (a relaxed system-scope store to
+//      the peer's flag array) and waits until rank p has signalled the same
+//      count (ld.acquire.sys, bounded by %globaltimer: on expiry
+//      BE_EDEVICE_TIMEOUT is recorded and the CTA returns);
+//   3. reads the row from every rank's slot (16-byte loads over NVLink, all
+//      ranks' loads in flight together, L1 bypassed), sums in rank order so
+//      every rank computes identical bits, in fp32, rounds to the storage
+//      type, adds it to the residual, and writes the normalised row -- the
+//      add_rmsnorm kernel's arithmetic.
 // Consecutive calls alternate between two slots: a rank can only write a slot
 // again after the barrier of the call in between, which every rank reaches
 // after finishing its reads of that slot -- so no closing barrier is needed.
@@ -43,8 +44,8 @@ __device__ __forceinline__ uint64_t comm_gtimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -52,45 +53,47 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// Barrier of CTA `cta` across ranks; false if it timed out.
+// Barrier of CTA `cta` across ranks; false if it timed out.  Thread p < world
+// signals rank p and waits for rank p's signal, so the peers are served in
+// parallel.  The signal is a relaxed store with no fence: the data it
+// announces (this rank's slot) was written by kernels that completed before
+// this one started, and peers read it from this GPU's L2 over NVLink.  (A
+// release fence at system scope cost ~10 us per call here.)  The wait is an
+// acquire load, so this thread's later reads stay behind it; the block
+// barrier after it orders the other threads' reads.
 __device__ bool comm_barrier(const CommArgs& a, int cta) {
+  __shared__ uint32_t epoch;
   __shared__ int ok;
-  if (threadIdx.x == 0) {
-    const uint32_t e = a.counter[cta] + 1;
-    asm volatile("fence.acq_rel.sys;" ::: "memory");   // prior writes before the signal
-    for (int p = 0; p < a.world; ++p)
-      st_release_sys(a.flags_out[p] + (size_t)cta * COMM_MAX_RANKS + a.rank, e);
-    bool good = true;
+  const int t = threadIdx.x;
+  if (t == 0) {
+    epoch = a.counter[cta] + 1;
+    ok = 1;
+  }
+  __syncthreads();
+  const uint32_t e = epoch;
+  if (t < a.world) {
+    st_relaxed_sys(a.flags_out[t] + (size_t)cta * COMM_MAX_RANKS + a.rank, e);
+    const uint32_t* f = a.flags_in + (size_t)cta * COMM_MAX_RANKS + t;
     const uint64_t t0 = comm_gtimer();
-    for (int p = 0; p < a.world && good; ++p) {
-      const uint32_t* f = a.flags_in + (size_t)cta * COMM_MAX_RANKS + p;
-      int polls = 0;
-      while ((int32_t)(ld_acquire_sys(f) - e) < 0) {   // monotonic: a peer may be ahead
-        if (++polls == 64) {
-          polls = 0;
-          if (comm_gtimer() - t0 > kCommWaitNs) {
-            atomicCAS(&g_device_status, 0, BE_EDEVICE_TIMEOUT);
-            good = false;
-            break;
-          }
+    int polls = 0;
+    while ((int32_t)(ld_acquire_sys(f) - e) < 0) {   // monotonic: a peer may be ahead
+      if (++polls == 64) {
+        polls = 0;
+        if (comm_gtimer() - t0 > kCommWaitNs) {
+          atomicCAS(&g_device_status, 0, BE_EDEVICE_TIMEOUT);
+          ok = 0;
+          break;
         }
       }
     }
-    a.counter[cta] = e;
-    ok = good ? 1 : 0;
   }
   __syncthreads();
+  if (t == 0) a.counter[cta] = e;
   return ok != 0;
 }
 
-// 16-byte load of a rank's slot: volatile (system-coherent, no stale L1 line
-// from the call two calls back, when this slot last held other data).
 template <typename T>
-__device__ __forceinline__ void load16_peer(const T* p, float* out) {
-  int4 raw;
-  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
-               : "l"(p));
+__device__ __forceinline__ void unpack16(const int4& raw, float* out) {
   if constexpr (sizeof(T) == 2) {
     const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
@@ -130,31 +133,45 @@ __device__ __forceinline__ void store16(T* p, const float* v) {
   *reinterpret_cast<int4*>(p) = raw;
 }
 
-// One CTA per row (grid-stride).  With residual: residual += round_T(sum);
-// out = w * round_T(residual * rsqrt(mean(residual^2) + eps)).  Without it:
-// out = round_T(sum).  H <= 256 threads x 8 vectors x (16 / sizeof(T)).
+constexpr int COMM_THREADS = 512;
+constexpr int COMM_NV = 4;   // 16-byte vectors per thread: hidden <= 512 x 4 x (16 / sizeof(T))
+
+// One CTA per row (grid-stride), one 16-byte vector of the row per thread and
+// pass (blockDim = hidden / vector width, up to 512 threads).  Every rank's
+// vector is loaded before any is summed, so the row costs one NVLink round
+// trip; sums in rank order (identical bits on every rank).  With residual:
+// residual += round_T(sum); out = w * round_T(residual * rsqrt(mean(residual^2)
+// + eps)).  Without it: out = round_T(sum).
 template <typename T>
-__global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(CommArgs a, T* __restrict__ residual,
-                                                                const T* __restrict__ w,
-                                                                T* __restrict__ out, int rows,
-                                                                int H, float eps) {
+__global__ void __launch_bounds__(COMM_THREADS) allreduce_rmsnorm_kernel(
+    CommArgs a, T* __restrict__ residual, const T* __restrict__ w, T* __restrict__ out, int rows,
+    int H, float eps) {
   constexpr int V = 16 / sizeof(T);
   const int cta = blockIdx.x;
+  pdl_wait();                      // the partials come from the kernel before this one
   if (!comm_barrier(a, cta)) return;
   __shared__ float red[32];
   for (int row = cta; row < rows; row += gridDim.x) {
-    float cache[8][V];   // fully unrolled below: stays in registers
+    float cache[COMM_NV][V];
     float ss = 0.f;
     const int64_t base = (int64_t)row * H;
 #pragma unroll
-    for (int nv = 0; nv < 8; ++nv) {
+    for (int nv = 0; nv < COMM_NV; ++nv) {
       const int c = (threadIdx.x + nv * blockDim.x) * V;
       if (c >= H) break;
+      int4 raw[COMM_MAX_RANKS];
+#pragma unroll
+      for (int p = 0; p < COMM_MAX_RANKS; ++p)   // L1-bypassing loads, all in flight
+        if (p < a.world)
+          raw[p] = __ldcv(reinterpret_cast<const int4*>(
+              reinterpret_cast<const T*>(a.slot[p]) + base + c));
       float s[V];
-      load16_peer(reinterpret_cast<const T*>(a.slot[0]) + base + c, s);
-      for (int p = 1; p < a.world; ++p) {
+      unpack16<T>(raw[0], s);
+#pragma unroll
+      for (int p = 1; p < COMM_MAX_RANKS; ++p) {
+        if (p >= a.world) break;
         float t[V];
-        load16_peer(reinterpret_cast<const T*>(a.slot[p]) + base + c, t);
+        unpack16<T>(raw[p], t);
 #pragma unroll
         for (int i = 0; i < V; ++i) s[i] += t[i];
       }
@@ -187,7 +204,7 @@ __global__ void __launch_bounds__(256) allreduce_rmsnorm_kernel(CommArgs a, T* _
     __syncthreads();
     const float inv = rsqrtf(red[0] / (float)H + eps);
 #pragma unroll
-    for (int nv = 0; nv < 8; ++nv) {
+    for (int nv = 0; nv < COMM_NV; ++nv) {
       const int c = (threadIdx.x + nv * blockDim.x) * V;
       if (c >= H) break;
       float wv[V], r[V];
@@ -311,7 +328,7 @@ extern "C" int be_comm_allreduce_rmsnorm(be_comm* c, int slot, void* residual, c
     return BE_EINVAL;
   }
   const int elt = dtype_size(dtype), V = 16 / elt;
-  if ((int64_t)rows * hidden * elt > c->slot_bytes || hidden % V || hidden > 256 * 8 * V ||
+  if ((int64_t)rows * hidden * elt > c->slot_bytes || hidden % V || hidden / V > COMM_THREADS * COMM_NV ||
       ((uintptr_t)out | (uintptr_t)residual | (uintptr_t)norm_w) % 16) {
     set_error("be_comm_allreduce_rmsnorm: %d x %d does not fit a %lld-byte slot / 16-byte rows",
               rows, hidden, (long long)c->slot_bytes);
@@ -334,20 +351,21 @@ extern "C" int be_comm_allreduce_rmsnorm(be_comm* c, int slot, void* residual, c
   a.world = c->world;
   a.max_ctas = c->max_ctas;
   const int grid = std::min(rows, c->max_ctas);
+  const int threads = std::min(COMM_THREADS, std::max(32, (hidden / V + 31) / 32 * 32));
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
     case BE_BF16:
-      allreduce_rmsnorm_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+      BE_CUDA_CHECK(launch_pdl(allreduce_rmsnorm_kernel<__nv_bfloat16>, grid, threads, 0, st,
           a, (__nv_bfloat16*)residual, (const __nv_bfloat16*)norm_w, (__nv_bfloat16*)out, rows,
-          hidden, eps);
+          hidden, eps));
       break;
     case BE_F16:
-      allreduce_rmsnorm_kernel<__half><<<grid, 256, 0, st>>>(
-          a, (__half*)residual, (const __half*)norm_w, (__half*)out, rows, hidden, eps);
+      BE_CUDA_CHECK(launch_pdl(allreduce_rmsnorm_kernel<__half>, grid, threads, 0, st,
+          a, (__half*)residual, (const __half*)norm_w, (__half*)out, rows, hidden, eps));
       break;
     default:
-      allreduce_rmsnorm_kernel<float><<<grid, 256, 0, st>>>(
-          a, (float*)residual, (const float*)norm_w, (float*)out, rows, hidden, eps);
+      BE_CUDA_CHECK(launch_pdl(allreduce_rmsnorm_kernel<float>, grid, threads, 0, st,
+          a, (float*)residual, (const float*)norm_w, (float*)out, rows, hidden, eps));
   }
   BE_LAUNCH_CHECK();
   return BE_OK;

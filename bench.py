@@ -723,7 +723,7 @@ def main():
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
                     help="N > 1: tensor parallel over the N GPUs (default) or N independent replicas")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--tp-comm", default="nccl", choices=["nccl", "peer"],
+    ap.add_argument("--tp-comm", default="peer", choices=["nccl", "peer"],
                     help="tensor-parallel all-reduce: NCCL, or the fused peer-memory kernel")
     ap.add_argument("--op", default=None, choices=["cfg2", "tiles3"],
                     help="op-level microbench instead of the decode benchmark")

@@ -109,10 +109,6 @@ def _run(dtype_name, tp_rank, world, port, q, comm="nccl"):
 def test_tp2_matches_single_gpu(dtype_name, tol, comm):
     if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
         pytest.skip("needs two GPUs")
-    if comm == "peer" and os.environ.get("BE_PEER_AR_TEST") != "1":
-        # device code on peer memory that has not yet run: kept out of the default
-        # pass on shared GPUs until it has passed once
-        pytest.skip("experimental peer all-reduce: set BE_PEER_AR_TEST=1")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
