@@ -682,11 +682,17 @@ extern "C" int be_tile_plan(int num_levels, const int32_t* const* qo_indptr,
   }
   const int64_t n_ent = nt ? S.estart[nt] : 0;
   if (cluster < 0) {
-    // auto: about target_pieces pieces over the tiles; a cluster per (tile, KV head)
-    // when that takes 2..16 pieces per tile, else the merge kernel (1 piece per
-    // tile needs no merge)
+    // auto: about target_pieces pieces over the tiles, as a cluster per (tile, KV
+    // head) of a power-of-two size: clusters of up to 8 CTAs pack two CTAs per
+    // SM into one wave (a cluster of 9 left CTAs waiting for a second wave), and
+    // 16 only when half the target still fills the grid (16-CTA clusters of two
+    // CTAs per SM did not all fit in one wave at 256 CTAs).  One piece per tile
+    // needs no merge.
     const int per_tile = nt ? std::max(1, target_pieces) / nt : 1;
-    cluster = per_tile <= 1 ? 0 : (per_tile <= 16 ? per_tile : 0);
+    cluster = 1;
+    while (cluster * 2 <= std::min(per_tile, 8)) cluster *= 2;
+    if (per_tile >= 32) cluster = 16;
+    if (cluster == 1) cluster = 0;
   }
   // pieces: about target_pieces in all, >= 8 entries (two 4-page chunks) each,
   // sizes rounded to whole chunks

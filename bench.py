@@ -646,7 +646,8 @@ def run_op_tiles(args):
     from beam_engine_b200.cascade import target_pieces, tile_plan_host
     from beam_engine_b200.page_table import PageTable, dtype_code
     dev = torch.device("cuda", 0)
-    Hq, Hkv, D, ps = 32, 8, 128, 16
+    # --op-tp N: one rank's share of the heads under N-way tensor parallelism
+    Hq, Hkv, D, ps = 32 // args.op_tp, 8 // args.op_tp, 128, 16
     pt = PageTable(1, ps, args.pool_pages, Hkv, D, device=dev, store_dtype=torch.bfloat16)
     rng = np.random.default_rng(0)
     bs = BeamState(BEAM, pt)
@@ -704,6 +705,7 @@ def run_op_tiles(args):
     byts = info.total_tokens * 2 * Hkv * D * 2 + 2 * n * Hq * D * 2
     hbm, _, src = peaks()
     return {"config": {"workload": "cfg3 decode attention, one layer", "beams": n,
+                       "heads": [Hq, Hkv],
                        "selection_steps": args.op_steps, "l2": "256 MB flush per iter"},
             "plan": {"tiles": info.n_tiles, "pieces": info.n_pieces, "entries": info.n_entries,
                      "tile_rows": info.tile_rows, "cluster": info.cluster},
@@ -733,6 +735,8 @@ def main():
     ap.add_argument("--cluster", type=int, default=-1,
                     help="--op tiles3: cluster size (-1: the planner's choice, 0: merge kernel)")
     ap.add_argument("--op-layers", type=int, default=32)
+    ap.add_argument("--op-tp", type=int, default=1, choices=[1, 2, 4, 8],
+                    help="--op tiles3: heads of one rank under this tensor parallelism")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true",
