@@ -713,6 +713,77 @@ def run_op_tiles(args):
             "frac": round(byts / us / 1e3 / hbm, 4), "peak_gbs": hbm, "peak_source": src}
 
 
+def run_op_allreduce(args, rank, world, local_rank):
+    """--op allreduce (under torchrun): one decode-step reduction, 128 rows x 4096
+    bf16 (1 MiB), as the fused peer all-reduce + add + RMSNorm and as NCCL's
+    all_reduce, `--iters` calls back to back, eagerly and replayed from a CUDA
+    graph; device time per call by CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from beam_engine_b200._lib import check, lib
+    from beam_engine_b200.page_table import stream_ptr
+    from beam_engine_b200.parallel import PeerAllReduce, TensorParallel
+    dev = torch.device("cuda", local_rank)
+    tp = TensorParallel()
+    n, H = 128, 4096
+    comm = PeerAllReduce(tp, n * H * 2, dev)
+    x = torch.randn(n, H, device=dev).bfloat16()
+    w = torch.ones(H, device=dev).bfloat16()
+    h = torch.empty_like(x)
+    for slot in (0, 1):
+        comm.slot_view(slot, (n, H), torch.bfloat16).normal_()
+    t = torch.randn(n, H, device=dev).bfloat16()
+
+    def peer(k):
+        for i in range(k):
+            check(lib().be_comm_allreduce_rmsnorm(comm.ptr, i & 1, x.data_ptr(), w.data_ptr(),
+                                                  h.data_ptr(), n, H, 1e-6, 2, stream_ptr(dev)),
+                  "allreduce")
+
+    def nccl(k):
+        for _ in range(k):
+            dist.all_reduce(t)
+
+    def timed(f, graph):
+        k = args.iters
+        torch.cuda.synchronize()
+        dist.barrier()
+        if graph:
+            g = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                f(4)
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                f(k)
+            run = g.replay
+        else:
+            def run():
+                f(k)
+        run()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        us = torch.tensor([e0.elapsed_time(e1) * 1e3 / k], device=dev)
+        dist.all_reduce(us, op=dist.ReduceOp.MAX)
+        return round(float(us.item()), 2)
+
+    res = {"op": "allreduce", "rows": n, "hidden": H, "bytes": n * H * 2, "n_gpus": world,
+           "calls": args.iters, "us_per_call": {}}
+    for name, f in (("peer", peer), ("nccl", nccl)):
+        for graph in (False, True):
+            res["us_per_call"][name + ("_graph" if graph else "")] = timed(f, graph)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -727,7 +798,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-comm", default="peer", choices=["nccl", "peer"],
                     help="tensor-parallel all-reduce: NCCL, or the fused peer-memory kernel")
-    ap.add_argument("--op", default=None, choices=["cfg2", "tiles3"],
+    ap.add_argument("--op", default=None, choices=["cfg2", "tiles3", "allreduce"],
                     help="op-level microbench instead of the decode benchmark")
     ap.add_argument("--pool-pages", type=int, default=65536)
     ap.add_argument("--op-steps", type=int, default=60,
@@ -750,6 +821,19 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.op == "allreduce":
+        import datetime
+        import torch
+        import torch.distributed as dist
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=180))
+        res = run_op_allreduce(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        sys.stdout.flush()
+        os._exit(0)
     if args.op:
         fn = run_op_tiles if args.op == "tiles3" else run_op_bench
         print(json.dumps(fn(args)), flush=True)
