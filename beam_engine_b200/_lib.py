@@ -116,6 +116,8 @@ _SIGS = {
     "be_comm_create": (C.c_int, [C.c_int, C.c_int, i64, C.c_int, C.c_int, vp, C.POINTER(vp)]),
     "be_comm_open": (C.c_int, [vp, vp]),
     "be_comm_slot": (vp, [vp, C.c_int]),
+    "be_comm_topk_layout": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_int64)]),
+    "be_comm_topk_merge": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]),
     "be_comm_flags": (vp, [vp]),
     "be_comm_close_peers": (C.c_int, [vp]),
     "be_comm_destroy": (C.c_int, [vp]),

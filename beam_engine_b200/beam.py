@@ -484,7 +484,7 @@ class BeamSearchGenerator:
         vocab-parallel across the tensor-parallel group when the model is sharded."""
         m = self.model
         return vocab_parallel_log_softmax_topk(logits, k, getattr(m, "v0", 0), getattr(m, "tp", None),
-                                               temperature)
+                                               temperature, getattr(m, "comm", None))
 
     def _topk(self, logits, k, temperature):
         vals, idx = self._logprob_topk(logits, k, temperature)
@@ -754,7 +754,9 @@ class BeamSearchGenerator:
         if not (ok and sg.fits(n, k, temperature, info)):
             off = step_plan_offset(n)
             size = off + 65536
-            cl = sg.caps["cluster"] if same else -1
+            # BE_ATTN_CLUSTER: cluster size of new step graphs (-1: the planner's
+            # choice, 0: the merge kernel, 2..16)
+            cl = sg.caps["cluster"] if same else int(os.environ.get("BE_ATTN_CLUSTER", "-1"))
             while True:
                 probe = np.empty(size, np.int32)
                 got = fill(probe.ctypes.data, size, off, cl)

@@ -217,6 +217,85 @@ __global__ void __launch_bounds__(COMM_THREADS) allreduce_rmsnorm_kernel(
   }
 }
 
+
+// Vocabulary-parallel scoring exchange: every rank's be_logsoftmax_topk wrote
+// its slice's top k (value desc, global id asc), row max and sum of
+// exponentials into its slot (layout of comm_topk_layout).  One CTA per row:
+// the log-sum-exp over the ranks (rank order, identical bits on every rank),
+// then every candidate's rank among all ranks' lists by binary search; ranks
+// 0..k-1 are written as log-probabilities with their ids.
+struct TopkSlot {
+  int64_t idx_off, val_off, max_off, sum_off;   // bytes from the slot start
+};
+__host__ __device__ inline TopkSlot comm_topk_layout(int rows, int k) {
+  TopkSlot t;
+  t.idx_off = 0;
+  t.val_off = (int64_t)rows * k * 8;
+  t.max_off = t.val_off + (int64_t)rows * k * 4;
+  t.sum_off = t.max_off + (int64_t)rows * 4;
+  return t;
+}
+constexpr int COMM_TOPK_MAX = 64;
+
+__device__ __forceinline__ bool topk_better(float a, int64_t ia, float b, int64_t ib) {
+  return a > b || (a == b && ia < ib);
+}
+
+__global__ void __launch_bounds__(128) topk_merge_kernel(CommArgs a, int rows, int k,
+                                                         float* __restrict__ out_val,
+                                                         int64_t* __restrict__ out_idx) {
+  const int cta = blockIdx.x;
+  pdl_wait();                      // the slices' top-k come from the kernel before this one
+  if (!comm_barrier(a, cta)) return;
+  __shared__ float sv[COMM_MAX_RANKS * COMM_TOPK_MAX];
+  __shared__ int64_t si[COMM_MAX_RANKS * COMM_TOPK_MAX];
+  __shared__ float s_lse;
+  const TopkSlot L = comm_topk_layout(rows, k);
+  const int tot = a.world * k;
+  for (int row = cta; row < rows; row += gridDim.x) {
+    for (int e = threadIdx.x; e < tot; e += blockDim.x) {
+      const int p = e / k, j = e - p * k;
+      const char* base = a.slot[p];
+      si[e] = __ldcv(reinterpret_cast<const long long*>(base + L.idx_off) + (int64_t)row * k + j);
+      sv[e] = __ldcv(reinterpret_cast<const float*>(base + L.val_off) + (int64_t)row * k + j);
+    }
+    if (threadIdx.x == 0) {
+      float m = -INFINITY;
+      for (int p = 0; p < a.world; ++p)
+        m = fmaxf(m, __ldcv(reinterpret_cast<const float*>(a.slot[p] + L.max_off) + row));
+      float s = 0.f;
+      for (int p = 0; p < a.world; ++p) {
+        const float mp = __ldcv(reinterpret_cast<const float*>(a.slot[p] + L.max_off) + row);
+        const float sp = __ldcv(reinterpret_cast<const float*>(a.slot[p] + L.sum_off) + row);
+        if (mp > -INFINITY) s += sp * expf(mp - m);
+      }
+      s_lse = m + logf(s);
+    }
+    __syncthreads();
+    const float lse = s_lse;
+    for (int e = threadIdx.x; e < tot; e += blockDim.x) {
+      const int p = e / k;
+      const float xv = sv[e];
+      const int64_t xi = si[e];
+      int rank = e - p * k;               // entries of its own list before it
+      for (int q = 0; q < a.world && rank < k; ++q) {
+        if (q == p) continue;
+        int lo = 0, hi = k;
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (topk_better(sv[q * k + mid], si[q * k + mid], xv, xi)) lo = mid + 1;
+          else hi = mid;
+        }
+        rank += lo;
+      }
+      if (rank < k) {
+        out_val[(int64_t)row * k + rank] = xv - lse;
+        out_idx[(int64_t)row * k + rank] = xi;
+      }
+    }
+    __syncthreads();               // sv / si / s_lse are reused by the next row
+  }
+}
 }  // namespace be
 
 using namespace be;
@@ -367,6 +446,55 @@ extern "C" int be_comm_allreduce_rmsnorm(be_comm* c, int slot, void* residual, c
       BE_CUDA_CHECK(launch_pdl(allreduce_rmsnorm_kernel<float>, grid, threads, 0, st,
           a, (float*)residual, (const float*)norm_w, (float*)out, rows, hidden, eps));
   }
+  BE_LAUNCH_CHECK();
+  return BE_OK;
+}
+
+extern "C" int be_comm_topk_layout(int rows, int k, int64_t* offsets) {
+  if (rows < 0 || k < 1 || !offsets) {
+    set_error("be_comm_topk_layout: invalid arguments");
+    return BE_EINVAL;
+  }
+  const TopkSlot t = comm_topk_layout(rows, k);
+  offsets[0] = t.idx_off;
+  offsets[1] = t.val_off;
+  offsets[2] = t.max_off;
+  offsets[3] = t.sum_off;
+  return BE_OK;
+}
+
+extern "C" int be_comm_topk_merge(be_comm* c, int slot, int rows, int k, float* out_val,
+                                  int64_t* out_idx, void* stream) {
+  if (!c || slot < 0 || slot >= c->num_slots || rows < 0 || k < 1 || k > COMM_TOPK_MAX ||
+      !out_val || !out_idx || c->world * k > COMM_MAX_RANKS * COMM_TOPK_MAX) {
+    set_error("be_comm_topk_merge: invalid arguments (k <= %d)", COMM_TOPK_MAX);
+    return BE_EINVAL;
+  }
+  const TopkSlot t = comm_topk_layout(rows, k);
+  if (t.sum_off + (int64_t)rows * 4 > c->slot_bytes) {
+    set_error("be_comm_topk_merge: %d rows x top-%d do not fit a %lld-byte slot", rows, k,
+              (long long)c->slot_bytes);
+    return BE_EINVAL;
+  }
+  for (int p = 0; p < c->world; ++p)
+    if (!c->peer[p]) {
+      set_error("be_comm_topk_merge: rank %d not opened (be_comm_open)", p);
+      return BE_EINVAL;
+    }
+  if (rows == 0) return BE_OK;
+  CommArgs a = {};
+  for (int p = 0; p < c->world; ++p) {
+    a.flags_out[p] = reinterpret_cast<uint32_t*>(c->peer[p]);
+    a.slot[p] = c->peer[p] + c->flags_bytes + (size_t)slot * c->slot_bytes;
+  }
+  a.flags_in = reinterpret_cast<uint32_t*>(c->base);
+  a.counter = reinterpret_cast<uint32_t*>(c->base + (size_t)c->max_ctas * COMM_MAX_RANKS * 4);
+  a.rank = c->rank;
+  a.world = c->world;
+  a.max_ctas = c->max_ctas;
+  const int grid = std::min(rows, c->max_ctas);
+  BE_CUDA_CHECK(launch_pdl(topk_merge_kernel, grid, 128, 0, (cudaStream_t)stream, a, rows, k,
+                           out_val, out_idx));
   BE_LAUNCH_CHECK();
   return BE_OK;
 }

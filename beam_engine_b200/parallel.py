@@ -70,7 +70,9 @@ class PeerAllReduce:
         self.slot_bytes = int(slot_bytes)
         h = (C.c_char * 64)()
         ptr = C.c_void_p()
-        check(lib().be_comm_create(tp.size, tp.rank, self.slot_bytes, 2, max_ctas, h,
+        # slots 0 / 1 alternate between the all-reduces; slot 2 holds the
+        # vocabulary-parallel scoring exchange
+        check(lib().be_comm_create(tp.size, tp.rank, self.slot_bytes, 3, max_ctas, h,
                                    C.byref(ptr)), "be_comm_create")
         self.ptr = ptr
         handles = [None] * tp.size
@@ -99,6 +101,26 @@ class PeerAllReduce:
     def fits(self, rows: int, hidden: int, elt: int) -> bool:
         return rows * hidden * elt <= self.slot_bytes
 
+    TOPK_SLOT = 2
+
+    def topk_addresses(self, rows: int, k: int):
+        """Device addresses (ids, values, row max, row sum) in this rank's scoring
+        slot for ``be_logsoftmax_topk``'s slice outputs, or None if they do not fit."""
+        import ctypes as C
+        from ._lib import check, lib
+        if k > 64 or rows * (12 * k + 8) > self.slot_bytes:
+            return None
+        off = (C.c_int64 * 4)()
+        check(lib().be_comm_topk_layout(rows, k, off), "be_comm_topk_layout")
+        base = lib().be_comm_slot(self.ptr, self.TOPK_SLOT)
+        return [base + off[i] for i in range(4)]
+
+    def topk_merge(self, rows: int, k: int, out_val: torch.Tensor, out_idx: torch.Tensor,
+                   stream) -> None:
+        from ._lib import check, lib
+        check(lib().be_comm_topk_merge(self.ptr, self.TOPK_SLOT, rows, k, out_val.data_ptr(),
+                                       out_idx.data_ptr(), stream), "be_comm_topk_merge")
+
     def close(self):
         """Collective teardown: unmap the peers, wait for every rank, free."""
         from ._lib import lib
@@ -112,18 +134,21 @@ class PeerAllReduce:
 
 
 def vocab_parallel_log_softmax_topk(logits: torch.Tensor, k: int, vocab_offset: int,
-                                    tp: TensorParallel | None, temperature: float = 1.0):
+                                    tp: TensorParallel | None, temperature: float = 1.0,
+                                    comm: "PeerAllReduce | None" = None):
     """``topk(log_softmax(logits_full / temperature), k)`` from a vocabulary
     slice per rank.
 
     ``logits`` is [n, V_local] float32 holding columns [vocab_offset,
     vocab_offset + V_local) of the full logits.  Returns (values [n, k] f32,
     global ids [n, k] int64), identical on every rank.  CUDA tensors go through
-    the fused ``be_logsoftmax_topk`` kernel; CPU tensors (gloo tests) through
-    torch."""
+    the fused ``be_logsoftmax_topk`` kernel, and with a peer communicator
+    (``comm``) the ranks' slices meet in one ``be_comm_topk_merge`` launch
+    instead of NCCL collectives; CPU tensors (gloo tests) go through torch."""
     sharded = tp is not None and tp.size > 1
     if logits.is_cuda:
-        return _fused(logits, k, vocab_offset, tp if sharded else None, temperature)
+        return _fused(logits, k, vocab_offset, tp if sharded else None, temperature,
+                      comm if sharded else None)
     if temperature != 1.0:
         logits = logits / temperature
     if not sharded:
@@ -143,7 +168,7 @@ def vocab_parallel_log_softmax_topk(logits: torch.Tensor, k: int, vocab_offset: 
     return v2 - lse[:, None], torch.gather(ig, 1, sel)
 
 
-def _fused(logits, k, vocab_offset, tp, temperature):
+def _fused(logits, k, vocab_offset, tp, temperature, comm=None):
     import ctypes as C
     from ._lib import check, lib
     if logits.dtype != torch.float32 or logits.stride(1) != 1:
@@ -158,6 +183,14 @@ def _fused(logits, k, vocab_offset, tp, temperature):
         check(lib().be_logsoftmax_topk(logits.data_ptr(), logits.stride(0), n, v, float(temperature),
                                        kl, vocab_offset, 1, vals.data_ptr(), idx.data_ptr(), None,
                                        None, st), "be_logsoftmax_topk")
+        return vals, idx
+    addr = comm.topk_addresses(n, kl) if comm is not None and kl == k else None
+    if addr is not None:
+        # the slice's top-k, max and sum go straight into this rank's scoring slot
+        check(lib().be_logsoftmax_topk(logits.data_ptr(), logits.stride(0), n, v,
+                                       float(temperature), kl, vocab_offset, 0, addr[1], addr[0],
+                                       addr[2], addr[3], st), "be_logsoftmax_topk")
+        comm.topk_merge(n, k, vals, idx, st)
         return vals, idx
     m = torch.empty(n, dtype=torch.float32, device=dev)
     s = torch.empty(n, dtype=torch.float32, device=dev)

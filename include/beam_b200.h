@@ -577,6 +577,21 @@ int be_comm_allreduce_rmsnorm(be_comm* comm, int slot, void* residual, const voi
                               void* out, int rows, int hidden, float eps, int dtype,
                               void* stream);
 
+/* Vocabulary-parallel scoring over the same peer buffer, replacing the two
+ * all-reduces and two all-gathers of the distributed log-softmax / top-k
+ * (beam.py:266-317 scoring, with the vocabulary sharded over the ranks).
+ * Each rank's be_logsoftmax_topk (full_vocab = 0) writes into this rank's slot
+ * at the byte offsets be_comm_topk_layout gives (offsets[0..3]: int64 global
+ * ids [rows][k], float values [rows][k], float row max [rows], float row sum of
+ * exponentials [rows]); be_comm_topk_merge then writes, on every rank, the
+ * global top k as log-probabilities (value desc, id asc) with their ids.
+ * k <= 64.  The slot must not be the one the last all-reduce before it used,
+ * and the next call that writes this slot must come after another call of
+ * this communicator (a slot of its own is simplest).                         */
+int be_comm_topk_layout(int rows, int k, int64_t* offsets);
+int be_comm_topk_merge(be_comm* comm, int slot, int rows, int k, float* out_val,
+                       int64_t* out_idx, void* stream);
+
 /* One host call per decode step after the device's top-k: vanilla selection
  * of every prompt (be_vanilla_select_segments, beam_strategy.py:433-488) then
  * the trie update (be_beam_update, beam_state.py:101-209).  new_leaf /

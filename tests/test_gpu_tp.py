@@ -3,7 +3,8 @@ model sharded over two GPUs selects the same beams as the unsharded model on
 one GPU, in fp32 (eager step) and in bf16 (CUDA-graph step, NCCL all-reduces
 captured in the graph; scores within 2e-2), with the all-reduces on NCCL or
 on the fused peer-memory kernel (be_comm_allreduce_rmsnorm, which is also
-checked on its own against torch on every rank).  Skipped on boxes with fewer than
+checked on its own against torch on every rank, as is the vocabulary-parallel
+scoring exchange be_comm_topk_merge).  Skipped on boxes with fewer than
 two GPUs.  NVLS is switched off: a rank dying while bound to a multicast
 object has faulted peers on this kind of box."""
 import os
@@ -63,6 +64,34 @@ def _check_peer_kernel(model, tp, dtype, rank):
     dist.barrier()
 
 
+def _check_peer_topk(model, tp, rank):
+    """be_comm_topk_merge (through vocab_parallel_log_softmax_topk with the peer
+    communicator) against torch log_softmax -> topk on the gathered full rows:
+    the same ids on every rank, values within 1e-5; rows with ties across the
+    ranks' slices come out by smaller id first."""
+    import torch.distributed as dist
+    from beam_engine_b200.parallel import vocab_parallel_log_softmax_topk
+    dev = model.device
+    n, v, k = 37, 1000, 16
+    gs = torch.Generator().manual_seed(77)
+    full = (torch.randn(n, v * tp.size, generator=gs) * 3).to(dev)
+    full[0, :] = 0.0                       # every column ties
+    full[1, [5, v + 5, 2 * v - 1]] = 50.0  # a three-way tie across the slices
+    mine = full[:, rank * v:(rank + 1) * v].contiguous()
+    for _ in range(2):                     # twice: the scoring slot is reused
+        vals, idx = vocab_parallel_log_softmax_topk(mine, k, rank * v, tp, 1.0, model.comm)
+        ref_v, ref_i = torch.topk(torch.log_softmax(full.double(), -1), k, -1)
+        # torch.topk's order among equal values is unspecified: compare as (value, id) sorted
+        assert idx[0].tolist() == list(range(k)), idx[0].tolist()
+        assert idx[1, :3].tolist() == [5, v + 5, 2 * v - 1]
+        assert torch.equal(idx[2:], ref_i[2:])
+        assert (vals.double() - ref_v).abs().max().item() < 1e-5
+        all_i = [torch.empty_like(idx) for _ in range(tp.size)]
+        dist.all_gather(all_i, idx)
+        assert all(torch.equal(all_i[0], t) for t in all_i)
+    dist.barrier()
+
+
 def _run(dtype_name, tp_rank, world, port, q, comm="nccl"):
     import torch.distributed as dist
     from beam_engine_b200.beam import BeamSearchGenerator
@@ -87,6 +116,7 @@ def _run(dtype_name, tp_rank, world, port, q, comm="nccl"):
         if world > 1 and comm == "peer":
             assert model.enable_peer_allreduce() is not None
             _check_peer_kernel(model, tp, dtype, tp_rank)
+            _check_peer_topk(model, tp, tp_rank)
         g = torch.Generator().manual_seed(2)
         prompts = [torch.randint(0, 1024, (40,), generator=g).tolist() for _ in range(2)]
         gen = BeamSearchGenerator(model, None, VanillaBeamSearchStrategy(), page_size=16,
