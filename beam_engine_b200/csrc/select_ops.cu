@@ -3,12 +3,14 @@
 // The reference scores every beam as `logits / temperature -> log_softmax ->
 // topk(2W)` (beam.py:266-317) with three library ops; torch's top-k alone is
 // ~10 launches per call on a [128, 128256] block.  Here one CTA owns one row:
-//   * every thread streams its part of the row with 16-byte loads, keeping a
-//     running max / sum of exponentials (online rescale) for the log-sum-exp;
-//   * every warp keeps the top KMAX (value, id) pairs of its chunk as a list
-//     sorted by (value desc, id asc), KMAX / 32 entries per lane; a candidate
-//     enters only if it beats the current k-th entry (ballot), so after the
-//     first few hundred elements almost nothing is inserted;
+//   * pass 1 streams the row from HBM with 16-byte loads: each lane's maximum;
+//     from the 1024 lane maxima the row max and tau, the k-th largest lane
+//     maximum -- a lower bound of the row's k-th largest value;
+//   * pass 2 reads the row again (from L2): the sum of exponentials against the
+//     exact max, and every warp keeps the top KMAX (value, id) pairs of its
+//     chunk as a list sorted by (value desc, id asc), KMAX / 32 entries per
+//     lane, offered only the values that reach tau (a handful per warp,
+//     instead of a few hundred insertions while a list fills up);
 //   * the warps' lists meet in shared memory, where every entry finds its rank
 //     among all lists by binary search (no serial merge);
 //   * out: log-probabilities (x - max) - log(sum) of the k best with global
@@ -110,7 +112,7 @@ __global__ void __launch_bounds__(TK_THREADS) logsoftmax_topk_kernel(
     float* __restrict__ row_max, float* __restrict__ row_sum) {
   __shared__ float s_v[TK_WARPS][TK_KMAX];
   __shared__ int s_i[TK_WARPS][TK_KMAX];
-  __shared__ float s_m[TK_WARPS], s_s[TK_WARPS];
+  __shared__ float s_s[TK_WARPS];
   pdl_wait();
   const int row = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -120,80 +122,99 @@ __global__ void __launch_bounds__(TK_THREADS) logsoftmax_topk_kernel(
   const int per_warp = ((v + TK_WARPS - 1) / TK_WARPS + 127) / 128 * 128;
   const int c0 = min(v, warp * per_warp), c1 = min(v, c0 + per_warp);
   const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  __shared__ float s_lmax[TK_THREADS];
+  __shared__ float s_tau;
+  auto load4 = [&](int col) {   // 4 scaled values from col (-inf past the chunk's end)
+    float4 r;
+    if (vec && col + 3 < c1) {
+      r = __ldcg(reinterpret_cast<const float4*>(x + col));   // kept in L2 for the second pass
+    } else {
+      r.x = col < c1 ? x[col] : -INFINITY;
+      r.y = col + 1 < c1 ? x[col + 1] : -INFINITY;
+      r.z = col + 2 < c1 ? x[col + 2] : -INFINITY;
+      r.w = col + 3 < c1 ? x[col + 3] : -INFINITY;
+    }
+    if (scale) {
+      r.x = r.x / temperature;
+      r.y = r.y / temperature;
+      r.z = r.z / temperature;
+      r.w = r.w / temperature;
+    }
+    return r;
+  };
+  // Pass 1 (from HBM): each lane's maximum.  TK_DEPTH 16-byte loads per lane in
+  // flight before any is used.
+  constexpr int TK_DEPTH = 4;
+  float lmax = -INFINITY;
+  for (int base0 = c0; base0 < c1; base0 += 128 * TK_DEPTH) {
+    float4 buf[TK_DEPTH];
+#pragma unroll
+    for (int u = 0; u < TK_DEPTH; ++u) buf[u] = load4(base0 + u * 128 + lane * 4);
+#pragma unroll
+    for (int u = 0; u < TK_DEPTH; ++u)
+      lmax = fmaxf(lmax, fmaxf(fmaxf(buf[u].x, buf[u].y), fmaxf(buf[u].z, buf[u].w)));
+  }
+  // The row max, and tau = the k-th largest of the 1024 lane maxima: they are
+  // k distinct elements of the row at least as large as tau, so tau is a lower
+  // bound of the row's k-th largest value and nothing below it can be selected.
+  s_lmax[tid] = lmax;
+  __syncthreads();
+  {
+    int above = 0, tie_before = 0;
+    for (int j = 0; j < TK_THREADS; ++j) {      // every thread reads the same word: broadcast
+      const float o = s_lmax[j];
+      above += o > lmax;
+      tie_before += (o == lmax) & (j < tid);
+    }
+    if (above + tie_before == k - 1) s_tau = lmax;
+  }
+  float m = -INFINITY;
+  for (int j = lane; j < TK_THREADS; j += 32) m = fmaxf(m, s_lmax[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __syncthreads();
+  const float tau = s_tau;
+  // Pass 2 (from L2): the sum of exponentials against the exact max, and the
+  // warp's top-k list offered only what reaches tau (a handful per warp).
   WarpTopK tk;
   tk.init();
   float tv = -INFINITY;
   int ti = INT_MAX;
-  float m = -INFINITY, s = 0.f;
-  auto consume = [&](float val, int col, bool valid) {
-    if (scale) val = val / temperature;
-    if (valid) {
-      if (val > m) {
-        s = s * __expf(m - val) + 1.f;
-        m = val;
-      } else {
-        s += __expf(val - m);
-      }
-    }
-    tk.offer(valid ? val : -INFINITY, valid ? col : INT_MAX, k, tv, ti);
-  };
-  // TK_DEPTH 16-byte loads per lane in flight before any is consumed: the row is
-  // read at memory speed instead of one DRAM round trip per 128 elements
-  constexpr int TK_DEPTH = 4;
+  float s = 0.f;
+  const float m0 = m == -INFINITY ? 0.f : m;   // a row of -inf sums to 0, not NaN
   for (int base0 = c0; base0 < c1; base0 += 128 * TK_DEPTH) {
     float4 buf[TK_DEPTH];
 #pragma unroll
+    for (int u = 0; u < TK_DEPTH; ++u) buf[u] = load4(base0 + u * 128 + lane * 4);
+#pragma unroll
     for (int u = 0; u < TK_DEPTH; ++u) {
+      if (base0 + u * 128 >= c1) break;              // warp-uniform
       const int col = base0 + u * 128 + lane * 4;
-      if (vec && col + 3 < c1) {
-        buf[u] = __ldcs(reinterpret_cast<const float4*>(x + col));   // read once: streaming
-      } else {
-        buf[u].x = col < c1 ? x[col] : -INFINITY;
-        buf[u].y = col + 1 < c1 ? x[col + 1] : -INFINITY;
-        buf[u].z = col + 2 < c1 ? x[col + 2] : -INFINITY;
-        buf[u].w = col + 3 < c1 ? x[col + 3] : -INFINITY;
+      const float e[4] = {buf[u].x, buf[u].y, buf[u].z, buf[u].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s += __expf(e[i] - m0);   // -inf past the end adds 0
+      const float bm = fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3]));
+      if (__any_sync(0xffffffffu, bm >= tau)) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const bool in = col + i < c1 && e[i] >= tau;
+          tk.offer(in ? e[i] : -INFINITY, in ? col + i : INT_MAX, k, tv, ti);
+        }
       }
     }
-#pragma unroll
-    for (int u = 0; u < TK_DEPTH; ++u) {
-      const int col = base0 + u * 128 + lane * 4;
-      if (base0 + u * 128 >= c1) break;              // warp-uniform
-      consume(buf[u].x, col, col < c1);
-      consume(buf[u].y, col + 1, col + 1 < c1);
-      consume(buf[u].z, col + 2, col + 2 < c1);
-      consume(buf[u].w, col + 3, col + 3 < c1);
-    }
   }
-  // log-sum-exp: warp, then block
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    const float mm = fmaxf(m, m2);
-    s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
-    m = mm;
-  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
 #pragma unroll
   for (int q = 0; q < TK_PER_LANE; ++q) {
     s_v[warp][q * 32 + lane] = tk.v[q];
     s_i[warp][q * 32 + lane] = tk.id[q];
   }
-  if (lane == 0) {
-    s_m[warp] = m;
-    s_s[warp] = s;
-  }
+  if (lane == 0) s_s[warp] = s;
   __syncthreads();
-  // block log-sum-exp, reduced by every warp (32 partials)
-  m = s_m[lane];
-  s = s_s[lane];
+  s = s_s[lane];   // every warp sums the 32 warp partials (same order: same bits)
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    const float mm = fmaxf(m, m2);
-    s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
-    m = mm;
-  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   const float log_s = logf(s);
   // the block's top k: the first k entries of every warp's sorted list are
   // ranked against all other lists at once (rank = entries strictly better,
