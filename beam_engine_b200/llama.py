@@ -24,7 +24,7 @@ from . import _lib
 
 from ._lib import check, lib
 from .page_table import dtype_code, stream_ptr
-from .weights import random_llama_weights
+from .weights import iter_random_llama_weights
 
 
 def inv_freq_table(head_dim, theta, device):
@@ -52,8 +52,6 @@ class BeamLlama:
         self.H = c["hidden_size"]
         self.eps = float(c["rms_norm_eps"])
         self.vocab = c["vocab_size"]
-        if weights is None:
-            weights = random_llama_weights(c, seed=seed, dtype=dtype, device=self.device)
         D, Hq, Hkv, F = self.D, self.Hq, self.Hkv, self.F
 
         def shard_rows(w, n_per, idx):   # output-feature shard
@@ -62,26 +60,54 @@ class BeamLlama:
         def prep(t):
             return t.to(device=self.device, dtype=dtype).contiguous()
 
-        self.w_qkv, self.w_o, self.w_gu, self.w_down, self.n_in, self.n_post = [], [], [], [], [], []
-        for i in range(self.L):
-            p = f"layers.{i}."
-            q = shard_rows(weights[p + "q"], Hq * D, tr)
-            k = shard_rows(weights[p + "k"], Hkv * D, tr)
-            v = shard_rows(weights[p + "v"], Hkv * D, tr)
-            self.w_qkv.append(prep(torch.cat([q, k, v], 0)))
-            self.w_o.append(prep(weights[p + "o"][:, tr * Hq * D:(tr + 1) * Hq * D]))
-            g = shard_rows(weights[p + "gate"], F, tr)
-            u = shard_rows(weights[p + "up"], F, tr)
-            self.w_gu.append(prep(torch.cat([g, u], 0)))
-            self.w_down.append(prep(weights[p + "down"][:, tr * F:(tr + 1) * F]))
-            self.n_in.append(prep(weights[p + "input_norm"]))
-            self.n_post.append(prep(weights[p + "post_norm"]))
-        self.embed = prep(weights["embed"])
-        self.norm = prep(weights["norm"])
         # vocab-parallel lm_head under TP (each rank scores its vocabulary slice)
         V = self.vocab
         self.v0, self.v1 = (tr * V) // ts, ((tr + 1) * V) // ts
-        self.lm_head = prep(weights["lm_head"][self.v0:self.v1])
+
+        def shard(name, w):
+            """This rank's part of one tensor, in storage of its own (a view would keep
+            the full tensor alive)."""
+            x = _shard(name, w)
+            if x.untyped_storage().nbytes() > x.numel() * x.element_size():
+                x = x.clone()
+            return x
+
+        def _shard(name, w):
+            m = name.rsplit(".", 1)[-1]
+            if m == "q":
+                return prep(shard_rows(w, Hq * D, tr))
+            if m in ("k", "v"):
+                return prep(shard_rows(w, Hkv * D, tr))
+            if m == "o":
+                return prep(w[:, tr * Hq * D:(tr + 1) * Hq * D])
+            if m in ("gate", "up"):
+                return prep(shard_rows(w, F, tr))
+            if m == "down":
+                return prep(w[:, tr * F:(tr + 1) * F])
+            if name == "lm_head":
+                return prep(w[self.v0:self.v1])
+            return prep(w)
+
+        # random init streams one tensor at a time (never the whole model on a rank)
+        items = (weights.items() if weights is not None else
+                 iter_random_llama_weights(c, seed=seed, dtype=dtype, device=self.device))
+        parts = {}
+        for name, w in items:
+            parts[name] = shard(name, w)
+            del w
+        self.w_qkv, self.w_o, self.w_gu, self.w_down, self.n_in, self.n_post = [], [], [], [], [], []
+        for i in range(self.L):
+            p = f"layers.{i}."
+            self.w_qkv.append(torch.cat([parts.pop(p + "q"), parts.pop(p + "k"),
+                                         parts.pop(p + "v")], 0).contiguous())
+            self.w_o.append(parts.pop(p + "o"))
+            self.w_gu.append(torch.cat([parts.pop(p + "gate"), parts.pop(p + "up")], 0).contiguous())
+            self.w_down.append(parts.pop(p + "down"))
+            self.n_in.append(parts.pop(p + "input_norm"))
+            self.n_post.append(parts.pop(p + "post_norm"))
+        self.embed = parts.pop("embed")
+        self.norm = parts.pop("norm")
+        self.lm_head = parts.pop("lm_head")
         self.inv_freq = inv_freq_table(D, float(c["rope_theta"]), self.device)
         self.dt = dtype_code(dtype)
         self.qkv_width = (Hq + 2 * Hkv) * D

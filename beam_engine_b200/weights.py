@@ -20,10 +20,14 @@ def weight_shapes(cfg):
             "gate": (f, h), "up": (f, h), "down": (h, f)}
 
 
-def random_llama_weights(cfg, seed=0, dtype=torch.float32, device="cpu", std=0.02, layers=None):
-    """Returns {name: tensor}.  ``layers`` limits which layer indices are made
-    (all by default); skipped layers still consume no random numbers, so a
-    partial set is NOT a prefix of the full set's stream beyond layer 0."""
+def iter_random_llama_weights(cfg, seed=0, dtype=torch.float32, device="cpu", std=0.02,
+                              layers=None):
+    """Yields (name, tensor) in drawing order, one tensor at a time, so a caller
+    that keeps only a shard of each (tensor parallelism) never holds the whole
+    model: the 70B shape is 141 GB in bf16.  ``layers`` limits which layer
+    indices are made (all by default); skipped layers still consume no random
+    numbers, so a partial set is NOT a prefix of the full set's stream beyond
+    layer 0."""
     g = torch.Generator(device=device).manual_seed(seed)
     shapes = weight_shapes(cfg)
 
@@ -32,14 +36,18 @@ def random_llama_weights(cfg, seed=0, dtype=torch.float32, device="cpu", std=0.0
         t.normal_(0.0, std, generator=g)
         return t.to(dtype)
 
-    w = {"embed": draw((cfg["vocab_size"], cfg["hidden_size"]))}
+    yield "embed", draw((cfg["vocab_size"], cfg["hidden_size"]))
     for i in range(cfg["num_hidden_layers"]):
         if layers is not None and i not in layers:
             continue
         for m in LAYER_MATS:
-            w[f"layers.{i}.{m}"] = draw(shapes[m])
-        w[f"layers.{i}.input_norm"] = torch.ones(cfg["hidden_size"], dtype=dtype, device=device)
-        w[f"layers.{i}.post_norm"] = torch.ones(cfg["hidden_size"], dtype=dtype, device=device)
-    w["norm"] = torch.ones(cfg["hidden_size"], dtype=dtype, device=device)
-    w["lm_head"] = draw((cfg["vocab_size"], cfg["hidden_size"]))
-    return w
+            yield f"layers.{i}.{m}", draw(shapes[m])
+        yield f"layers.{i}.input_norm", torch.ones(cfg["hidden_size"], dtype=dtype, device=device)
+        yield f"layers.{i}.post_norm", torch.ones(cfg["hidden_size"], dtype=dtype, device=device)
+    yield "norm", torch.ones(cfg["hidden_size"], dtype=dtype, device=device)
+    yield "lm_head", draw((cfg["vocab_size"], cfg["hidden_size"]))
+
+
+def random_llama_weights(cfg, seed=0, dtype=torch.float32, device="cpu", std=0.02, layers=None):
+    """Returns {name: tensor} (the tensors of iter_random_llama_weights)."""
+    return dict(iter_random_llama_weights(cfg, seed, dtype, device, std, layers))

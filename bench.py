@@ -125,6 +125,25 @@ class Clocks:
                 "samples": len(sm)}
 
 
+def write_kernel_trace(prof, path, rank, steps):
+    """Per-kernel device time of the timed steps (CUPTI activity records via
+    torch.profiler, graph-replayed kernels included), one table per rank.  A
+    traced run is for the table only: its step time is not a bench value."""
+    import collections
+    tot = collections.defaultdict(lambda: [0, 0.0])
+    for e in prof.events():
+        if str(e.device_type).endswith("CUDA"):
+            t = tot[e.name[:100]]
+            t[0] += 1
+            t[1] += e.device_time_total
+    allt = sum(v[1] for v in tot.values()) or 1.0
+    with open(f"{path}.rank{rank}.txt", "w") as f:
+        f.write(f"timed steps {steps}; kernel time per step {allt / steps:.0f} us\n")
+        f.write("us/step | launches/step | share | kernel\n")
+        for name, (n, us) in sorted(tot.items(), key=lambda kv: -kv[1][1]):
+            f.write(f"{us / steps:9.1f} | {n / steps:6.1f} | {100 * us / allt:5.1f}% | {name}\n")
+
+
 def run_b200(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -207,6 +226,10 @@ def run_b200(args, rank, world, local_rank):
             if world > 1:
                 dist.barrier()
             clocks.start()
+            if args.kernel_trace:
+                from torch.profiler import ProfilerActivity, profile
+                ev["prof"] = profile(activities=[ProfilerActivity.CUDA])
+                ev["prof"].__enter__()
             ev["start"] = torch.cuda.Event(enable_timing=True)
             ev["start"].record()
             timing["on"] = True
@@ -220,6 +243,9 @@ def run_b200(args, rank, world, local_rank):
             if world > 1:
                 dist.barrier()
             ev["clocks"] = clocks.stop()
+            if args.kernel_trace:
+                ev["prof"].__exit__(None, None, None)
+                write_kernel_trace(ev["prof"], args.kernel_trace, rank, K)
 
     # -- timed decode run (inputs resident: model, pages) ------------------
     gen.generate_ids(prompts, BEAM, max_new_tokens=W + K + 1, on_step=on_step)
@@ -810,6 +836,9 @@ def main():
                     help="--op tiles3: heads of one rank under this tensor parallelism")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--split", type=int, default=0)
+    ap.add_argument("--kernel-trace", default=None, metavar="PATH",
+                    help="write per-kernel device time of the timed steps to PATH.rank<r>.txt "
+                         "(torch.profiler; the traced run's numbers are not bench values)")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end pass and print a short line (for profiling)")
     args = ap.parse_args()
