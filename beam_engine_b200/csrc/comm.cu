@@ -61,7 +61,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 // release fence at system scope cost ~10 us per call here.)  The wait is an
 // acquire load, so this thread's later reads stay behind it; the block
 // barrier after it orders the other threads' reads.
-__device__ bool comm_barrier(const CommArgs& a, int cta) {
+__device__ bool comm_barrier(const CommArgs& a, int cta, uint32_t* epoch_out = nullptr) {
   __shared__ uint32_t epoch;
   __shared__ int ok;
   const int t = threadIdx.x;
@@ -71,6 +71,7 @@ __device__ bool comm_barrier(const CommArgs& a, int cta) {
   }
   __syncthreads();
   const uint32_t e = epoch;
+  if (epoch_out) *epoch_out = e;
   if (t < a.world) {
     st_relaxed_sys(a.flags_out[t] + (size_t)cta * COMM_MAX_RANKS + a.rank, e);
     const uint32_t* f = a.flags_in + (size_t)cta * COMM_MAX_RANKS + t;
@@ -218,6 +219,130 @@ __global__ void __launch_bounds__(COMM_THREADS) allreduce_rmsnorm_kernel(
 }
 
 
+// Two-shot form for many ranks (one-shot reads world - 1 full partials per
+// rank over NVLink: 7 MiB per call at 8 ranks).  Row r belongs to rank
+// r % world: its owner sums the ranks' partial rows, adds the residual and
+// stores the new residual row over its own partial row (only the owner reads
+// that row of its slot), then signals every rank; the other ranks wait for the
+// owner's signal and copy the row from its slot.  Every rank then applies the
+// RMSNorm to its copy: the same bits as the one-shot kernel, with about
+// 2 x (world - 1) / world rows read per rank instead of world - 1.
+// Row flags: uint32 [max_ctas] after the barrier flags and counters.
+__device__ __forceinline__ uint32_t* comm_row_flags(uint32_t* flags, int max_ctas) {
+  return flags + (size_t)max_ctas * COMM_MAX_RANKS + max_ctas;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(COMM_THREADS) allreduce_rmsnorm_2shot_kernel(
+    CommArgs a, T* __restrict__ residual, const T* __restrict__ w, T* __restrict__ out, int rows,
+    int H, float eps) {
+  constexpr int V = 16 / sizeof(T);
+  const int row = blockIdx.x;      // rows <= max_ctas: one CTA per row
+  pdl_wait();                      // the partials come from the kernel before this one
+  uint32_t e = 0;
+  if (!comm_barrier(a, row, &e)) return;
+  __shared__ float red[32];
+  __shared__ int ok;
+  const int owner = row % a.world;
+  const int64_t base = (int64_t)row * H;
+  float cache[COMM_NV][V];
+  float ss = 0.f;
+  if (owner == a.rank) {
+    T* mine = reinterpret_cast<T*>(const_cast<char*>(a.slot[a.rank]));
+#pragma unroll
+    for (int nv = 0; nv < COMM_NV; ++nv) {
+      const int c = (threadIdx.x + nv * blockDim.x) * V;
+      if (c >= H) break;
+      int4 raw[COMM_MAX_RANKS];
+#pragma unroll
+      for (int p = 0; p < COMM_MAX_RANKS; ++p)
+        if (p < a.world)
+          raw[p] = __ldcv(reinterpret_cast<const int4*>(
+              reinterpret_cast<const T*>(a.slot[p]) + base + c));
+      float sum[V];
+      unpack16<T>(raw[0], sum);
+#pragma unroll
+      for (int p = 1; p < COMM_MAX_RANKS; ++p) {
+        if (p >= a.world) break;
+        float t[V];
+        unpack16<T>(raw[p], t);
+#pragma unroll
+        for (int i = 0; i < V; ++i) sum[i] += t[i];
+      }
+      float x[V];
+      load16(residual + base + c, x);
+#pragma unroll
+      for (int i = 0; i < V; ++i) x[i] = to_f(from_f<T>(x[i] + to_f(from_f<T>(sum[i]))));
+      store16(residual + base + c, x);
+      store16(mine + base + c, x);            // the new residual row, for the other ranks
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        ss += x[i] * x[i];
+        cache[nv][i] = x[i];
+      }
+    }
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");   // the row is in this GPU's L2
+    __syncthreads();
+    if (threadIdx.x < a.world && threadIdx.x != a.rank)
+      st_relaxed_sys(comm_row_flags(a.flags_out[threadIdx.x], a.max_ctas) + row, e);
+  } else {
+    if (threadIdx.x == 0) {
+      ok = 1;
+      const uint32_t* f = comm_row_flags(a.flags_in, a.max_ctas) + row;
+      const uint64_t t0 = comm_gtimer();
+      int polls = 0;
+      while ((int32_t)(ld_acquire_sys(f) - e) < 0) {
+        if (++polls == 64) {
+          polls = 0;
+          if (comm_gtimer() - t0 > kCommWaitNs) {
+            atomicCAS(&g_device_status, 0, BE_EDEVICE_TIMEOUT);
+            ok = 0;
+            break;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (!ok) return;
+    const T* src = reinterpret_cast<const T*>(a.slot[owner]);
+#pragma unroll
+    for (int nv = 0; nv < COMM_NV; ++nv) {
+      const int c = (threadIdx.x + nv * blockDim.x) * V;
+      if (c >= H) break;
+      float x[V];
+      unpack16<T>(__ldcv(reinterpret_cast<const int4*>(src + base + c)), x);
+      store16(residual + base + c, x);
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        ss += x[i] * x[i];
+        cache[nv][i] = x[i];
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)H + eps);
+#pragma unroll
+  for (int nv = 0; nv < COMM_NV; ++nv) {
+    const int c = (threadIdx.x + nv * blockDim.x) * V;
+    if (c >= H) break;
+    float wv[V], r[V];
+    load16(w + c, wv);
+#pragma unroll
+    for (int i = 0; i < V; ++i) r[i] = wv[i] * to_f(from_f<T>(cache[nv][i] * inv));
+    store16(out + base + c, r);
+  }
+}
+
 // Vocabulary-parallel scoring exchange: every rank's be_logsoftmax_topk wrote
 // its slice's top k (value desc, global id asc), row max and sum of
 // exponentials into its slot (layout of comm_topk_layout).  One CTA per row:
@@ -311,7 +436,8 @@ struct be_comm {
 };
 
 static size_t comm_flags_bytes(int max_ctas) {
-  const size_t b = (size_t)max_ctas * COMM_MAX_RANKS * 4 + (size_t)max_ctas * 4;
+  // barrier flags [cta][rank], per-CTA counters, two-shot row flags [cta]
+  const size_t b = (size_t)max_ctas * COMM_MAX_RANKS * 4 + 2 * (size_t)max_ctas * 4;
   return (b + 255) / 256 * 256;
 }
 
@@ -432,6 +558,31 @@ extern "C" int be_comm_allreduce_rmsnorm(be_comm* c, int slot, void* residual, c
   const int grid = std::min(rows, c->max_ctas);
   const int threads = std::min(COMM_THREADS, std::max(32, (hidden / V + 31) / 32 * 32));
   cudaStream_t st = (cudaStream_t)stream;
+  // two-shot from BE_COMM_TWO_SHOT_WORLD ranks on (default 4; 0 = never)
+  static const int two_shot_world = [] {
+    const char* v = getenv("BE_COMM_TWO_SHOT_WORLD");
+    return v ? atoi(v) : 4;
+  }();
+  if (residual && two_shot_world > 0 && c->world >= two_shot_world && rows <= c->max_ctas) {
+    switch (dtype) {
+      case BE_BF16:
+        BE_CUDA_CHECK(launch_pdl(allreduce_rmsnorm_2shot_kernel<__nv_bfloat16>, rows, threads, 0,
+                                 st, a, (__nv_bfloat16*)residual, (const __nv_bfloat16*)norm_w,
+                                 (__nv_bfloat16*)out, rows, hidden, eps));
+        break;
+      case BE_F16:
+        BE_CUDA_CHECK(launch_pdl(allreduce_rmsnorm_2shot_kernel<__half>, rows, threads, 0, st, a,
+                                 (__half*)residual, (const __half*)norm_w, (__half*)out, rows,
+                                 hidden, eps));
+        break;
+      default:
+        BE_CUDA_CHECK(launch_pdl(allreduce_rmsnorm_2shot_kernel<float>, rows, threads, 0, st, a,
+                                 (float*)residual, (const float*)norm_w, (float*)out, rows, hidden,
+                                 eps));
+    }
+    BE_LAUNCH_CHECK();
+    return BE_OK;
+  }
   switch (dtype) {
     case BE_BF16:
       BE_CUDA_CHECK(launch_pdl(allreduce_rmsnorm_kernel<__nv_bfloat16>, grid, threads, 0, st,

@@ -4,7 +4,8 @@ one GPU, in fp32 (eager step) and in bf16 (CUDA-graph step, NCCL all-reduces
 captured in the graph; scores within 2e-2), with the all-reduces on NCCL or
 on the fused peer-memory kernel (be_comm_allreduce_rmsnorm, which is also
 checked on its own against torch on every rank, as is the vocabulary-parallel
-scoring exchange be_comm_topk_merge).  Skipped on boxes with fewer than
+scoring exchange be_comm_topk_merge), in its one-shot form and in the two-shot
+form that is the default from four ranks on.  Skipped on boxes with fewer than
 two GPUs.  NVLS is switched off: a rank dying while bound to a multicast
 object has faulted peers on this kind of box."""
 import os
@@ -113,7 +114,9 @@ def _run(dtype_name, tp_rank, world, port, q, comm="nccl"):
                    hidden_size=512)
         model = BeamLlama(cfg, None, dtype=dtype, device=torch.device("cuda", tp_rank), seed=5,
                           tp=tp)
-        if world > 1 and comm == "peer":
+        if comm == "peer2shot":           # the two-shot kernel (default from 4 ranks) on 2
+            os.environ["BE_COMM_TWO_SHOT_WORLD"] = "2"
+        if world > 1 and comm in ("peer", "peer2shot"):
             assert model.enable_peer_allreduce() is not None
             _check_peer_kernel(model, tp, dtype, tp_rank)
             _check_peer_topk(model, tp, tp_rank)
@@ -134,8 +137,9 @@ def _run(dtype_name, tp_rank, world, port, q, comm="nccl"):
         raise
 
 
-@pytest.mark.parametrize("comm", ["nccl", "peer"])
-@pytest.mark.parametrize("dtype_name,tol", [("float32", 1e-4), ("bfloat16", 2e-2)])
+@pytest.mark.parametrize("dtype_name,tol,comm", [
+    ("float32", 1e-4, "nccl"), ("bfloat16", 2e-2, "nccl"), ("float32", 1e-4, "peer"),
+    ("bfloat16", 2e-2, "peer"), ("bfloat16", 2e-2, "peer2shot")])
 def test_tp2_matches_single_gpu(dtype_name, tol, comm):
     if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
         pytest.skip("needs two GPUs")
