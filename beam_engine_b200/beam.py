@@ -885,6 +885,15 @@ class BeamSearchGenerator:
                                     np.asarray(sc_all, np.float64))
                 seg = np.asarray(new_seg)
             self._flush_fork()
+            if getattr(self.model, "comm", None) is not None:
+                # a peer exchange whose bounded wait ran out returns without writing
+                # its rows: report it instead of returning beams from undefined states
+                st = C.c_int(0)
+                check(lib().be_device_status(C.byref(st), None), "be_device_status")
+                if st.value != 0:
+                    raise RuntimeError(
+                        f"device status {st.value} during a tensor-parallel generation (a peer "
+                        "exchange timed out or a page id was out of range); its beams are undefined")
             if on_step is not None:
                 on_step(n_steps)
         out = []

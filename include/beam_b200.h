@@ -546,7 +546,13 @@ int be_diverse_select(int nseg, const int32_t* seg_ptr, int k, const double* par
  * be_comm_allreduce_rmsnorm sums every rank's slot (plain peer loads, no
  * multicast) and applies the residual add and the norm.  Consecutive calls
  * must alternate between two slots.  A rank that stops answering makes the
- * others' barrier time out after 2 s (BE_EDEVICE_TIMEOUT in be_device_status). */
+ * others' barrier time out after 2 s (BE_EDEVICE_TIMEOUT in be_device_status);
+ * a CTA whose wait ran out returns without writing its rows, so residual / out
+ * of that call are undefined (BeamSearchGenerator raises when the status is
+ * set at the end of a tensor-parallel generation).  From 4 ranks on the call
+ * runs in a two-shot form (each row reduced by one owner rank, then copied by
+ * the others; same results); BE_COMM_TWO_SHOT_WORLD sets the rank count
+ * (0: never).                                                                */
 typedef struct be_comm be_comm;
 #define BE_IPC_HANDLE_BYTES 64
 /* Allocate this rank's flags + slots; writes its IPC handle (BE_IPC_HANDLE_BYTES)
