@@ -21,10 +21,15 @@ decode step from the two plans the host builds anyway:
   launch-level model of the work-item kernels:
   ``time = launches * t_launch + waves * t_cta + bytes / HBM``, where a wave
   is one CTA per SM (two for the tcgen05 prefix tiles), the bytes are every
-  work item's K/V plus the partial rows written and merged.  The per-CTA times
-  are the measured lifetimes of the kernels on B200 (decode shapes, Hkv 8,
-  D 128): ~15 us for a tcgen05 prefix tile, ~11 us for an all-heads suffix
-  tile, ~18 us for a slot-list (tree) tile.
+  work item's K/V plus the partial rows written and merged.  The launch,
+  per-wave and bandwidth terms are a least-squares fit
+  (``fit_work_item_model``) to 32 cascade runs on the work-item kernels on
+  B200 (``bench.py --op picker``: shared prefixes of 256-4096 tokens, 4-64
+  beams with suffixes of up to 16 or 256 tokens, Hq 32 / Hkv 8 / D 128, bf16,
+  cold L2; median error 5.5 %, largest 23 %): 6.17 us per launch, 0.60 us per
+  wave of tcgen05 prefix tiles, 2.06 us per wave of suffix tiles, bytes at an
+  effective 2 315 GB/s.  The slot-list (tree) tile's ~18 us is its measured
+  lifetime; it only matters when page-list tree plans are off.
 """
 from __future__ import annotations
 
@@ -37,10 +42,10 @@ import numpy as np
 @dataclass
 class PickerModel:
     num_sms: int = 148
-    hbm_gbs: float = 6500.0
-    t_launch_us: float = 3.0
-    t_wide_cta_us: float = 15.0      # tcgen05 prefix tile (two CTAs per SM)
-    t_narrow_cta_us: float = 11.0    # all-heads suffix tile (one CTA per SM)
+    hbm_gbs: float = 2315.0          # effective, fitted (the copy peak is ~6 540)
+    t_launch_us: float = 6.17
+    t_wide_cta_us: float = 0.60      # per wave of tcgen05 prefix tiles (two CTAs per SM)
+    t_narrow_cta_us: float = 2.06    # per wave of all-heads suffix tiles (one CTA per SM)
     t_slot_cta_us: float = 18.0      # slot-list tile of the tree plan (two CTAs per SM)
 
     def cascade_us(self, info, hkv, hq, d, elt=2):
@@ -57,6 +62,56 @@ class PickerModel:
         kv = info.total_tokens * 2 * hkv * d * elt
         parts = info.n_parts * hq * (d + 1) * 4 * 2          # written, then read by the merge
         return (kv + parts) / (self.hbm_gbs * 1e3)
+
+
+def work_item_waves(model: PickerModel, n_work, n_work_wide, hkv):
+    """(wide waves, narrow waves) of a work-item plan, as ``cascade_us`` counts them."""
+    return (math.ceil(n_work_wide * hkv / (2 * model.num_sms)),
+            math.ceil((n_work - n_work_wide) / model.num_sms))
+
+
+def fit_work_item_model(samples, base: PickerModel | None = None) -> PickerModel:
+    """Least-squares fit of the work-item cost model to measured launches.
+
+    ``samples``: dicts with the measured time of one cascade run on the
+    work-item kernels (``us``) and its plan (``n_work``, ``n_work_wide``,
+    ``n_parts``, ``total_tokens``, ``hkv``, ``hq``, ``d``, ``elt``).  Each time
+    is fitted as ``3 * t_launch + wide_waves * t_wide_cta + narrow_waves *
+    t_narrow_cta + bytes / hbm`` with the effective bandwidth ``hbm`` fitted
+    too (as a multiple of ``base.hbm_gbs``).  A coefficient that comes out
+    negative is dropped (held at zero) and the rest refitted, so the model
+    never credits a CTA with negative time.  ``t_slot_cta_us`` (slot-list tree
+    tiles, only used when page-list tree plans are off) is carried over from
+    ``base``."""
+    base = base or PickerModel()
+    if len(samples) < 4:
+        raise ValueError("need at least 4 samples to fit 4 coefficients")
+    rows, rhs = [], []
+    for s in samples:
+        wide, narrow = work_item_waves(base, s["n_work"], s["n_work_wide"], s["hkv"])
+        info = _PlanCounts(s["n_parts"], s["total_tokens"])
+        rows.append([3.0, float(wide), float(narrow),
+                     base._bytes_us(info, s["hkv"], s["hq"], s["d"], s.get("elt", 2))])
+        rhs.append(s["us"])
+    A, y = np.asarray(rows), np.asarray(rhs)
+    keep = [0, 1, 2, 3]
+    coef = np.zeros(4)
+    while keep:
+        sol = np.linalg.lstsq(A[:, keep], y, rcond=None)[0]
+        if (sol >= 0).all():
+            coef[keep] = sol
+            break
+        keep = [k for k, c in zip(keep, sol) if c >= 0]
+    hbm = base.hbm_gbs / coef[3] if coef[3] > 0 else float("inf")
+    return PickerModel(num_sms=base.num_sms, hbm_gbs=float(hbm),
+                       t_launch_us=float(coef[0]), t_wide_cta_us=float(coef[1]),
+                       t_narrow_cta_us=float(coef[2]), t_slot_cta_us=base.t_slot_cta_us)
+
+
+@dataclass
+class _PlanCounts:
+    n_parts: int
+    total_tokens: int
 
 
 def cascade_counts_pages_twice(levels) -> bool:

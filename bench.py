@@ -659,6 +659,94 @@ def run_op_bench(args):
     }
 
 
+def run_op_picker(args):
+    """--op picker: fits the tree-vs-cascade picker's work-item cost model
+    (picker.fit_work_item_model) to cascade runs on the work-item kernels over
+    a sweep of cfg2-like states: one shared prefix of P tokens and W beams with
+    suffixes of U[1, S] tokens, Hq 32 / Hkv 8 / D 128, page size 16, bf16, page
+    ids a seeded permutation of the pool.  Each run is preceded by a 256 MB L2
+    flush; times are CUDA events (differential against the flush alone)."""
+    import numpy as np
+    import torch
+    from beam_engine_b200.cascade import MultiLevelCascadeAttentionWrapper
+    from beam_engine_b200.page_table import PageTable
+    from beam_engine_b200.picker import PickerModel, fit_work_item_model
+    dev = torch.device("cuda", 0)
+    Hq, Hkv, D, ps = 32, 8, 128, 16
+    P = min(args.pool_pages, 16384)
+    pt = PageTable(1, ps, P, Hkv, D, device=dev, store_dtype=torch.bfloat16)
+    pt.kv_cache.normal_(generator=torch.Generator(device=dev).manual_seed(1))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ws = torch.empty(128 << 20, dtype=torch.uint8, device=dev)
+    hbm, _, src = peaks()
+    t = lambda a: torch.tensor(np.asarray(a, np.int32))  # noqa: E731
+
+    def timeit(fn, iters):
+        for _ in range(3):
+            fn()
+
+        def run(with_op):
+            torch.cuda.synchronize()
+            torch.cuda._sleep(2_000_000)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(iters):
+                flush.zero_()
+                if with_op:
+                    fn()
+            e.record()
+            torch.cuda.synchronize()
+            return s.elapsed_time(e)
+        base = min(run(False) for _ in range(3))
+        return max(min(run(True) for _ in range(3)) - base, 0.0) / iters * 1e3
+
+    samples = []
+    g = torch.Generator().manual_seed(0)
+    for prefix in (256, 1024, 2048, 4096):
+        for W in (4, 16, 32, 64):
+            for smax in (16, 256):
+                perm = torch.randperm(P, generator=g).tolist()
+                suf = torch.randint(1, smax + 1, (W,), generator=g).tolist()
+                npre = prefix // ps
+                off, kvp, kvi, last = npre, [0], [], []
+                for L in suf:
+                    n = -(-L // ps)
+                    kvi += perm[off:off + n]
+                    off += n
+                    kvp.append(len(kvi))
+                    last.append(L - (n - 1) * ps)
+                lv = [([0, W], [0, npre], perm[:npre], [ps]), (list(range(W + 1)), kvp, kvi, last)]
+                w = MultiLevelCascadeAttentionWrapper(2, ws)
+                w.plan([t(x[0]) for x in lv], [t(x[1]) for x in lv], [t(x[2]) for x in lv],
+                       [t(x[3]) for x in lv], Hq, Hkv, D, ps, causal=True, sm_scale=D ** -0.5)
+                w._plan_items()                   # the work-item kernels the model describes
+                q = torch.randn((W, Hq, D), device=dev).to(torch.bfloat16)
+                out = torch.empty_like(q)
+                us = timeit(lambda: w.run(q, pt.kv_cache_at_layer[0], out=out), args.iters)
+                inf = w._plan.info
+                samples.append(dict(prefix=prefix, beams=W, suffix_max=smax, us=round(us, 2),
+                                    n_work=inf.n_work, n_work_wide=inf.n_work_wide,
+                                    n_parts=inf.n_parts, total_tokens=inf.total_tokens,
+                                    hkv=Hkv, hq=Hq, d=D, elt=2))
+    base = PickerModel(num_sms=torch.cuda.get_device_properties(dev).multi_processor_count,
+                       hbm_gbs=hbm)
+    fit = fit_work_item_model(samples, base)
+    err = [abs(fit.cascade_us(_Counts(s), Hkv, Hq, D) - s["us"]) / s["us"] for s in samples]
+    return {"op": "picker", "peak_gbs": hbm, "peak_source": src, "samples": samples,
+            "fit": {k: round(getattr(fit, k), 3) for k in
+                    ("num_sms", "hbm_gbs", "t_launch_us", "t_wide_cta_us", "t_narrow_cta_us")},
+            "rel_err_median": round(float(np.median(err)), 4),
+            "rel_err_max": round(float(np.max(err)), 4)}
+
+
+class _Counts:
+    """A work-item plan's counts from one picker sample (what cascade_us reads)."""
+
+    def __init__(self, s):
+        self.n_work, self.n_work_wide = s["n_work"], s["n_work_wide"]
+        self.n_parts, self.total_tokens = s["n_parts"], s["total_tokens"]
+
+
 def run_op_tiles(args):
     """Decode attention of one layer at a cfg3 decode state, on the beam-tile
     kernel: 8 prompts x 1024 tokens, 16 beams each, after `--op-steps` random
@@ -824,7 +912,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-comm", default="peer", choices=["nccl", "peer"],
                     help="tensor-parallel all-reduce: NCCL, or the fused peer-memory kernel")
-    ap.add_argument("--op", default=None, choices=["cfg2", "tiles3", "allreduce"],
+    ap.add_argument("--op", default=None, choices=["cfg2", "tiles3", "allreduce", "picker"],
                     help="op-level microbench instead of the decode benchmark")
     ap.add_argument("--pool-pages", type=int, default=65536)
     ap.add_argument("--op-steps", type=int, default=60,
@@ -864,7 +952,7 @@ def main():
         sys.stdout.flush()
         os._exit(0)
     if args.op:
-        fn = run_op_tiles if args.op == "tiles3" else run_op_bench
+        fn = {"tiles3": run_op_tiles, "picker": run_op_picker}.get(args.op, run_op_bench)
         print(json.dumps(fn(args)), flush=True)
         return
     if args.impl == "reference":

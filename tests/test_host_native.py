@@ -1,5 +1,6 @@
 """Native host page manager (C++ via the C ABI) against the reference fixtures.
 CPU only: allocation, trie forks, cascade / FastTree metadata, selection."""
+import math
 import re
 import os
 
@@ -594,3 +595,34 @@ def test_new_entry_points_reject_bad_arguments():
                                    None) == _lib.BE_EINVAL
     # exactness check: negative level count
     assert L.be_cascade_pages_twice(-1, None, None, None, None, 0) == -_lib.BE_EINVAL
+
+
+def test_picker_fit_recovers_a_known_model_and_drops_negative_terms():
+    """fit_work_item_model: samples made by a known work-item model are fitted
+    back to its per-launch and per-wave times and its bandwidth; a term the data contradicts
+    (negative) is held at zero instead of crediting CTAs with negative time."""
+    import random
+    from types import SimpleNamespace
+    from beam_engine_b200.picker import PickerModel, fit_work_item_model
+    true = PickerModel(t_launch_us=2.5, t_wide_cta_us=13.0, t_narrow_cta_us=7.5)
+    rnd = random.Random(0)
+    samples = []
+    for _ in range(16):
+        nw = rnd.randint(8, 900)
+        info = SimpleNamespace(n_work=nw, n_work_wide=rnd.randint(0, nw),
+                               n_parts=rnd.randint(0, 4000), total_tokens=rnd.randint(500, 40000))
+        samples.append(dict(us=true.cascade_us(info, 8, 32, 128), n_work=info.n_work,
+                            n_work_wide=info.n_work_wide, n_parts=info.n_parts,
+                            total_tokens=info.total_tokens, hkv=8, hq=32, d=128))
+    fit = fit_work_item_model(samples)
+    assert fit.t_launch_us == pytest.approx(2.5, abs=1e-6)
+    assert fit.t_wide_cta_us == pytest.approx(13.0, abs=1e-6)
+    assert fit.t_narrow_cta_us == pytest.approx(7.5, abs=1e-6)
+    assert fit.hbm_gbs == pytest.approx(true.hbm_gbs, rel=1e-6)
+    # times that fall as narrow waves grow: the narrow term is dropped, not negative
+    for s in samples:
+        s["us"] -= 5.0 * math.ceil((s["n_work"] - s["n_work_wide"]) / 148)
+    fit = fit_work_item_model(samples)
+    assert min(fit.t_launch_us, fit.t_wide_cta_us, fit.t_narrow_cta_us) >= 0.0
+    with pytest.raises(ValueError):
+        fit_work_item_model(samples[:3])
