@@ -185,6 +185,7 @@ def run_b200(args, rank, world, local_rank):
     plan_bytes = []
     plan_stats = []
     plan_kind = set()
+    plan_seq = []                      # kind of every timed step's plan, in order
     timing = {"on": False}
     gen.time_attention = True          # per-layer attention events recorded inside the step graph
 
@@ -200,6 +201,7 @@ def run_b200(args, rank, world, local_rank):
             else:
                 plan_stats.append((nq, inf.n_work, inf.n_work_wide, inf.n_parts, inf.n_merge))
             plan_kind.add("tiles" if tiles else "items")
+            plan_seq.append("tiles" if tiles else "items")
             # per layer: 2 add_rmsnorm, rope_append, silu_mul + attention (one beam-tile
             # launch, or tcgen05 wide + all-heads narrow + LSE merge); final norm; fused
             # log-softmax / top-k; the copy-on-write fork list at the head of the step
@@ -356,6 +358,22 @@ def run_b200(args, rank, world, local_rank):
         "kernel_picks": ({k: gen.picks.count(k) for k in set(gen.picks)} if gen.picks else None),
         "clocks": ev.get("clocks"),
     }
+    if len(plan_kind) > 1:
+        # mixed steps (kernel_type auto): the beam-tile and the work-item kernels separately
+        # (each graph step records one plan, then one attention event pair per layer)
+        by = {} if len(attn_ms) == len(plan_seq) * L else None
+        for kind in sorted(plan_kind) if by is not None else []:
+            idx = [i for i, k_ in enumerate(plan_seq) if k_ == kind]
+            ms = sum(sum(attn_ms[i * L:(i + 1) * L]) for i in idx)
+            b = sum(plan_bytes[i] * L for i in idx)
+            a = b / (ms / 1e3) / 1e9 if ms else 0.0
+            by[kind] = {"steps": len(idx), "avg_launch_us": round(ms / max(len(idx) * L, 1) * 1e3, 2),
+                        "achieved": round(a, 1), "frac": round(a / hbm, 4)}
+        res["roofline"]["by_kind"] = by
+        res["roofline"]["kernel"] = ("mixed: be_attn_tiles_run (beam-tile kernel) on exact cascade "
+                                     "steps, the work-item kernels on tree steps (see by_kind); "
+                                     "timed by event nodes inside the step graph")
+        res["roofline"]["plan_avg"] = None
     return res
 
 
