@@ -804,7 +804,7 @@ def run_op_tiles(args):
     n = len(bs.leaves)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     info, plan = tile_plan_host(levels, n, ps, Hq, Hkv, num_sms=sms, cluster=args.cluster,
-                                pieces=target_pieces(sms, Hkv))
+                                pieces=args.op_pieces or target_pieces(sms, Hkv))
     plan_d = torch.from_numpy(np.ascontiguousarray(plan)).to(dev)
     slots = max(1, info.n_part_pieces) * Hkv * info.tile_rows
     po = torch.empty(slots * D, dtype=torch.bfloat16, device=dev)
@@ -938,6 +938,8 @@ def main():
     ap.add_argument("--cluster", type=int, default=-1,
                     help="--op tiles3: cluster size (-1: the planner's choice, 0: merge kernel)")
     ap.add_argument("--op-layers", type=int, default=32)
+    ap.add_argument("--op-pieces", type=int, default=0,
+                    help="--op tiles3: pieces per KV head (0: the planner's target)")
     ap.add_argument("--op-tp", type=int, default=1, choices=[1, 2, 4, 8],
                     help="--op tiles3: heads of one rank under this tensor parallelism")
     ap.add_argument("--iters", type=int, default=20)

@@ -206,3 +206,44 @@ def test_decode_tiles_match_separate_calls():
         seg_ptr = ptr  # every candidate's children
         bs.update_native(bs.leaves, seg_ptr, rng.integers(0, 500, int(ptr[-1])).astype(np.int32),
                          -rng.random(int(ptr[-1])))
+
+
+def _decode_state(prompts, prompt_len, beams, steps, seed=0):
+    """Beam trie after `steps` selections in which half of every prompt's
+    beams fork in two and the other half end."""
+    rng = np.random.default_rng(seed)
+    bs = BeamState(beams, cpu_table(16, 65536))
+    for _ in range(prompts):
+        bs.add_root_sequence(rng.integers(0, 1000, prompt_len).tolist())
+    bs.update_native(bs.leaves, np.arange(prompts + 1, dtype=np.int32) * beams,
+                     rng.integers(0, 1000, prompts * beams).astype(np.int32),
+                     -rng.random(prompts * beams))
+    for _ in range(steps):
+        cnt = np.zeros(len(bs.leaves), np.int32)
+        for p in range(prompts):
+            c = np.zeros(beams, np.int32)
+            c[: beams // 2] = 2
+            rng.shuffle(c)
+            cnt[p * beams:(p + 1) * beams] = c
+        ptr = np.concatenate([[0], np.cumsum(cnt)]).astype(np.int32)
+        bs.update_native(bs.leaves, ptr, rng.integers(0, 1000, int(ptr[-1])).astype(np.int32),
+                         -rng.random(int(ptr[-1])))
+    return bs
+
+
+@pytest.mark.parametrize("prompts,prompt_len,beams,tp,cluster", [
+    (8, 1024, 16, 1, 4), (8, 1024, 16, 2, 8), (8, 1024, 16, 4, 8), (8, 1024, 16, 8, 16),
+    (1, 4096, 32, 1, 0), (1, 4096, 32, 8, 0)])
+def test_auto_cluster_choice(prompts, prompt_len, beams, tp, cluster):
+    """The planner's own cluster size: power-of-two clusters sized to the pieces
+    a tile gets, except that one long tile (a single prompt with a long prefix),
+    which a 16-CTA cluster would cap at 16 pieces, takes the merge kernel's form
+    and keeps all its pieces."""
+    from beam_engine_b200.cascade import target_pieces
+    bs = _decode_state(prompts, prompt_len, beams, 20)
+    hq, hkv = 32 // tp, 8 // tp
+    info, _ = tile_plan_host(bs.cascade_levels(), len(bs.leaves), 16, hq, hkv, num_sms=148,
+                             pieces=target_pieces(148, hkv))
+    assert info.cluster == cluster
+    if cluster == 0:
+        assert info.n_pieces > 16 * info.n_tiles
