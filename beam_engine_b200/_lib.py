@@ -137,6 +137,9 @@ _SIGS = {
     "be_diverse_select": (C.c_int, [C.c_int, vp, C.c_int, vp, vp,
                                     vp, vp, vp, C.c_int, C.c_int, C.c_double,
                                     C.c_int, C.c_double, vp, vp, vp, vp]),
+    "be_diverse_select_device": (C.c_int, [C.c_int, vp, C.c_int, vp, vp, vp, vp, C.c_int,
+                                           C.c_int, C.c_double, C.c_int, C.c_double, C.c_int,
+                                           vp, vp, vp, vp, vp]),
     "be_vanilla_select": (C.c_int, [C.c_int, C.c_int, vp, vp,
                                     vp, C.c_int, vp, vp,
                                     vp]),

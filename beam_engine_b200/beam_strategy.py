@@ -77,6 +77,36 @@ def diverse_select_segments(seg, parent_scores, tokens, logps, seq_ptr, seq_toke
     return ptr, ct[:m], cs[:m], ns
 
 
+def diverse_select_device(seg, parent_scores, tokens, logps, seq_ptr, beam_size, num_groups,
+                          diversity_penalty, length_penalty, stream=None):
+    """be_diverse_select_device (hamming penalty) on device tensors: ``seg``
+    int32 [nseg + 1], ``parent_scores`` float64 [ncand], ``tokens`` int32 /
+    ``logps`` float64 [ncand, k], ``seq_ptr`` int32 [ncand + 1] (the parents'
+    lengths).  Returns device tensors (child_ptr, child_tokens, child_scores,
+    new_seg) sized like ``diverse_select_segments``'s outputs; the children are
+    the first new_seg[-1] entries.  ``seg`` is also read on the host once, for
+    the launch's largest prompt."""
+    import torch
+    nseg = seg.numel() - 1
+    ncand, k = tokens.shape
+    segh = seg.cpu().numpy()
+    max_cands = int(np.max(np.diff(segh))) if nseg > 0 else 0
+    dev = tokens.device
+    cap = max(1, nseg * max(beam_size, num_groups))
+    ptr = torch.zeros(ncand + 1, dtype=torch.int32, device=dev)
+    ct = torch.zeros(cap, dtype=torch.int32, device=dev)
+    cs = torch.zeros(cap, dtype=torch.float64, device=dev)
+    ns = torch.zeros(nseg + 1, dtype=torch.int32, device=dev)
+    st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    check(lib().be_diverse_select_device(nseg, seg.data_ptr(), k, parent_scores.data_ptr(),
+                                         tokens.data_ptr(), logps.data_ptr(), seq_ptr.data_ptr(),
+                                         int(beam_size), int(num_groups), float(diversity_penalty),
+                                         0, float(length_penalty), max_cands, ptr.data_ptr(),
+                                         ct.data_ptr(), cs.data_ptr(), ns.data_ptr(),
+                                         C.c_void_p(st)), "diverse select (device)")
+    return ptr, ct, cs, ns
+
+
 def vanilla_select_arrays(parent_scores, tokens, logps, beam_size):
     """parent_scores [n] f64, tokens/logps [n, k] -> (child_ptr [n+1], child_tokens,
     child_scores)."""

@@ -362,3 +362,180 @@ extern "C" int be_vanilla_select_device(int nseg, const int32_t* seg_ptr, int k,
                            max_seg_cands * k, sel_parent, sel_token, sel_score));
   return BE_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Diverse beam search selection on the device, hamming penalty:
+// DiverseBeamSearchStrategy.select_candidates (src/beam_engine/beam_strategy.py:
+// 173-317, penalty :105-125), the same outputs as the host be_diverse_select.
+// One CTA per prompt.  The prompt's (candidate, j) choices are first ordered by
+// log-probability (stable, descending): ord[e] is that position.  Group g
+// scores every choice not yet taken as (logp - pen) / (len + 1) ** lpen, with
+// pen = diversity_penalty when an earlier group of this step took the same
+// token, and takes the bpg = max(1, beam_size / num_groups) best by (score
+// descending, ord ascending) -- the host's second stable sort -- each choice
+// counting the untaken choices ranked before it.  Picks are listed per parent
+// (parents ascending, picks in pick order) and the first beam_size kept, which
+// is what dropping children from the end, last parent first, leaves.
+// ---------------------------------------------------------------------------
+namespace be {
+
+constexpr int DIV_PICKS = 1024;        // picks per prompt (num_groups * bpg) held in shared memory
+
+__global__ void __launch_bounds__(SEL_THREADS) diverse_select_kernel(
+    const int32_t* __restrict__ seg_ptr, int k, const double* __restrict__ parent_scores,
+    const int32_t* __restrict__ tokens, const double* __restrict__ logps,
+    const int32_t* __restrict__ seq_ptr, int beam_size, int num_groups, double dpen, double lpen,
+    int cap_entries, int32_t* __restrict__ child_ptr, int32_t* __restrict__ child_tokens,
+    double* __restrict__ child_scores, int32_t* __restrict__ new_seg_ptr) {
+  extern __shared__ __align__(16) unsigned char div_smem[];
+  __shared__ int picks[DIV_PICKS];
+  __shared__ int pick_tok[DIV_PICKS];
+  pdl_wait();
+  const int s = blockIdx.x;
+  const int c0 = seg_ptr[s], c1 = seg_ptr[s + 1];
+  const int m = (c1 - c0) * k;
+  if (c1 < c0 || m > cap_entries) {
+    if (threadIdx.x == 0) flag_range_error();
+    return;
+  }
+  const int bpg = max(1, beam_size / num_groups);
+  const int npick_all = min(num_groups * bpg, m);   // sum over groups of min(bpg, untaken)
+  const int kept = min(beam_size, npick_all);
+  int off = 0;                                      // kept children of the earlier prompts
+  for (int t = 0; t < s; ++t)
+    off += min(beam_size, min(num_groups * bpg, (seg_ptr[t + 1] - seg_ptr[t]) * k));
+  double* score = reinterpret_cast<double*>(div_smem);
+  int* ord = reinterpret_cast<int*>(score + cap_entries);
+  unsigned char* taken = reinterpret_cast<unsigned char*>(ord + cap_entries);
+  const double* lp = logps + (int64_t)c0 * k;
+  const int32_t* tk = tokens + (int64_t)c0 * k;
+  for (int e = threadIdx.x; e < m; e += blockDim.x) {
+    const double le = lp[e];
+    int r = 0;
+    for (int f = 0; f < m; ++f) {
+      const double lf = lp[f];
+      r += (lf > le) || (lf == le && f < e);
+    }
+    ord[e] = r;
+    taken[e] = 0;
+  }
+  int npick = 0;
+  for (int g = 0; g < num_groups && npick < npick_all; ++g) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < m; e += blockDim.x) {
+      if (taken[e]) continue;
+      const int32_t tok = tk[e];
+      double pen = 0.0;
+      for (int q = 0; q < npick; ++q)
+        if (pick_tok[q] == tok) {
+          pen = dpen;
+          break;
+        }
+      double sc = lp[e] - pen;
+      if (lpen != 0.0) {
+        const int c = c0 + e / k;
+        const double len1 = (double)(seq_ptr[c + 1] - seq_ptr[c]) + 1.0;
+        sc = sc / (lpen == 1.0 ? len1 : pow(len1, lpen));
+      }
+      score[e] = sc;
+    }
+    __syncthreads();
+    const int take = min(bpg, m - npick);
+    for (int e = threadIdx.x; e < m; e += blockDim.x) {
+      if (taken[e]) continue;
+      const double se = score[e];
+      const int oe = ord[e];
+      int r = 0;
+      for (int f = 0; f < m && r < take; ++f) {
+        if (taken[f]) continue;
+        const double sf = score[f];
+        r += (sf > se) || (sf == se && ord[f] < oe);
+      }
+      if (r < take) picks[npick + r] = e;
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < take; r += blockDim.x) {
+      const int e = picks[npick + r];
+      taken[e] = 1;
+      pick_tok[npick + r] = tk[e];
+    }
+    npick += take;
+  }
+  __syncthreads();
+  // parent-major order of the picks; the first `kept` are the children
+  for (int r = threadIdx.x; r < npick; r += blockDim.x) {
+    const int e = picks[r];
+    const int pe = e / k;
+    int pos = 0;
+    for (int q = 0; q < npick; ++q) {
+      const int pq = picks[q] / k;
+      pos += (pq < pe) || (pq == pe && q < r);
+    }
+    if (pos < kept) {
+      child_tokens[off + pos] = tk[e];
+      child_scores[off + pos] = parent_scores[c0 + pe] + lp[e];
+    }
+  }
+  for (int i = threadIdx.x; i < c1 - c0; i += blockDim.x) {
+    int cnt = 0;
+    for (int q = 0; q < npick; ++q) cnt += picks[q] / k <= i;
+    child_ptr[c0 + i + 1] = off + min(kept, cnt);
+  }
+  if (threadIdx.x == 0) {
+    new_seg_ptr[s + 1] = off + kept;
+    if (s == 0) {
+      child_ptr[0] = 0;
+      new_seg_ptr[0] = 0;
+    }
+  }
+}
+
+}  // namespace be
+
+extern "C" int be_diverse_select_device(int nseg, const int32_t* seg_ptr, int k,
+                                        const double* parent_scores, const int32_t* tokens,
+                                        const double* logps, const int32_t* seq_ptr,
+                                        int beam_size, int num_groups, double diversity_penalty,
+                                        int diversity_type, double length_penalty,
+                                        int max_seg_cands, int32_t* child_ptr,
+                                        int32_t* child_tokens, double* child_scores,
+                                        int32_t* new_seg_ptr, void* stream) {
+  using namespace be;
+  if (nseg < 0 || k < 1 || beam_size < 1 || num_groups < 1 || max_seg_cands < 0 || !seg_ptr ||
+      !parent_scores || !tokens || !logps || !seq_ptr || !child_ptr || !child_tokens ||
+      !child_scores || !new_seg_ptr) {
+    set_error("be_diverse_select_device: invalid arguments");
+    return BE_EINVAL;
+  }
+  if (diversity_type != 0) {
+    set_error("be_diverse_select_device: only the hamming penalty runs on the device "
+              "(be_diverse_select serves the cumulative one)");
+    return BE_ENOTSUP;
+  }
+  if ((int64_t)max_seg_cands * k > SEL_MAX) {
+    set_error("be_diverse_select_device: %d candidates x top-%d exceed %d entries per prompt",
+              max_seg_cands, k, SEL_MAX);
+    return BE_EINVAL;
+  }
+  const int bpg = std::max(1, beam_size / num_groups);
+  if ((int64_t)num_groups * bpg > DIV_PICKS) {
+    set_error("be_diverse_select_device: %d groups x %d picks exceed %d per prompt", num_groups,
+              bpg, DIV_PICKS);
+    return BE_EINVAL;
+  }
+  if (nseg == 0) return BE_OK;
+  const int cap = std::max(1, max_seg_cands * k);
+  const size_t smem = (size_t)cap * (sizeof(double) + sizeof(int) + 1);
+  static bool set = false;
+  if (!set) {
+    BE_CUDA_CHECK(cudaFuncSetAttribute(diverse_select_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)(SEL_MAX * (sizeof(double) + sizeof(int) + 1))));
+    set = true;
+  }
+  BE_CUDA_CHECK(launch_pdl(diverse_select_kernel, nseg, SEL_THREADS, smem, (cudaStream_t)stream,
+                           seg_ptr, k, parent_scores, tokens, logps, seq_ptr, beam_size,
+                           num_groups, diversity_penalty, length_penalty, cap, child_ptr,
+                           child_tokens, child_scores, new_seg_ptr));
+  return BE_OK;
+}

@@ -536,6 +536,21 @@ int be_diverse_select(int nseg, const int32_t* seg_ptr, int k, const double* par
                       double diversity_penalty, int diversity_type, double length_penalty,
                       int32_t* child_ptr, int32_t* child_tokens, double* child_scores,
                       int32_t* new_seg_ptr);
+/* be_diverse_select on the device for the hamming penalty (diversity_type 0;
+ * DiverseBeamSearchStrategy.select_candidates, src/beam_engine/beam_strategy.py:
+ * 173-317 with :105-125): the same arguments and outputs, all pointers device
+ * memory, one CTA per prompt.  seq_ptr [ncand + 1] only gives the parents'
+ * lengths for the length penalty (no token sequences are read).  Limits:
+ * max_seg_cands (the largest prompt's candidate count) * k <= 8192 and
+ * num_groups * max(1, beam_size / num_groups) <= 1024; diversity_type 1
+ * returns BE_ENOTSUP.  A length_penalty other than 0 or 1 goes through the
+ * device pow(), whose last bit may differ from the host's.                   */
+int be_diverse_select_device(int nseg, const int32_t* seg_ptr, int k, const double* parent_scores,
+                             const int32_t* tokens, const double* logps, const int32_t* seq_ptr,
+                             int beam_size, int num_groups, double diversity_penalty,
+                             int diversity_type, double length_penalty, int max_seg_cands,
+                             int32_t* child_ptr, int32_t* child_tokens, double* child_scores,
+                             int32_t* new_seg_ptr, void* stream);
 
 /* ---- Tensor-parallel all-reduce over peer memory (one process per GPU) ----
  * Replaces the NCCL all-reduce after the row-parallel projections
