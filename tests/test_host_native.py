@@ -626,3 +626,23 @@ def test_picker_fit_recovers_a_known_model_and_drops_negative_terms():
     assert min(fit.t_launch_us, fit.t_wide_cta_us, fit.t_narrow_cta_us) >= 0.0
     with pytest.raises(ValueError):
         fit_work_item_model(samples[:3])
+
+
+def test_diverse_select_device_argument_checks():
+    """be_diverse_select_device refuses bad calls before any CUDA call (no GPU
+    needed): null pointers, the cumulative penalty (host only), more entries
+    per prompt than shared memory holds, more picks than the pick list holds."""
+    L = _lib.lib()
+    a = np.zeros(64, np.int64)
+    p = a.ctypes.data
+
+    def call(nseg=1, k=2, beam=4, groups=2, dtype=0, max_c=4, ptr=p):
+        return L.be_diverse_select_device(nseg, ptr, k, p, p, p, p, beam, groups, 0.5, dtype, 1.0,
+                                          max_c, p, p, p, p, None)
+    assert call(ptr=None) == _lib.BE_EINVAL
+    assert call(nseg=-1) == _lib.BE_EINVAL
+    assert call(dtype=1) == _lib.BE_ENOTSUP
+    assert b"hamming" in L.be_last_error()
+    assert call(k=64, max_c=129) == _lib.BE_EINVAL
+    assert call(beam=2048, groups=2048) == _lib.BE_EINVAL
+    assert call(nseg=0) == _lib.BE_OK
