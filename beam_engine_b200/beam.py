@@ -161,9 +161,16 @@ def step_sel_offsets(n):
     return seg_off, scores_off
 
 
+def step_lens_offset(n):
+    """Offset (int32 units) of the parents' sequence offsets [n + 1] (their
+    lengths, for the device diverse selection's length penalty), after the
+    scores."""
+    return step_sel_offsets(n)[1] + 2 * n
+
+
 def step_plan_offset(n):
     """Offset (int32 units) of the attention plan in a step buffer of n beams."""
-    return -(-(step_sel_offsets(n)[1] + 2 * n) // 32) * 32
+    return -(-(step_lens_offset(n) + n + 1) // 32) * 32
 
 
 def _pool_dtype(pt):
@@ -179,6 +186,19 @@ class DeviceSelection:
 
     def __init__(self, parent, token, score):
         self.parent, self.token, self.score = parent, token, score
+
+
+class DiverseSelection:
+    """A step's diverse selection (hamming) made on the device
+    (be_diverse_select_device): children per parent as be_diverse_select
+    returns them -- child_ptr [candidates + 1], tokens and scores, and the new
+    prompt ranges."""
+    __slots__ = ("child_ptr", "tokens", "scores", "new_seg")
+
+    def __init__(self, child_ptr, tokens, scores, new_seg):
+        m = int(new_seg[-1])
+        self.child_ptr, self.tokens, self.scores, self.new_seg = (child_ptr, tokens[:m],
+                                                                  scores[:m], new_seg)
 
 
 class StepGraph:
@@ -222,9 +242,22 @@ class StepGraph:
         self.vals_h = torch.empty(n * k, dtype=torch.float32).pin_memory()
         self.idx_h = torch.empty(n * k, dtype=torch.int64).pin_memory()
         # global top-W on the device (vanilla strategy): nseg prompts of beam width W
-        self.select = caps.get("select")          # None or (nseg, W, max candidates per prompt)
-        if self.select is not None:
-            nseg, W, _ = self.select
+        # None or (nseg, W, max candidates per prompt, diverse): diverse is None for the
+        # vanilla selection, else (num_groups, diversity_penalty, length_penalty)
+        self.select = caps.get("select")
+        if self.select is not None and self.select[3] is not None:
+            nseg, W, _, (groups, _, _) = self.select
+            self.seg_off, self.scores_off = step_sel_offsets(n)
+            self.lens_off = step_lens_offset(n)
+            cap = max(1, nseg * max(W, groups))
+            self.sel_d = (torch.empty(n + 1, dtype=torch.int32, device=dev),
+                          torch.empty(cap, dtype=torch.int32, device=dev),
+                          torch.empty(cap, dtype=torch.float64, device=dev),
+                          torch.empty(nseg + 1, dtype=torch.int32, device=dev))
+            self.sel_h = tuple(torch.empty(x.numel(), dtype=x.dtype).pin_memory()
+                               for x in self.sel_d)
+        elif self.select is not None:
+            nseg, W, _, _ = self.select
             self.seg_off, self.scores_off = step_sel_offsets(n)
             self.sel_d = (torch.empty(nseg * W, dtype=torch.int32, device=dev),
                           torch.empty(nseg * W, dtype=torch.int32, device=dev),
@@ -328,9 +361,23 @@ class StepGraph:
         logits = self.gen.model.forward(d[0:n], d[n:2 * n], self.gen.page_table, d[2 * n:3 * n],
                                         d[3 * n:4 * n], self)
         v, i = self.gen._logprob_topk(logits, self.k, self.temp)
+        if self.select is not None and self.select[3] is not None:
+            # diverse selection (hamming) on the device; only the children leave it
+            nseg, W, maxc, (groups, dpen, lpen) = self.select
+            v64 = v.to(torch.float64).contiguous()
+            i32 = i.to(torch.int32).contiguous()
+            cp, ct, cs, ns = self.sel_d
+            check(lib().be_diverse_select_device(
+                nseg, d.data_ptr() + 4 * self.seg_off, self.k, d.data_ptr() + 4 * self.scores_off,
+                i32.data_ptr(), v64.data_ptr(), d.data_ptr() + 4 * self.lens_off, W, groups,
+                dpen, 0, lpen, maxc, cp.data_ptr(), ct.data_ptr(), cs.data_ptr(), ns.data_ptr(),
+                stream_ptr(self.gen.device)), "device diverse selection")
+            for h, x in zip(self.sel_h, self.sel_d):
+                h.copy_(x, non_blocking=True)
+            return
         if self.select is not None:
             # selection on the device; only beam_size (parent, token, score) per prompt leave it
-            nseg, W, maxc = self.select
+            nseg, W, maxc, _ = self.select
             v, i = v.contiguous(), i.contiguous()
             sp, st, ss = self.sel_d
             check(lib().be_vanilla_select_device(
@@ -372,16 +419,21 @@ class StepGraph:
         k = self.k
         if self.select is not None:
             self.gen.d2h_bytes += sum(h.numel() * h.element_size() for h in self.sel_h)
+            if self.select[3] is not None:
+                return DiverseSelection(*(h.numpy().copy() for h in self.sel_h))
             return DeviceSelection(*(h.numpy().copy() for h in self.sel_h))
         self.gen.d2h_bytes += n * k * (4 + 8)
         return (self.vals_h.numpy()[:n * k].reshape(n, k).astype(np.float64),
                 self.idx_h.numpy()[:n * k].reshape(n, k).astype(np.int32))
 
-    def set_selection_inputs(self, seg, scores):
-        """Prompt ranges and parent scores of this step for the device selection."""
+    def set_selection_inputs(self, seg, scores, seq_ptr=None):
+        """Prompt ranges and parent scores of this step for the device selection
+        (and, for the diverse selection, the parents' sequence offsets)."""
         h = self.host_buf.numpy()
         h[self.seg_off:self.seg_off + len(seg)] = seg
         h[self.scores_off:self.scores_off + 2 * len(scores)].view(np.float64)[:] = scores
+        if seq_ptr is not None:
+            h[self.lens_off:self.lens_off + len(seq_ptr)] = seq_ptr
 
 
 class BeamSearchGenerator:
@@ -730,10 +782,12 @@ class BeamSearchGenerator:
 
         want_sel = None
         if self._sel_ctx is not None:
-            seg, W = self._sel_ctx
-            want_sel = (len(seg) - 1, W)
+            seg, W, div = self._sel_ctx
+            want_sel = (len(seg) - 1, W, div)
+        have_sel = (None if sg is None or sg.select is None else
+                    (sg.select[0], sg.select[1], sg.select[3]))
         same = (sg is not None and sg.n == n and sg.k == k and sg.temp == temperature
-                and (sg.select[:2] if sg.select is not None else None) == want_sel
+                and have_sel == want_sel
                 and (want_sel is None or int(np.max(np.diff(self._sel_ctx[0]))) <= sg.select[2]))
 
         def fill(buf_ptr, cap, plan_off, cluster):
@@ -769,8 +823,8 @@ class BeamSearchGenerator:
             cl = info.cluster
             sel = None
             if self._sel_ctx is not None:
-                seg, W = self._sel_ctx
-                sel = (len(seg) - 1, W, int(np.max(np.diff(seg))))
+                seg, W, div = self._sel_ctx
+                sel = (len(seg) - 1, W, int(np.max(np.diff(seg))), div)
             if cl > 1:   # one cluster per (tile, KV head): pieces = tiles x cluster
                 caps = dict(pieces=info.n_pieces, tiles=info.n_tiles, part_pieces=0,
                             ints=3 * info.total_ints + 64 * n + 4096, rows=info.tile_rows,
@@ -802,8 +856,9 @@ class BeamSearchGenerator:
             self.plan_hook(n, info)
         self._take_fork(sg)
         if sg.select is not None:
-            seg, W = self._sel_ctx
-            sg.set_selection_inputs(seg, state.scores)
+            seg, W, div = self._sel_ctx
+            sg.set_selection_inputs(seg, state.scores,
+                                    state.leaf_sequences()[0] if div is not None else None)
         return sg.step_filled(sg.plan_off + info.total_ints)
 
     def generate_ids(self, prompts: List[List[int]], beam_size: int = 4,
@@ -845,13 +900,19 @@ class BeamSearchGenerator:
                     on_step(step)
                 k = min(2 * W, V) if W != 1 else 1
                 vanilla = type(self.strategy) is VanillaBeamSearchStrategy
-                self._sel_ctx = ((np.asarray(seg, np.int32), W)
-                                 if vanilla and getattr(self, "device_select", False) and k <= 64
+                div = self._device_diverse_params(W)
+                self._sel_ctx = ((np.asarray(seg, np.int32), W, div)
+                                 if (vanilla or div is not None)
+                                 and getattr(self, "device_select", False) and k <= 64
                                  and int(np.max(np.diff(seg))) * k <= 8192 else None)
                 with _Range("decode_step"):
                     res = self.decode_topk(state, k, temperature)
                 self._sel_ctx = None
                 with _Range("select"):
+                    if isinstance(res, DiverseSelection):
+                        self._apply(state, res.child_ptr, res.tokens, res.scores)
+                        seg = np.asarray(res.new_seg)
+                        continue
                     if isinstance(res, DeviceSelection):
                         new_seg = state.vanilla_step_selected(seg, res.parent, res.token,
                                                               res.score, W)
@@ -903,6 +964,19 @@ class BeamSearchGenerator:
             out.append(self.strategy.get_final_sequences(sub, num_return_sequences))
         self.last_state = state
         return out
+
+    def _device_diverse_params(self, W):
+        """(num_groups, diversity_penalty, length_penalty) when this step's
+        diverse selection can run on the device (hamming penalty, within
+        be_diverse_select_device's pick limit), else None."""
+        from .beam_strategy import _DIVERSITY_TYPES, DiverseBeamSearchStrategy
+        st = self.strategy
+        if type(st) is not DiverseBeamSearchStrategy or _DIVERSITY_TYPES.get(st.diversity_type, 1):
+            return None
+        groups = int(st.num_groups)
+        if groups < 1 or groups * max(1, W // groups) > 1024:
+            return None
+        return (groups, float(st.diversity_penalty), float(st.length_penalty))
 
     def _apply(self, state, child_ptr, child_tokens, child_scores):
         state.update_native(state.leaves, child_ptr, child_tokens, child_scores)

@@ -99,3 +99,31 @@ def test_cumulative_is_refused():
                                              z32.data_ptr(), z32.data_ptr(), z64.data_ptr(),
                                              z32.data_ptr(), None)
     assert rc == _lib.BE_ENOTSUP
+
+
+@pytest.mark.parametrize("groups,lpen", [(2, 1.0), (4, 0.0)])
+def test_engine_with_device_diverse_selection_matches_host(monkeypatch, groups, lpen):
+    """Three prompts, bf16 graph steps, diverse (hamming) strategy: the beams and
+    scores of a search whose selection runs inside the step graph on the GPU
+    equal the host-selection search's."""
+    from beam_engine_b200.beam import BeamSearchGenerator
+    from beam_engine_b200.beam_strategy import DiverseBeamSearchStrategy
+    from beam_engine_b200.configs import TINY
+    from beam_engine_b200.llama import BeamLlama
+    cfg = dict(TINY, head_dim=128, num_attention_heads=4, num_key_value_heads=2, hidden_size=512)
+    model = BeamLlama(cfg, None, dtype=torch.bfloat16, device=torch.device("cuda", 0), seed=3)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, 1024, (70,), generator=g).tolist() for _ in range(3)]
+    outs = []
+    for on in ("0", "1"):
+        monkeypatch.setenv("BE_DEVICE_SELECT", on)
+        strat = DiverseBeamSearchStrategy(num_groups=groups, diversity_penalty=0.75,
+                                          diversity_type="hamming", length_penalty=lpen)
+        gen = BeamSearchGenerator(model, None, strat, page_size=16, max_num_pages=512)
+        outs.append(gen.generate_ids(prompts, 8, max_new_tokens=24, num_return_sequences=8))
+        sg = gen.step_graph_tiles
+        assert sg is not None
+        assert (sg.select is not None and sg.select[3] is not None) == (on == "1")
+    for a, b in zip(*outs):
+        assert [s for s, _ in a] == [s for s, _ in b]
+        assert [x for _, x in a] == [x for _, x in b]
